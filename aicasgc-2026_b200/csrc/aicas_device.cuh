@@ -1,0 +1,212 @@
+// Device-side primitives for sm_100a: mbarriers, bulk async copies
+// (global -> shared, completed on an mbarrier), bounded waits and a bounded
+// software grid barrier.  Every wait here gives up after a time limit or when
+// another CTA raised the scratch `abort` word, so a fault never hangs the GPU.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "aicas_phase_program.h"
+
+namespace aicas {
+
+// Error codes written to AicasScratch::error (also returned by the C ABI).
+enum : int {
+  kErrNone = 0,
+  kErrBarrierTimeout = 10,   // grid barrier did not complete in time
+  kErrFullTimeout = 11,      // a stage's bulk copy did not land in time
+  kErrEmptyTimeout = 12,     // consumers did not release a stage in time
+  kErrDrainTimeout = 13,     // in-flight copies did not land before exit
+  kErrBadPhase = 14,         // unknown phase kind / bad descriptor
+  kErrBadInput = 15,         // token id or cache position out of range
+};
+
+// Wait limit: two seconds of %globaltimer.  Far above any legal phase time
+// (a full 28-layer step is ~0.5 ms) and far below a watchdog.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy (bulk copy) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Bulk async copy global -> this CTA's shared memory; completes `bytes` of
+// transaction count on `bar`.  dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ int ld_volatile_int(const int32_t* p) {
+  return *reinterpret_cast<const volatile int32_t*>(p);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Record the first error and tell every other wait to give up.
+__device__ __forceinline__ void raise_error(AicasScratch* s, int code) {
+  atomicCAS(&s->error, 0, code);
+  atomicExch(&s->abort, 1);
+}
+
+// Bounded wait for phase `parity` of `bar`; false on timeout or abort.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, AicasScratch* s, int err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (ld_volatile_int(&s->abort)) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, err);
+        return false;
+      }
+    }
+  }
+}
+
+// Software grid barrier over `nct` co-resident CTAs, called by ONE thread per
+// CTA.  Sense by generation counter; the last arriver resets the count and
+// publishes the next generation.  Bounded: gives up after kWaitLimitNs.
+__device__ __forceinline__ bool grid_barrier(AicasScratch* s, uint32_t nct, uint32_t& gen) {
+  __threadfence();
+  const uint32_t g = gen;
+  const uint32_t prev = atomicAdd(&s->bar_count, 1u);
+  if (prev == nct - 1) {
+    atomicExch(&s->bar_count, 0u);
+    __threadfence();
+    st_release_u32(&s->bar_gen, g + 1);
+  } else {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while (ld_acquire_u32(&s->bar_gen) == g) {
+      if ((++it & 15u) == 0) {
+        if (ld_volatile_int(&s->abort)) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_error(s, kErrBarrierTimeout);
+          return false;
+        }
+      }
+      __nanosleep(20);
+    }
+  }
+  gen = g + 1;
+  __threadfence();
+  return true;
+}
+
+// fp16 helpers -------------------------------------------------------------
+__device__ __forceinline__ float r16(float x) { return __half2float(__float2half_rn(x)); }
+
+// acc += w * x for the two fp16 lanes of each 32-bit word (exact fp16
+// products, fp32 accumulation: PTX mixed-precision fma, sm_100+).
+__device__ __forceinline__ float fma2_f16_f32(uint32_t w, uint32_t x, float acc) {
+  asm("{\n .reg .f16 wl, wh, xl, xh;\n"
+      " mov.b32 {wl, wh}, %1;\n"
+      " mov.b32 {xl, xh}, %2;\n"
+      " fma.rn.f32.f16 %0, wl, xl, %0;\n"
+      " fma.rn.f32.f16 %0, wh, xh, %0;\n}\n"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+  return acc;
+}
+
+__device__ __forceinline__ float dot8_f16(const uint4 w, const uint4 x, float acc) {
+  acc = fma2_f16_f32(w.x, x.x, acc);
+  acc = fma2_f16_f32(w.y, x.y, acc);
+  acc = fma2_f16_f32(w.z, x.z, acc);
+  acc = fma2_f16_f32(w.w, x.w, acc);
+  return acc;
+}
+
+__device__ __forceinline__ uint4 ldcg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+__device__ __forceinline__ float ldcg_half(const __half* p) {
+  unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(p));
+  return __half2float(__ushort_as_half(u));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Named barrier over the consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+}  // namespace aicas

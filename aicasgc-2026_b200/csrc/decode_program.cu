@@ -1,0 +1,1098 @@
+// Persistent decode-program kernel for B200 (sm_100a).
+//
+// One launch runs a list of phases (phase_program.h) with one CTA per SM:
+//   warp 0      producer: streams every tile this CTA will consume, phase after
+//               phase, from HBM into a 12-stage shared-memory ring with bulk
+//               async copies (cp.async.bulk + mbarrier complete_tx).  It never
+//               waits on a grid barrier, so HBM keeps streaming the next
+//               phase's weights while the consumers wait for activations.
+//   warps 1..8  consumers: per phase, wait on the grid barrier, build the input
+//               vector (RMSNorm prologue with HF's fp16 rounding points), then
+//               reduce each tile against it with exact fp16 products and fp32
+//               accumulation; per-group epilogues apply rounding, residuals,
+//               SiLU*up, or the running argmax.
+//
+// GEMV tile: 4 weight rows x 2048 columns (16 KB).  Consumer warp w owns
+// columns [256w, 256w+256) of every row, lane l the 8 columns at 256w + 8l, so
+// each lane keeps its slice of the input vector in registers for the whole
+// phase and every weight byte is read from shared memory exactly once.
+//
+// Attention tile: K and V rows of 32 cache positions of one KV head (16 KB).
+// Work units (KV head, 32-position chunk) are split into contiguous ranges per
+// CTA; each CTA's segment of a head yields one (max, sum, acc) partial, and the
+// last CTA to finish a head (atomic arrival count) merges its partials in a
+// fixed order, so the result does not depend on arrival order.
+//
+// Reference behaviour this replaces (file:line in the reference checkout):
+//   fused RMSNorm+QKV      cuda_extensions/decode_gemv_kernel_fused.cuh:99-185
+//   o_proj GEMV            cuda_extensions/decode_gemv_kernel_matvec.cuh:276-343
+//   post-attn MLP          cuda_extensions/decode_gemv_kernel_fused.cuh:850-1076
+//   split-KV attention     cuda_extensions/decode_attention_v4_kernel.cu:647-900
+//   lm_head GEMV           cuda_extensions/decode_gemv_kernel_matvec.cuh:209-274
+//   argmax                 evaluation_wrapper.py:952 (torch.argmax, first max wins)
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+#include <stddef.h>
+
+#include "aicas_device.cuh"
+#include "aicas_phase_program.h"
+
+namespace aicas {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kRows = 4;            // weight rows per GEMV tile
+constexpr int kChunk = 2048;        // columns per GEMV tile
+constexpr int kRowBytes = kChunk * 2;
+constexpr int kStageBytes = kRows * kRowBytes;  // 16 KB
+constexpr int kStages = 12;
+constexpr int kAttnChunk = 32;      // cache positions per attention tile
+constexpr int kHD = AICAS_HEAD_DIM;
+constexpr int kMaxChunks = AICAS_MAX_K / kChunk;
+
+static_assert(kAttnChunk * kHD * 2 * 2 == kStageBytes, "attention tile must fill one stage");
+
+struct AttnSmem {
+  float q[2][kHD];        // rotated queries of the head pair
+  float cs[kHD], sn[kHD]; // cos/sin (fp16 values)
+  float kf[kHD], vf[kHD]; // fresh k (normed+rotated) / v of the current position
+  float tmp[2][kHD];
+  float wm[kConsumerWarps][2];
+  float wl[kConsumerWarps][2];
+  float wacc[kConsumerWarps][2][kHD];
+  float red[kConsumerWarps];
+  int last;
+};
+
+struct __align__(128) Smem {
+  uint8_t ring[kStages][kStageBytes];
+  union {
+    __half xbuf[AICAS_MAX_K];
+    AttnSmem at;
+  } u;
+  float red[2][kConsumerWarps][8];
+  float nred[kConsumerWarps];
+  float best_v[kRows];
+  int best_i[kRows];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+};
+
+struct ProgramArgs {
+  const AicasPhase* phases;  // device array, or null: use `inl`
+  int n_phases;
+  int pad;
+  AicasStepState* state;     // may be null (op-level calls)
+  AicasScratch* scratch;
+  AicasPhase inl[4];
+};
+
+struct StepIn {
+  int64_t token;
+  int64_t pos;
+  int64_t rope[3];
+  int64_t step;
+};
+
+struct Range {
+  int start, count;
+};
+
+// Contiguous split of `total` items over `nct` CTAs, CTA order rotated by `rot`.
+__device__ __forceinline__ Range split_range(int total, int nct, int cta, int rot) {
+  int c = (cta - rot) % nct;
+  if (c < 0) c += nct;
+  const int base = total / nct, extra = total % nct;
+  return {c * base + min(c, extra), base + (c < extra ? 1 : 0)};
+}
+
+// Inverse of split_range (rot 0): the CTA owning item u.
+__device__ __forceinline__ int owner_of(int u, int total, int nct) {
+  const int base = total / nct, extra = total % nct;
+  const int big = extra * (base + 1);
+  if (u < big) return u / (base + 1);
+  return extra + (u - big) / base;
+}
+
+// Attention covers cache slots [0, valid); 0 when the position is outside
+// the cache (the phase is then skipped by producer and consumers alike and
+// kErrBadInput is raised).
+__device__ __forceinline__ int phase_valid_len(const AicasPhase& d, const StepIn& in) {
+  const int64_t pos = d.pos_ptr ? *reinterpret_cast<const int64_t*>(d.pos_ptr) : in.pos;
+  if (pos < 0 || pos >= d.max_len) return 0;
+  return (int)pos + 1;
+}
+
+__device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
+  const int C = (d.k + kChunk - 1) / kChunk;
+  return d.kind == AICAS_PH_GATEUP ? 2 * C : C;
+}
+
+// ---------------------------------------------------------------------------
+// Producer (warp 0, lane 0)
+// ---------------------------------------------------------------------------
+struct Ring {
+  uint32_t it = 0;  // tiles issued/consumed so far in this launch
+  __device__ __forceinline__ int stage() const { return it % kStages; }
+  __device__ __forceinline__ uint32_t round() const { return it / kStages; }
+};
+
+__device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+  AicasScratch* s = a.scratch;
+  const int nct = gridDim.x, cta = blockIdx.x;
+  const uint64_t pol = l2_evict_first_policy();
+  Ring r;
+  bool ok = true;
+  const AicasPhase* P = a.phases ? a.phases : a.inl;
+  auto acquire = [&](int st) -> bool {
+    if (r.round() == 0) return true;
+    return mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+  };
+  for (int ph = 0; ph < a.n_phases && ok; ++ph) {
+    const AicasPhase& d = P[ph];
+    if (d.kind == AICAS_PH_ATTN) {
+      const int valid = phase_valid_len(d, in);
+      const int cph = (valid + kAttnChunk - 1) / kAttnChunk;
+      const Range rg = split_range(d.kv_heads * cph, nct, cta, 0);  // empty when valid == 0
+      const __half* kc = reinterpret_cast<const __half*>(d.k_cache);
+      const __half* vc = reinterpret_cast<const __half*>(d.v_cache);
+      for (int u = rg.start; u < rg.start + rg.count; ++u) {
+        const int st = r.stage();
+        if (!(ok = acquire(st))) break;
+        const int h = u / cph, p0 = (u % cph) * kAttnChunk;
+        const int rows = min(kAttnChunk, valid - p0);
+        const uint32_t bytes = rows * kHD * 2;
+        mbar_arrive_expect_tx(&sm.full[st], 2 * bytes);
+        const size_t off = ((size_t)h * d.max_len + p0) * kHD;
+        bulk_g2s_nohint(sm.ring[st], kc + off, bytes, &sm.full[st]);
+        bulk_g2s_nohint(sm.ring[st] + kStageBytes / 2, vc + off, bytes, &sm.full[st]);
+        ++r.it;
+      }
+    } else if (d.kind == AICAS_PH_GEMV || d.kind == AICAS_PH_GATEUP || d.kind == AICAS_PH_LMHEAD) {
+      const int G = (d.n + kRows - 1) / kRows;
+      const int C = (d.k + kChunk - 1) / kChunk;
+      const int T = tiles_per_group(d);
+      const Range rg = split_range(G, nct, cta, d.rot);
+      const __half* W = reinterpret_cast<const __half*>(d.w);
+      for (int g = rg.start; g < rg.start + rg.count && ok; ++g) {
+        const int nrows = min(kRows, d.n - g * kRows);
+        for (int t = 0; t < T; ++t) {
+          const int st = r.stage();
+          if (!(ok = acquire(st))) break;
+          const int c = t % C;
+          const int row0 = g * kRows + (t >= C ? d.n : 0);
+          const int col0 = c * kChunk;
+          const uint32_t bytes = min(kChunk, d.k - col0) * 2;
+          mbar_arrive_expect_tx(&sm.full[st], nrows * bytes);
+          for (int i = 0; i < nrows; ++i)
+            bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
+          ++r.it;
+        }
+      }
+    }
+  }
+  // Drain: every issued copy must land before this CTA may exit.  In the
+  // normal path the consumers already waited for all of them.
+  const uint32_t issued = r.it;
+  const uint32_t first = issued > (uint32_t)kStages ? issued - kStages : 0;
+  for (uint32_t it = first; it < issued; ++it) {
+    const int st = it % kStages;
+    if (!mbar_wait_bounded(&sm.full[st], (it / kStages) & 1u, s, kErrDrainTimeout)) {
+      // abort raised by someone else: still give the copy its own bounded time
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.full[st], (it / kStages) & 1u)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumers (warps 1..8)
+// ---------------------------------------------------------------------------
+struct Consumer {
+  const ProgramArgs& a;
+  Smem& sm;
+  const StepIn& in;
+  AicasScratch* s;
+  int tid;   // 0..255
+  int w;     // consumer warp 0..7
+  int lane;
+  int nct, cta;
+  Ring r;
+  uint32_t gen;
+  bool ok = true;
+
+  // Waits never end the consumer loop early: after a failed (timed-out or
+  // aborted) wait the CTA keeps walking the same program without waiting, so
+  // every named barrier is still reached by all 256 consumer threads and the
+  // launch ends promptly with the error recorded in the scratch block.
+  __device__ void wait_full(int st) {
+    if (!mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout)) ok = false;
+  }
+  __device__ void release(int st) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[st]);
+    ++r.it;
+  }
+
+  __device__ bool barrier() {
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) sm.nred[0] = grid_barrier(s, nct, gen) ? 1.f : 0.f;
+    consumer_sync(kConsumerThreads);
+    const bool good = sm.nred[0] != 0.f;
+    consumer_sync(kConsumerThreads);
+    return ok = ok && good;
+  }
+
+  // Block-wide sum over the 256 consumer threads.
+  __device__ float block_sum(float v) {
+    v = warp_sum(v);
+    if (lane == 0) sm.nred[w] = v;
+    consumer_sync(kConsumerThreads);
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kConsumerWarps; ++i) t += sm.nred[i];
+    consumer_sync(kConsumerThreads);
+    return t;
+  }
+
+  // Token id of the step, checked against the embedding table (an
+  // out-of-range id raises kErrBadInput and reads row 0 instead).
+  __device__ int64_t checked_token(const AicasPhase& d) {
+    if (in.token >= 0 && in.token < d.embed_rows) return in.token;
+    if (tid == 0) raise_error(s, kErrBadInput);
+    return 0;
+  }
+
+  // Builds the phase input vector into sm.u.xbuf (fp16 values):
+  //   v = x (or the token's embedding row) [+ x2, rounded]; optionally
+  //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
+  __device__ void build_x(const AicasPhase& d) {
+    const int k = d.k;
+    const __half* x = reinterpret_cast<const __half*>(d.x);
+    if (d.flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
+    const __half* x2 = reinterpret_cast<const __half*>(d.x2);
+    float ss = 0.f;
+    const int nvec = k / 8;
+    for (int v = tid; v < nvec; v += kConsumerThreads) {
+      uint4 raw = ldcg_u4(x + v * 8);
+      __half2* hp = reinterpret_cast<__half2*>(&raw);
+      if (d.flags & AICAS_F_X_ADD) {
+        uint4 raw2 = ldcg_u4(x2 + v * 8);
+        const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 fa = __half22float2(hp[j]), fb = __half22float2(hq[j]);
+          hp[j] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(hp[j]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+      *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]) = raw;
+    }
+    if (d.flags & AICAS_F_NORM) {
+      const float tot = block_sum(ss);
+      const float inv = rsqrtf(tot / (float)k + d.eps);
+      const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
+      for (int v = tid; v < nvec; v += kConsumerThreads) {
+        uint4 raw = *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]);
+        uint4 wr = __ldg(reinterpret_cast<const uint4*>(nw + v * 8));
+        __half2* hp = reinterpret_cast<__half2*>(&raw);
+        const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __half22float2(hp[j]);
+          float2 g = __half22float2(wp[j]);
+          hp[j] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
+        }
+        *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]) = raw;
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    if ((d.flags & AICAS_F_STORE_X) && cta == 0 && d.x_out) {
+      __half* xo = reinterpret_cast<__half*>(d.x_out);
+      for (int v = tid; v < nvec; v += kConsumerThreads)
+        *reinterpret_cast<uint4*>(xo + v * 8) = *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]);
+    }
+  }
+
+  __device__ float resid_value(const AicasPhase& d, int row) {
+    const __half* rp = reinterpret_cast<const __half*>(d.resid);
+    if (d.flags & AICAS_F_RESID_EMBED) rp += (size_t)checked_token(d) * d.n;
+    float rv = ldcg_half(rp + row);
+    if (d.flags & AICAS_F_RESID_ADD) rv = r16(rv + ldcg_half(reinterpret_cast<const __half*>(d.resid2) + row));
+    return rv;
+  }
+
+  // Reduce-scatter of NV per-lane partials: afterwards lane l holds the warp
+  // total of value index ((l>>4)&1)*NV/2 + ... (see idx below).
+  template <int NV>
+  __device__ __forceinline__ float reduce_scatter(float (&v)[NV], int& idx) {
+    // NV in {4, 8}
+    float a[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) a[i] = v[i];
+    int half = NV / 2, base = 0;
+    // step xor 16
+    {
+      const bool hi = lane & 16;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        float send = hi ? a[i] : a[i + NV / 2];
+        float keep = hi ? a[i + NV / 2] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+      base = hi ? NV / 2 : 0;
+    }
+    // step xor 8
+    {
+      const bool hi = lane & 8;
+#pragma unroll
+      for (int i = 0; i < NV / 4; ++i) {
+        float send = hi ? a[i] : a[i + NV / 4];
+        float keep = hi ? a[i + NV / 4] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      base += hi ? NV / 4 : 0;
+    }
+    float t = a[0];
+    if (NV == 8) {
+      const bool hi = lane & 4;
+      float send = hi ? a[0] : a[1];
+      float keep = hi ? a[1] : a[0];
+      t = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      base += hi ? 1 : 0;
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+    } else {
+      t += __shfl_xor_sync(0xffffffffu, t, 4);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+    }
+    (void)half;
+    idx = base;
+    return t;
+  }
+
+  // GEMV / GATEUP / LMHEAD phase.
+  __device__ void run_matvec(const AicasPhase& d) {
+    build_x(d);
+    const int C = (d.k + kChunk - 1) / kChunk;
+    const int G = (d.n + kRows - 1) / kRows;
+    const Range rg = split_range(G, nct, cta, d.rot);
+    const int col_in_chunk = 256 * w + 8 * lane;
+    uint4 xr[kMaxChunks];
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = c * kChunk + col_in_chunk;
+      xr[c] = (c < C && col < d.k) ? *reinterpret_cast<const uint4*>(&sm.u.xbuf[col]) : make_uint4(0, 0, 0, 0);
+    }
+    const bool gateup = d.kind == AICAS_PH_GATEUP;
+    const bool lm = d.kind == AICAS_PH_LMHEAD;
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+    __half* logits = nullptr;
+    if (lm && a.state && a.state->logits) {
+      const int64_t ring = a.state->logits_ring > 0 ? a.state->logits_ring : 1;
+      logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * d.n;
+    }
+    int buf = 0;
+    for (int g = rg.start; g < rg.start + rg.count; ++g) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        if (part == 1 && !gateup) break;
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+          if (c < C) {
+            const int st = r.stage();
+            wait_full(st);
+            const int clen = min(kChunk, d.k - c * kChunk);
+            if (col_in_chunk < clen) {
+              const uint8_t* base = sm.ring[st] + col_in_chunk * 2;
+#pragma unroll
+              for (int i = 0; i < kRows; ++i) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(base + i * kRowBytes);
+                acc[part * 4 + i] = dot8_f16(wv, xr[c], acc[part * 4 + i]);
+              }
+            }
+            release(st);
+          }
+        }
+      }
+      int idx;
+      if (gateup) {
+        float t = reduce_scatter<8>(acc, idx);
+        if ((lane & 3) == 0) sm.red[buf][w][idx] = t;
+      } else {
+        float a4[4] = {acc[0], acc[1], acc[2], acc[3]};
+        float t = reduce_scatter<4>(a4, idx);
+        if ((lane & 7) == 0) sm.red[buf][w][idx] = t;
+      }
+      consumer_sync(kConsumerThreads);
+      if (tid < kRows) {
+        const int row = g * kRows + tid;
+        if (row < d.n) {
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < kConsumerWarps; ++i) sum += sm.red[buf][i][tid];
+          __half* out = reinterpret_cast<__half*>(d.out);
+          if (gateup) {
+            float up = 0.f;
+#pragma unroll
+            for (int i = 0; i < kConsumerWarps; ++i) up += sm.red[buf][i][4 + tid];
+            const float gq = r16(sum), uq = r16(up);
+            const float sl = r16(gq / (1.0f + expf(-gq)));
+            out[row] = __float2half_rn(sl * uq);
+          } else {
+            if (d.flags & AICAS_F_BIAS) sum += __half2float(reinterpret_cast<const __half*>(d.bias)[row]);
+            float y = r16(sum);
+            if (d.flags & AICAS_F_RESID) y = r16(resid_value(d, row) + y);
+            if (lm) {
+              if (logits) logits[row] = __float2half_rn(y);
+              if (d.out) out[row] = __float2half_rn(y);
+              if (y > best_v) {  // rows ascend: strict > keeps the first max
+                best_v = y;
+                best_i = row;
+              }
+            } else {
+              out[row] = __float2half_rn(y);
+            }
+          }
+        }
+      }
+      buf ^= 1;
+    }
+    if (lm) finish_argmax(d, best_v, best_i);
+  }
+
+  __device__ void finish_argmax(const AicasPhase& d, float bv, int bi) {
+    if (tid < kRows) {
+      sm.best_v[tid] = bv;
+      sm.best_i[tid] = bi;
+    }
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      float v = sm.best_v[0];
+      int i = sm.best_i[0];
+      for (int t = 1; t < kRows; ++t) {
+        if (sm.best_v[t] > v || (sm.best_v[t] == v && sm.best_i[t] < i)) {
+          v = sm.best_v[t];
+          i = sm.best_i[t];
+        }
+      }
+      s->am_val[cta] = v;
+      s->am_idx[cta] = i;
+      __threadfence();
+      const uint32_t prev = atomicAdd(&s->argmax_done, 1u);
+      if (prev == (uint32_t)nct - 1) {
+        __threadfence();
+        float bv2 = -INFINITY;
+        int bi2 = 0x7fffffff;
+        for (int c = 0; c < nct; ++c) {
+          const float cv = __ldcg(&s->am_val[c]);
+          const int ci = __ldcg(&s->am_idx[c]);
+          if (cv > bv2 || (cv == bv2 && ci < bi2)) {
+            bv2 = cv;
+            bi2 = ci;
+          }
+        }
+        s->argmax_done = 0;
+        if (d.idx_out) *reinterpret_cast<int64_t*>(d.idx_out) = bi2;
+        AicasStepState* stt = a.state;
+        if (stt) {
+          const int64_t step = in.step;
+          if (stt->out_tokens && step < stt->max_steps) stt->out_tokens[step] = bi2;
+          const int64_t nx = step + 1;
+          if (stt->script && nx < stt->script_len) {
+            const int64_t* e = stt->script + nx * 5;
+            stt->token = e[0];
+            stt->cache_pos = e[1];
+            stt->rope[0] = e[2];
+            stt->rope[1] = e[3];
+            stt->rope[2] = e[4];
+          } else {
+            stt->token = bi2;
+            stt->cache_pos = in.pos + 1;
+            stt->rope[0] = in.rope[0] + 1;
+            stt->rope[1] = in.rope[1] + 1;
+            stt->rope[2] = in.rope[2] + 1;
+          }
+          stt->step = nx;
+          __threadfence();
+        }
+      }
+    }
+    consumer_sync(kConsumerThreads);
+  }
+
+  // q/k RMSNorm over one head (128 threads: t in [0,128) of group `grp`) and
+  // rotary embedding; returns the rotated fp16 value as float.
+  // (modeling_qwen3_vl.py:398-403 per head, then :124-128 + :427-431)
+  __device__ float norm_rope_128(float v, const __half* nw, int grp, int t, float eps, bool rope) {
+    AttnSmem& at = sm.u.at;
+    float ss = warp_sum(v * v);
+    if (lane == 0) at.red[w] = ss;
+    consumer_sync(kConsumerThreads);
+    const float tot = at.red[grp * 4 + 0] + at.red[grp * 4 + 1] + at.red[grp * 4 + 2] + at.red[grp * 4 + 3];
+    const float n = r16(v * rsqrtf(tot / (float)kHD + eps));
+    const float qn = r16(__half2float(nw[t]) * n);
+    if (!rope) {
+      consumer_sync(kConsumerThreads);
+      return qn;
+    }
+    at.tmp[grp][t] = qn;
+    consumer_sync(kConsumerThreads);
+    const float rot = t < kHD / 2 ? -at.tmp[grp][t + kHD / 2] : at.tmp[grp][t - kHD / 2];
+    const float outv = r16(r16(qn * at.cs[t]) + r16(rot * at.sn[t]));
+    consumer_sync(kConsumerThreads);
+    return outv;
+  }
+
+  __device__ void run_attention(const AicasPhase& d) {
+    AttnSmem& at = sm.u.at;
+    const bool q_ready = d.flags & AICAS_F_Q_READY;
+    const int valid = phase_valid_len(d, in);
+    if (valid == 0) {
+      if (tid == 0 && cta == 0) raise_error(s, kErrBadInput);
+      return;
+    }
+    const int pos = valid - 1;
+    const int cph = (valid + kAttnChunk - 1) / kAttnChunk;
+    const int U = d.kv_heads * cph;
+    const Range rg = split_range(U, nct, cta, 0);
+    const __half* qkv = reinterpret_cast<const __half*>(d.x);
+    __half* kc = reinterpret_cast<__half*>(d.k_cache);
+    __half* vc = reinterpret_cast<__half*>(d.v_cache);
+    const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
+    if (!q_ready && tid < kHD) {
+      // interleaved MRoPE (modeling_qwen3_vl.py:352-386)
+      const int i = tid % (kHD / 2);
+      const AicasStepState* stt = a.state;
+      int axis = 0;
+      if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
+      else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
+      const float ang = stt->inv_freq[i] * (float)in.rope[axis];
+      at.cs[tid] = r16(cosf(ang));
+      at.sn[tid] = r16(sinf(ang));
+    }
+    consumer_sync(kConsumerThreads);
+    const float scale = d.scale;
+    const int grp = tid / kHD, t = tid % kHD;
+    // per-warp online-softmax state for the 2 query heads of the current KV head
+    float m[2], l[2], acc[2][4];
+    float qreg[2][4];
+    for (int u = rg.start; u < rg.start + rg.count; ++u) {
+      const int h = u / cph, j = u % cph;
+      const bool seg_start = (u == rg.start) || (j == 0);
+      const bool seg_end = (u == rg.start + rg.count - 1) || (j == cph - 1);
+      const int jpos = pos / kAttnChunk;
+      if (seg_start) {
+        const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
+        const bool has_pos = !q_ready && jpos >= j && jpos <= last_j;
+        // queries of heads 2h, 2h+1
+        const int qh = h * 2 + grp;
+        float qv = ldcg_half(qkv + qh * kHD + t);
+        if (!q_ready) qv = norm_rope_128(qv, reinterpret_cast<const __half*>(d.norm_w), grp, t, d.eps, true);
+        at.q[grp][t] = qv;
+        if (has_pos) {
+          // fresh k (group 0 threads) and v (group 1 threads) of this head
+          const float raw = ldcg_half(qkv + qsz + (grp == 0 ? 0 : kvsz) + h * kHD + t);
+          const float kv = norm_rope_128(raw, reinterpret_cast<const __half*>(d.norm_w2), grp, t, d.eps, true);
+          if (grp == 0) at.kf[t] = kv;
+          else at.vf[t] = raw;
+        }
+        consumer_sync(kConsumerThreads);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) qreg[g][e] = at.q[g][lane * 4 + e];
+          m[g] = -INFINITY;
+          l[g] = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+        }
+      }
+      const int st = r.stage();
+      wait_full(st);
+      const int p0 = j * kAttnChunk;
+      uint8_t* kt = sm.ring[st];
+      uint8_t* vt = sm.ring[st] + kStageBytes / 2;
+      if (!q_ready && j == jpos) {
+        // write the current position into the tile and into the cache
+        const int rr = pos - p0;
+        if (grp == 0) {
+          const __half hv = __float2half_rn(at.kf[t]);
+          reinterpret_cast<__half*>(kt)[rr * kHD + t] = hv;
+          kc[((size_t)h * d.max_len + pos) * kHD + t] = hv;
+        } else {
+          const __half hv = __float2half_rn(at.vf[t]);
+          reinterpret_cast<__half*>(vt)[rr * kHD + t] = hv;
+          vc[((size_t)h * d.max_len + pos) * kHD + t] = hv;
+        }
+        fence_proxy_async_smem();
+        consumer_sync(kConsumerThreads);
+      }
+      // scores of this warp's 4 positions for both query heads
+      float sc[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int pr = w * 4 + i;
+        const uint2 kv = *reinterpret_cast<const uint2*>(kt + pr * kHD * 2 + lane * 8);
+        const __half2* kh = reinterpret_cast<const __half2*>(&kv);
+        const float2 k01 = __half22float2(kh[0]), k23 = __half22float2(kh[1]);
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+          sc[i * 2 + g] = qreg[g][0] * k01.x + qreg[g][1] * k01.y + qreg[g][2] * k23.x + qreg[g][3] * k23.y;
+      }
+      int idx;
+      const float tot = reduce_scatter<8>(sc, idx);
+      // broadcast all 8 scores: value v lives in lane ((v>>2)&1)<<4 | ((v>>1)&1)<<3 | (v&1)<<2
+      float s8[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const int src = (((v >> 2) & 1) << 4) | (((v >> 1) & 1) << 3) | ((v & 1) << 2);
+        s8[v] = __shfl_sync(0xffffffffu, tot, src);
+      }
+      (void)idx;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        float cmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int p = p0 + w * 4 + i;
+          s8[i * 2 + g] = (p < valid) ? s8[i * 2 + g] * scale : -INFINITY;
+          cmax = fmaxf(cmax, s8[i * 2 + g]);
+        }
+        const float mn = fmaxf(m[g], cmax);
+        if (mn == -INFINITY) continue;
+        const float corr = expf(m[g] - mn);
+        l[g] *= corr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+        m[g] = mn;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int p = p0 + w * 4 + i;
+          if (p < valid) {
+            const float pr = expf(s8[i * 2 + g] - mn);
+            l[g] += pr;
+            const uint2 vv = *reinterpret_cast<const uint2*>(vt + (w * 4 + i) * kHD * 2 + lane * 8);
+            const __half2* vh = reinterpret_cast<const __half2*>(&vv);
+            const float2 v01 = __half22float2(vh[0]), v23 = __half22float2(vh[1]);
+            acc[g][0] += pr * v01.x;
+            acc[g][1] += pr * v01.y;
+            acc[g][2] += pr * v23.x;
+            acc[g][3] += pr * v23.y;
+          }
+        }
+      }
+      release(st);
+      if (seg_end) {
+        // merge the 8 warps' states of this segment into one partial
+        if (lane == 0) {
+          at.wm[w][0] = m[0];
+          at.wm[w][1] = m[1];
+          at.wl[w][0] = l[0];
+          at.wl[w][1] = l[1];
+        }
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
+        consumer_sync(kConsumerThreads);
+        float M = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][grp]);
+        float L = 0.f, A = 0.f;
+#pragma unroll
+        for (int i = 0; i < kConsumerWarps; ++i) {
+          const float mi = at.wm[i][grp];
+          if (mi != -INFINITY) {
+            const float f = expf(mi - M);
+            L += at.wl[i][grp] * f;
+            A += at.wacc[i][grp][t] * f;
+          }
+        }
+        const int first_owner = owner_of(h * cph, U, nct);
+        const int last_owner = owner_of(h * cph + cph - 1, U, nct);
+        const int split = cta - first_owner;
+        const int nsplit = last_owner - first_owner + 1;
+        float* pp = &s->part[h][split][grp][0];
+        if (t == 0) {
+          pp[0] = M;
+          pp[1] = L;
+        }
+        pp[2 + t] = A;
+        __threadfence();
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) {
+          const uint32_t prev = atomicAdd(&s->head_done[h], 1u);
+          at.last = (prev == (uint32_t)nsplit - 1) ? 1 : 0;
+          if (at.last) {
+            s->head_done[h] = 0;
+            __threadfence();
+          }
+        }
+        consumer_sync(kConsumerThreads);
+        if (at.last) {
+          float Mg = -INFINITY;
+          for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, __ldcg(&s->part[h][sp][grp][0]));
+          float Lg = 0.f, Ag = 0.f;
+          for (int sp = 0; sp < nsplit; ++sp) {
+            const float* q = &s->part[h][sp][grp][0];
+            const float f = expf(__ldcg(q) - Mg);
+            Lg += __ldcg(q + 1) * f;
+            Ag += __ldcg(q + 2 + t) * f;
+          }
+          reinterpret_cast<__half*>(d.out)[(h * 2 + grp) * kHD + t] = __float2half_rn(Ag / Lg);
+        }
+        consumer_sync(kConsumerThreads);
+      }
+    }
+  }
+
+  __device__ void run(const AicasPhase* P, int n_phases) {
+    for (int ph = 0; ph < n_phases; ++ph) {
+      if (ph > 0) barrier();
+      const AicasPhase& d = P[ph];
+      if (d.kind == AICAS_PH_ATTN) run_attention(d);
+      else run_matvec(d);
+    }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  StepIn in{};
+  if (a.state) {
+    const volatile AicasStepState* st = a.state;
+    in.token = st->token;
+    in.pos = st->cache_pos;
+    in.rope[0] = st->rope[0];
+    in.rope[1] = st->rope[1];
+    in.rope[2] = st->rope[2];
+    in.step = st->step;
+  }
+  const AicasPhase* P = a.phases ? a.phases : a.inl;
+  const int warp = threadIdx.x / 32;
+  if (warp == 0) {
+    if ((threadIdx.x & 31) == 0) run_producer(a, sm, in);
+    return;
+  }
+  Consumer c{a, sm, in, a.scratch};
+  c.tid = threadIdx.x - 32;
+  c.w = warp - 1;
+  c.lane = threadIdx.x & 31;
+  c.nct = gridDim.x;
+  c.cta = blockIdx.x;
+  c.gen = *reinterpret_cast<volatile uint32_t*>(&a.scratch->bar_gen);
+  c.run(P, a.n_phases);
+}
+
+}  // namespace aicas
+
+// ===========================================================================
+// Host side: launch + C ABI
+// ===========================================================================
+#include "aicas_decode.h"
+
+namespace aicas {
+
+static constexpr int kMaxDevices = 64;
+static int g_attr_done[kMaxDevices];
+static int g_num_sms[kMaxDevices];
+static int g_cooperative = 1;
+
+static int device_setup(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
+  if (!g_attr_done[dev]) {
+    if (cudaFuncSetAttribute(decode_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(Smem)) != cudaSuccess)
+      return AICAS_ERR_CUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
+    g_num_sms[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
+    g_attr_done[dev] = 1;
+  }
+  *dev_out = dev;
+  return AICAS_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int validate_phase(const AicasPhase& d) {
+  switch (d.kind) {
+    case AICAS_PH_GEMV:
+    case AICAS_PH_GATEUP:
+    case AICAS_PH_LMHEAD:
+      if (d.n < 1 || d.k < 8 || d.k % 8 != 0 || d.k > AICAS_MAX_K) return AICAS_ERR_SHAPE;
+      if (!d.w || !aligned16(d.w)) return AICAS_ERR_ALIGN;
+      if (!d.x || !aligned16(d.x)) return AICAS_ERR_ALIGN;
+      if ((d.flags & AICAS_F_X_ADD) && (!d.x2 || !aligned16(d.x2))) return AICAS_ERR_ALIGN;
+      if ((d.flags & AICAS_F_NORM) && (!d.norm_w || !aligned16(d.norm_w))) return AICAS_ERR_ALIGN;
+      if ((d.flags & (AICAS_F_X_EMBED | AICAS_F_RESID_EMBED)) && d.embed_rows < 1) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_RESID) && !d.resid) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_RESID_ADD) && !d.resid2) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_BIAS) && !d.bias) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_STORE_X) && (!d.x_out || !aligned16(d.x_out))) return AICAS_ERR_ALIGN;
+      if (d.kind != AICAS_PH_LMHEAD && !d.out) return AICAS_ERR_ARG;
+      if (d.kind == AICAS_PH_GATEUP && (d.flags & (AICAS_F_RESID | AICAS_F_BIAS))) return AICAS_ERR_ARG;
+      return AICAS_OK;
+    case AICAS_PH_ATTN:
+      if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
+      if (d.max_len < 1) return AICAS_ERR_SHAPE;
+      if (!d.k_cache || !d.v_cache || !aligned16(d.k_cache) || !aligned16(d.v_cache)) return AICAS_ERR_ALIGN;
+      if (!d.x || !d.out) return AICAS_ERR_ARG;
+      if (!(d.flags & AICAS_F_Q_READY) && (!d.norm_w || !d.norm_w2)) return AICAS_ERR_ARG;
+      return AICAS_OK;
+    default:
+      return AICAS_ERR_ARG;
+  }
+}
+
+static int launch_program(ProgramArgs& a, cudaStream_t stream) {
+  int dev;
+  int rc = device_setup(&dev);
+  if (rc) return rc;
+  if (!a.scratch) return AICAS_ERR_ARG;
+  if (a.n_phases < 1) return AICAS_ERR_ARG;
+  // Attention needs the rotary table of a step state unless q is final.
+  const AicasPhase* P = a.phases ? nullptr : a.inl;
+  if (P) {
+    for (int i = 0; i < a.n_phases; ++i) {
+      if ((rc = validate_phase(P[i]))) return rc;
+      if (P[i].kind == AICAS_PH_ATTN && !(P[i].flags & AICAS_F_Q_READY) && !a.state) return AICAS_ERR_ARG;
+      if ((P[i].flags & (AICAS_F_X_EMBED | AICAS_F_RESID_EMBED)) && !a.state) return AICAS_ERR_ARG;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g_num_sms[dev]);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = g_cooperative;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_program_kernel, a);
+  return e == cudaSuccess ? AICAS_OK : AICAS_ERR_CUDA;
+}
+
+
+}  // namespace aicas
+
+using namespace aicas;
+
+extern "C" {
+
+AICAS_API int aicas_abi_version(void) { return AICAS_ABI_VERSION; }
+
+AICAS_API size_t aicas_scratch_bytes(void) { return sizeof(AicasScratch); }
+
+AICAS_API int aicas_layout_signature(int64_t* out, int n) {
+  const int64_t v[] = {(int64_t)sizeof(AicasPhase), (int64_t)sizeof(AicasStepState), (int64_t)sizeof(AicasScratch),
+                       (int64_t)offsetof(AicasPhase, w), (int64_t)offsetof(AicasPhase, eps),
+                       (int64_t)offsetof(AicasStepState, inv_freq), (int64_t)offsetof(AicasScratch, part)};
+  const int m = (int)(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < n && i < m; ++i) out[i] = v[i];
+  return m;
+}
+
+AICAS_API int aicas_num_ctas(int device) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return -AICAS_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return -AICAS_ERR_CUDA;
+  int dev = 0;
+  const int rc = device_setup(&dev);
+  if (device != prev) cudaSetDevice(prev);
+  return rc ? -rc : g_num_sms[dev];
+}
+
+AICAS_API int aicas_set_cooperative_launch(int enable) {
+  g_cooperative = enable ? 1 : 0;
+  return AICAS_OK;
+}
+
+AICAS_API const char* aicas_error_string(int code) {
+  switch (code) {
+    case AICAS_OK: return "ok";
+    case AICAS_ERR_ARG: return "invalid argument";
+    case AICAS_ERR_SHAPE: return "unsupported shape";
+    case AICAS_ERR_ALIGN: return "pointer or size not 16-byte aligned";
+    case AICAS_ERR_CUDA: return "CUDA runtime error (launch or device query failed)";
+    case kErrBarrierTimeout: return "device: grid barrier timed out";
+    case kErrFullTimeout: return "device: bulk copy did not complete in time";
+    case kErrEmptyTimeout: return "device: ring stage was not released in time";
+    case kErrDrainTimeout: return "device: in-flight copies did not drain in time";
+    case kErrBadPhase: return "device: bad phase descriptor";
+    case kErrBadInput: return "device: token id or cache position out of range";
+    default: return "unknown error";
+  }
+}
+
+AICAS_API int aicas_validate_phases(const AicasPhase* phases, int n) {
+  if (!phases || n < 1) return AICAS_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const int rc = validate_phase(phases[i]);
+    if (rc) return rc;
+  }
+  return AICAS_OK;
+}
+
+AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
+                                       void* scratch, cudaStream_t stream) {
+  if (!device_phases || n_phases < 1 || !state) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  a.phases = device_phases;
+  a.n_phases = n_phases;
+  a.state = state;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_gemv_f16(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t k,
+                             void* scratch, cudaStream_t stream) {
+  if (n < 1 || n > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  AicasPhase& d = a.inl[0];
+  d.kind = AICAS_PH_GEMV;
+  d.flags = bias ? AICAS_F_BIAS : 0;
+  d.n = (int32_t)n;
+  d.k = (int32_t)k;
+  d.w = w;
+  d.x = x;
+  d.bias = bias;
+  d.out = y;
+  a.n_phases = 1;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_rmsnorm_qkv_f16(const void* x, const void* norm_w, const void* w, const void* bias, void* y,
+                                    int64_t n, int64_t k, float eps, void* scratch, cudaStream_t stream) {
+  if (n < 1 || n > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  AicasPhase& d = a.inl[0];
+  d.kind = AICAS_PH_GEMV;
+  d.flags = AICAS_F_NORM | (bias ? AICAS_F_BIAS : 0);
+  d.n = (int32_t)n;
+  d.k = (int32_t)k;
+  d.w = w;
+  d.x = x;
+  d.norm_w = norm_w;
+  d.bias = bias;
+  d.out = y;
+  d.eps = eps;
+  a.n_phases = 1;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out, const void* norm_w,
+                                      const void* gate_up_w, const void* down_w, const void* bias, void* act_out,
+                                      void* out, int64_t hidden, int64_t inter, float eps, void* scratch,
+                                      cudaStream_t stream) {
+  if (hidden < 1 || inter < 1 || hidden > AICAS_MAX_K || inter > AICAS_MAX_K) return AICAS_ERR_SHAPE;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  AicasPhase& g = a.inl[0];
+  g.kind = AICAS_PH_GATEUP;
+  g.flags = AICAS_F_X_ADD | AICAS_F_NORM;
+  g.n = (int32_t)inter;
+  g.k = (int32_t)hidden;
+  g.w = gate_up_w;
+  g.x = residual;
+  g.x2 = attn_out;
+  g.norm_w = norm_w;
+  g.out = act_out;
+  g.eps = eps;
+  AicasPhase& dn = a.inl[1];
+  dn.kind = AICAS_PH_GEMV;
+  dn.flags = AICAS_F_RESID | AICAS_F_RESID_ADD | (bias ? AICAS_F_BIAS : 0);
+  dn.n = (int32_t)hidden;
+  dn.k = (int32_t)inter;
+  dn.w = down_w;
+  dn.x = act_out;
+  dn.resid = residual;
+  dn.resid2 = attn_out;
+  dn.bias = bias;
+  dn.out = out;
+  dn.rot = 37;  // the down sweep's extra row groups land on other CTAs than gate_up's
+  a.n_phases = 2;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,
+                                            const void* cache_position, float scale, void* out, int64_t q_heads,
+                                            int64_t kv_heads, int64_t max_len, void* scratch, cudaStream_t stream) {
+  if (max_len < 1 || max_len > (1 << 30)) return AICAS_ERR_SHAPE;
+  if (!cache_position) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  AicasPhase& d = a.inl[0];
+  d.kind = AICAS_PH_ATTN;
+  d.flags = AICAS_F_Q_READY;
+  d.q_heads = (int32_t)q_heads;
+  d.kv_heads = (int32_t)kv_heads;
+  d.max_len = (int32_t)max_len;
+  d.x = q;
+  d.k_cache = const_cast<void*>(k_cache);
+  d.v_cache = const_cast<void*>(v_cache);
+  d.pos_ptr = cache_position;
+  d.out = out;
+  d.scale = scale;
+  a.n_phases = 1;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const void* w, void* logits,
+                                       void* token_out, int64_t vocab, int64_t k, float eps, void* scratch,
+                                       cudaStream_t stream) {
+  if (vocab < 1 || vocab > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
+  if (!token_out) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  AicasPhase& d = a.inl[0];
+  d.kind = AICAS_PH_LMHEAD;
+  d.flags = norm_w ? AICAS_F_NORM : 0;
+  d.n = (int32_t)vocab;
+  d.k = (int32_t)k;
+  d.w = w;
+  d.x = x;
+  d.norm_w = norm_w;
+  d.out = logits;
+  d.idx_out = token_out;
+  d.eps = eps;
+  a.n_phases = 1;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+}  // extern "C"

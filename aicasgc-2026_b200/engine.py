@@ -1,0 +1,302 @@
+"""B200 decode engine for the Qwen3-VL-2B text decoder.
+
+One decode step = ONE persistent launch of the phase-program kernel
+(`aicas_decode_program_f16`): 28 x [RMSNorm+QKV, q/k-norm+MRoPE+KV-write+
+split-KV attention, o_proj+residual, RMSNorm+gate_up+SiLU*up,
+down+residual] + final RMSNorm + tied lm_head + argmax, 141 phases separated
+by bounded grid barriers, weights streamed by bulk async copies.
+
+The step reads its inputs (token, cache slot, 3-axis rope position) from a
+device-resident step state and advances it itself, so a run of N steps is N
+back-to-back launches with no host work between them, captured once in a
+CUDA graph.  A prompt is fed as a "script" of forced inputs: one step per
+prompt token, whose argmax outputs are ignored until the script ends.
+
+This replaces, in the reference: `GreedyDecodeEngine.generate`'s hot loop
+(evaluation_wrapper.py:278-313), `DecodeCudaGraphRunner` replay/_run_step
+(evaluation_wrapper.py:788-791, 941-960), HF's layer loop with
+`OptimizedDecoderLayer.forward` (optimized_layer.py:108-469), the patched
+lm_head (evaluation_wrapper.py:1210-1245) and `torch.argmax` (:952).
+
+KV layout: per layer `keys/values [1, num_kv_heads, max_cache_len, 128]` fp16,
+the layout of HF `StaticLayer` (transformers/cache_utils.py:247-354) that the
+reference's kernels index.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from _native import (F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED, PH_ATTN, PH_GATEUP, PH_GEMV,
+                     PH_LMHEAD, AicasError, AicasPhase, AicasStepState, check, lib, scratch_bytes)
+from _ops import device_error
+from qwen3vl_config import QWEN3VL_2B, Qwen3VLTextShape
+
+
+def hf_inv_freq(shape: Qwen3VLTextShape) -> torch.Tensor:
+    """Rotary inverse frequencies computed exactly as HF does (CPU fp32,
+    modeling_qwen3_vl.py:343-346)."""
+    d = shape.head_dim
+    return 1.0 / (shape.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64).to(dtype=torch.float) / d))
+
+
+class Qwen3VLDecodeEngine:
+    """Batch-1 greedy decode engine (fp16 weights, fp32 accumulation).
+
+    `state` maps HF text-model keys (see `qwen3vl_config.synthetic_state`) to
+    tensors on any device / dtype; they are converted to fp16 on `device`.
+    """
+
+    def __init__(self, state: dict, shape: Qwen3VLTextShape = QWEN3VL_2B, *, max_cache_len: int = 2048,
+                 device: torch.device | str = "cuda", max_steps: int = 8192, logits_ring: int = 0):
+        self.shape = shape
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        if max_cache_len % 32:
+            max_cache_len += 32 - max_cache_len % 32
+        self.max_cache_len = max_cache_len
+        self.max_steps = max_steps
+        self._lib = lib()
+        dev = self.device
+        f16 = dict(dtype=torch.float16, device=dev)
+        s = shape
+
+        def W(key):
+            return state[key].to(**f16).contiguous()
+
+        with torch.cuda.device(dev):
+            self.embed = W("embed_tokens.weight")
+            self.final_norm = W("norm.weight")
+            self.layers = []
+            for i in range(s.num_layers):
+                p = f"layers.{i}."
+                self.layers.append({
+                    "ln1": W(p + "input_layernorm.weight"),
+                    "qkv": torch.cat([W(p + "self_attn.q_proj.weight"), W(p + "self_attn.k_proj.weight"),
+                                      W(p + "self_attn.v_proj.weight")], 0).contiguous(),
+                    "qn": W(p + "self_attn.q_norm.weight"),
+                    "kn": W(p + "self_attn.k_norm.weight"),
+                    "o": W(p + "self_attn.o_proj.weight"),
+                    "ln2": W(p + "post_attention_layernorm.weight"),
+                    "gate_up": torch.cat([W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight")],
+                                         0).contiguous(),
+                    "down": W(p + "mlp.down_proj.weight"),
+                })
+            # StaticCache-layout KV: [layers][1, KVH, Lmax, 128]
+            kv_shape = (s.num_layers, 1, s.num_kv_heads, max_cache_len, s.head_dim)
+            self.k_cache = torch.zeros(kv_shape, **f16)
+            self.v_cache = torch.zeros(kv_shape, **f16)
+            self.h = torch.zeros(s.hidden, **f16)
+            self.h_mid = torch.zeros(s.hidden, **f16)
+            self.qkv = torch.zeros(s.qkv_rows, **f16)
+            self.attn = torch.zeros(s.q_size, **f16)
+            self.act = torch.zeros(s.intermediate, **f16)
+            self.out_tokens = torch.full((max_steps,), -1, dtype=torch.int64, device=dev)
+            self.logits_ring = int(logits_ring)
+            self.logits = (torch.zeros((logits_ring, s.vocab), **f16) if logits_ring > 0 else None)
+            self.scratch = torch.zeros(scratch_bytes(), dtype=torch.uint8, device=dev)
+            self.state_dev = torch.zeros(ctypes.sizeof(AicasStepState), dtype=torch.uint8, device=dev)
+            self.script = torch.zeros((1, 5), dtype=torch.int64, device=dev)
+            self.num_ctas = self._lib.aicas_num_ctas(dev.index)
+            if self.num_ctas <= 0:
+                raise AicasError(f"aicas_num_ctas failed ({self.num_ctas})")
+            self._build_program()
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._start_dev = None
+        self.script_len = 0
+        self._inv_freq = hf_inv_freq(s)
+
+    # ------------------------------------------------------------------ program
+    def _build_program(self):
+        s, nct = self.shape, self.num_ctas
+        eps = float(s.rms_eps)
+        phases = []
+        extra = 0
+
+        def ptr(t):
+            return t.data_ptr()
+
+        def gemv_like(kind, flags, n, k, w, x, out, norm_w=None, resid=None):
+            nonlocal extra
+            p = AicasPhase()
+            p.kind, p.flags, p.n, p.k = kind, flags, n, k
+            p.rot = extra % nct
+            groups = -(-n // 4)
+            extra += groups % nct
+            p.w, p.x, p.out = ptr(w), ptr(x), ptr(out)
+            p.norm_w = ptr(norm_w) if norm_w is not None else None
+            p.resid = ptr(resid) if resid is not None else None
+            p.embed_rows = s.vocab
+            p.eps = eps
+            phases.append(p)
+
+        for li, L in enumerate(self.layers):
+            first = li == 0
+            gemv_like(PH_GEMV, F_NORM | (F_X_EMBED if first else 0), s.qkv_rows, s.hidden, L["qkv"],
+                      self.embed if first else self.h, self.qkv, norm_w=L["ln1"])
+            a = AicasPhase()
+            a.kind, a.flags = PH_ATTN, 0
+            a.kv_heads, a.q_heads, a.max_len = s.num_kv_heads, s.num_heads, self.max_cache_len
+            a.x, a.out = ptr(self.qkv), ptr(self.attn)
+            a.norm_w, a.norm_w2 = ptr(L["qn"]), ptr(L["kn"])
+            a.k_cache, a.v_cache = ptr(self.k_cache[li]), ptr(self.v_cache[li])
+            a.eps, a.scale = eps, float(s.head_dim ** -0.5)
+            phases.append(a)
+            gemv_like(PH_GEMV, F_RESID | (F_RESID_EMBED if first else 0), s.hidden, s.q_size, L["o"], self.attn,
+                      self.h_mid, resid=self.embed if first else self.h)
+            gemv_like(PH_GATEUP, F_NORM, s.intermediate, s.hidden, L["gate_up"], self.h_mid, self.act,
+                      norm_w=L["ln2"])
+            gemv_like(PH_GEMV, F_RESID, s.hidden, s.intermediate, L["down"], self.act, self.h, resid=self.h_mid)
+        gemv_like(PH_LMHEAD, F_NORM, s.vocab, s.hidden, self.embed, self.h, self.h, norm_w=self.final_norm)
+        phases[-1].out = None
+        arr = (AicasPhase * len(phases))(*phases)
+        check(self._lib.aicas_validate_phases(arr, len(phases)), "aicas_validate_phases")
+        raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+        self.program = raw.to(self.device)
+        self.n_phases = len(phases)
+
+    # ------------------------------------------------------------------ state
+    def _write_state(self, token, cache_pos, rope, step, script_len):
+        st = AicasStepState()
+        st.token, st.cache_pos = int(token), int(cache_pos)
+        for i in range(3):
+            st.rope[i] = int(rope[i])
+        st.step, st.script_len = int(step), int(script_len)
+        st.script = self.script.data_ptr()
+        st.out_tokens = self.out_tokens.data_ptr()
+        st.max_steps = self.max_steps
+        st.logits = self.logits.data_ptr() if self.logits is not None else None
+        st.logits_ring = max(self.logits_ring, 1)
+        for i in range(64):
+            st.inv_freq[i] = float(self._inv_freq[i])
+        for i in range(3):
+            st.mrope_section[i] = int(self.shape.mrope_section[i])
+        host = torch.frombuffer(bytearray(bytes(st)), dtype=torch.uint8)
+        self.state_dev.copy_(host, non_blocking=False)
+
+    def load_script(self, tokens, pos3=None, start_slot: int = 0):
+        """Forced inputs for the next len(tokens) steps: token i goes to cache
+        slot start_slot + i with rope positions pos3[:, i] (default: the slot
+        on all three axes).  After the script the engine decodes greedily
+        from slot start_slot + len(tokens), rope positions advancing by one."""
+        tokens = torch.as_tensor(tokens, dtype=torch.int64).reshape(-1).cpu()
+        P = tokens.numel()
+        if P < 1 or start_slot + P > self.max_cache_len:
+            raise AicasError("script does not fit the cache")
+        slots = torch.arange(start_slot, start_slot + P, dtype=torch.int64)
+        if pos3 is None:
+            pos3 = slots.expand(3, P)
+        pos3 = torch.as_tensor(pos3, dtype=torch.int64).reshape(3, P).cpu()
+        script = torch.stack([tokens, slots, pos3[0], pos3[1], pos3[2]], 1).contiguous()
+        self.script = script.to(self.device)
+        self.out_tokens.fill_(-1)
+        self._write_state(script[0, 0], script[0, 1], script[0, 2:5], 0, P)
+        self.script_len = P
+
+    # ------------------------------------------------------------------ launch
+    def launch(self, n: int = 1):
+        """n decode steps, eagerly (no graph)."""
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        for _ in range(n):
+            rc = self._lib.aicas_decode_program_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
+                                                    ctypes.c_void_p(self.state_dev.data_ptr()),
+                                                    ctypes.c_void_p(self.scratch.data_ptr()), stream)
+            check(rc, "aicas_decode_program_f16")
+
+    def graph(self, steps: int) -> torch.cuda.CUDAGraph:
+        """A CUDA graph of `steps` consecutive decode steps (captured once;
+        replays advance the device step state)."""
+        g = self._graphs.get(steps)
+        if g is None:
+            snap = self.snapshot()
+            self.launch(1)  # warm-up outside capture
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.launch(steps)
+            torch.cuda.synchronize(self.device)
+            self.restore(snap)
+            self._graphs[steps] = g
+        return g
+
+    def run(self, n: int, graph_steps: int = 32):
+        """n steps using graphs of `graph_steps` launches plus an eager tail."""
+        if graph_steps > 1 and n >= graph_steps:
+            g = self.graph(graph_steps)
+            for _ in range(n // graph_steps):
+                g.replay()
+            n %= graph_steps
+        if n:
+            self.launch(n)
+
+    def decode_host(self, start: torch.Tensor, n: int, out: torch.Tensor | None = None,
+                    graph_steps: int = 32) -> torch.Tensor:
+        """Public host-buffer decode call: `start` is a (pinned) CPU int64
+        tensor [5] = (token, cache_slot, t, h, w) of the first step; runs `n`
+        greedy steps and returns their tokens in a (pinned) CPU int64 tensor.
+        Host->device copy of the inputs and device->host copy of the tokens
+        are part of the call (the reference's replay writes its inputs and
+        reads the token back every step, evaluation_wrapper.py:788-791, 906-939)."""
+        if out is None:
+            out = torch.empty(n, dtype=torch.int64, pin_memory=True)
+        if self._start_dev is None:
+            self._start_dev = torch.empty(5, dtype=torch.int64, device=self.device)
+        self._start_dev.copy_(start, non_blocking=True)
+        # state fields token, cache_pos, rope[3] are the first five int64 words;
+        # step restarts at the script end so out_tokens[step] stays in range
+        st = self.state_dev.view(torch.int64)
+        st[0:5].copy_(self._start_dev)
+        st[5].fill_(self.script_len)
+        self.run(n, graph_steps)
+        out.copy_(self.out_tokens[self.script_len:self.script_len + n], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
+    def snapshot(self):
+        return self.state_dev.clone()
+
+    def restore(self, snap):
+        self.state_dev.copy_(snap)
+
+    # ------------------------------------------------------------------ API
+    def generate(self, prompt, max_new_tokens: int, pos3=None, graph_steps: int = 32) -> torch.Tensor:
+        """Greedy decode: prefill `prompt` (one step per token), then
+        max_new_tokens - 1 decode steps.  Returns the new tokens (CPU int64),
+        like `GreedyDecodeEngine.generate` (evaluation_wrapper.py:149-315)
+        minus the prompt."""
+        self.load_script(prompt, pos3)
+        P = self.script_len
+        total = P + max_new_tokens - 1
+        if total > self.max_steps or P + max_new_tokens > self.max_cache_len:
+            raise AicasError("request exceeds max_steps / max_cache_len")
+        self.launch(P)
+        self.run(max_new_tokens - 1, graph_steps)
+        toks = self.out_tokens[P - 1:P - 1 + max_new_tokens].cpu()
+        self.check_error()
+        return toks
+
+    def check_error(self):
+        code = device_error(self.scratch)
+        if code:
+            self.scratch.zero_()
+            raise AicasError(f"device error {code}: {self._lib.aicas_error_string(code).decode()}")
+
+    def step_logits(self, step: int) -> torch.Tensor:
+        if self.logits is None:
+            raise AicasError("engine built without a logits ring")
+        return self.logits[step % self.logits_ring]
+
+    # ------------------------------------------------------------------ roofline
+    def algorithmic_bytes(self, cache_pos: int) -> int:
+        """Bytes one step at cache slot `cache_pos` must move: all weights
+        plus K/V of slots [0, cache_pos) read and the new slot written."""
+        s = self.shape
+        return s.weight_bytes_per_step() + s.kv_bytes_per_position() * (cache_pos + 1)
+
+
+def estimate_tokens_per_second(shape: Qwen3VLTextShape, ctx: int, gbs: float) -> float:
+    b = shape.weight_bytes_per_step() + shape.kv_bytes_per_position() * (ctx + 1)
+    return gbs * 1e9 / b if b else math.inf

@@ -1,0 +1,316 @@
+"""Benchmark: batch-1 greedy decode of the Qwen3-VL-2B text decoder on B200.
+
+Workload: 28-layer fp16 text decoder with seeded random
+weights N(0, 0.02); KV cache prefilled from a 1024-token synthetic prefix whose
+slots 16..271 are a 16x16 image grid with 3-axis MRoPE positions; then 256
+greedy decode tokens, CUDA-graph captured.  One bench STEP = one such 256-token
+decode request starting from the prefilled cache (the prefix stays resident,
+decode slots 1024..1279 are rewritten by every step).  Weights (3.44 GB) are
+streamed from HBM for every token, far above the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU, each decoding its own request
+(request-level data parallelism, no collective on the decode path; "weak"
+scaling).  Rank 0 prints one JSON line.
+
+`--impl reference` times the reference's CPU path instead: the CPU oracle
+port (numpy fp32 restatement of the reference's HF decode step, oracle/) on
+the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "aicasgc-2026_b200"))
+sys.path.insert(0, str(REPO))
+
+PREFIX = 1024
+NEW = 256
+METRIC = "batch-1 decode tok/s"
+UNIT = "tok/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak_gbs():
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "BASELINE config 4: Qwen3-VL-2B text decoder, 28 layers fp16, batch 1, 1024-token prefix "
+                    "(16x16 vision grid, 3-axis MRoPE), 256 greedy decode tokens per step, CUDA graph",
+        "model": "Qwen3-VL-2B text decoder (random init N(0,0.02))",
+        "batch": 1, "prefix_len": PREFIX, "decode_tokens_per_step": NEW,
+        "parallelism": f"request-dp{n_gpus}",
+        "l2": "inputs larger than L2: 3.44 GB of weights streamed from HBM per token",
+    }
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxs.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxs) if maxs else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# --------------------------------------------------------------------------- CPU
+def cpu_oracle_decode(state16, seconds: float = 12.0, min_steps: int = 2, max_steps: int | None = None):
+    """Time the CPU oracle port (numpy fp32, all host threads) decoding at
+    cache slot 1024 over a synthetic KV prefix.  Returns (tok/s, steps, s)."""
+    import numpy as np
+
+    from engine import hf_inv_freq
+    from oracle.qwen3vl_oracle import Qwen3VLOracle
+    from qwen3vl_config import QWEN3VL_2B
+
+    cap = max_steps if max_steps is not None else 512
+    o = Qwen3VLOracle(state16, QWEN3VL_2B.num_layers, mode="fp32", max_cache_len=PREFIX + cap + 2,
+                      inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
+    rng = np.random.default_rng(0)
+    o.k_cache[:, :, :PREFIX] = rng.standard_normal(o.k_cache[:, :, :PREFIX].shape, dtype=np.float32)
+    o.v_cache[:, :, :PREFIX] = rng.standard_normal(o.v_cache[:, :, :PREFIX].shape, dtype=np.float32)
+    tok = 1234
+    o.decode_step(tok, PREFIX, np.full((3, 1), PREFIX, np.int64))  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        pos = PREFIX + 1 + n
+        logits = o.decode_step(tok, pos, np.full((3, 1), pos, np.int64))
+        tok = int(np.argmax(logits))
+        n += 1
+        el = time.perf_counter() - t0
+        if (n >= min_steps and el >= seconds) or n >= cap:
+            break
+    return n / el, n, el
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    import torch
+
+    from qwen3vl_config import QWEN3VL_2B, synthetic_state
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    st = synthetic_state(QWEN3VL_2B, seed=0, dtype=torch.float16)
+    # warm-up steps then exactly K timed steps; each step = 1 decode token at ctx ~1024
+    tps_w, _, _ = cpu_oracle_decode(st, seconds=0.0, min_steps=max(1, args.warmup), max_steps=max(1, args.warmup))
+    tps, n, el = cpu_oracle_decode(st, seconds=0.0, min_steps=args.steps, max_steps=args.steps)
+    sample = f"{n} decode tokens at cache slot {PREFIX}+ over a synthetic 1024-slot KV prefix (numpy fp32 port)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * el / n, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(world),
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference arm: CPU oracle port of the reference's HF decode step; a step here is one token",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU
+def run_ours(args, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+
+    from engine import Qwen3VLDecodeEngine
+    from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state, vision_grid_positions
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    shape = QWEN3VL_2B.with_layers(args.layers)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16)
+    eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev,
+                              max_steps=PREFIX + NEW + 8)
+    pos3, _ = vision_grid_positions(PREFIX)
+    prompt = synthetic_prompt(PREFIX, seed=1234 + rank)
+    # prefill: one forced step per prefix token (not timed)
+    eng.load_script(prompt, pos3)
+    eng.launch(PREFIX)
+    torch.cuda.synchronize(dev)
+    eng.check_error()
+    start_state = eng.snapshot()
+    first = eng.out_tokens[PREFIX - 1].item()
+    graph_steps = 32
+    eng.graph(graph_steps)
+
+    def one_request():
+        eng.restore(start_state)
+        eng.run(NEW, graph_steps)  # 256 decode steps = 8 replays of a 32-launch graph
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        one_request()
+    torch.cuda.synchronize(dev)
+    eng.check_error()
+
+    # ---- timed (device): K requests of 256 tokens
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        one_request()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    eng.check_error()
+    toks = eng.out_tokens[PREFIX:PREFIX + NEW].cpu()
+
+    # ---- timed (e2e): same requests through the host-buffer public call
+    start_host = torch.tensor([first, PREFIX, *[int(x) + 1 for x in pos3[:, -1]]], dtype=torch.int64).pin_memory()
+    out_host = torch.empty(NEW, dtype=torch.int64).pin_memory()
+    eng.decode_host(start_host, NEW, out_host, graph_steps)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        eng.decode_host(start_host, NEW, out_host, graph_steps)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_wall = time.perf_counter() - t0
+    e2e_ms = max(f0.elapsed_time(f1), 1000 * e2e_wall)
+    barrier()
+    e2e_ok = bool(torch.equal(out_host, toks))
+
+    # ---- max over ranks
+    vals = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(vals[0]), float(vals[1])
+
+    tokens = args.steps * NEW * world
+    value = tokens / (ms / 1000.0)
+    e2e_value = args.steps * NEW * world / (e2e_ms / 1000.0)
+    # roofline: algorithmic bytes of the 256 launches of one request (ctx 1024..1279)
+    bytes_req = sum(eng.algorithmic_bytes(PREFIX + i) for i in range(NEW))
+    per_launch_s = ms / 1000.0 / (args.steps * NEW)
+    achieved = bytes_req / NEW / per_launch_s / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+        "config": workload_config(world),
+        "step_us_per_token": 1000.0 * ms / (args.steps * NEW),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "decode_program_kernel (one launch per token)",
+                     "algorithmic_bytes_per_launch": bytes_req / NEW},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 8 * NEW,
+                "tokens_match_device_run": e2e_ok},
+        "gpu_launches": args.steps * NEW,
+        "clocks": clocks,
+    }
+    if args.layers != QWEN3VL_2B.num_layers:
+        line["config"]["workload"] = f"profiling case ({args.layers} layers), not the headline workload"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.layers == QWEN3VL_2B.num_layers:
+        tps, n, el = cpu_oracle_decode(st, seconds=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{n} decode tokens ({el:.1f} s) at cache slot {PREFIX}+ over a synthetic "
+                                          f"KV prefix, numpy fp32 oracle port, all host threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layers", type=int, default=28,
+                    help="profiling case only: a smaller model (the headline is 28 layers)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/* C ABI of the B200 decode engine for the Qwen3-VL-2B text decoder.
+ *
+ * Every entry point takes raw device pointers (fp16 data unless stated),
+ * plain integer sizes and a CUDA stream; none allocates memory, none
+ * synchronises the stream, and all are safe to capture in a CUDA graph.
+ * Return value: AICAS_OK (0) or an AICAS_ERR_* code for errors detected on the
+ * host (bad argument, shape, alignment, failed launch).  Errors detected on the
+ * device during a launch (bounded waits that gave up, out-of-range token or
+ * cache position) are written to the `error` word at the start of the scratch
+ * block (see AicasScratch in aicas_phase_program.h); read it after the stream
+ * synchronises.  After a device error, zero the scratch block again before the
+ * next launch.
+ *
+ * Scratch: kernels that need workspace (grid barrier, split-KV partials, the
+ * cross-CTA argmax) take a `scratch` pointer to aicas_scratch_bytes() bytes of
+ * device memory that the caller zero-fills ONCE; every launch leaves it ready
+ * for the next.  Launches that share a scratch block must be ordered on one
+ * stream (never concurrent).
+ *
+ * Each function names the reference interface it replaces (paths and lines
+ * are within the reference checkout, wangxiyu191/AICASGC-2026).
+ */
+#ifndef AICAS_DECODE_H
+#define AICAS_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "aicas_phase_program.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define AICAS_API __attribute__((visibility("default")))
+#else
+#define AICAS_API
+#endif
+
+#define AICAS_ABI_VERSION 1
+
+/* Host-side error codes (device error codes 10..15 are listed by
+ * aicas_error_string). */
+#define AICAS_OK 0
+#define AICAS_ERR_ARG 1
+#define AICAS_ERR_SHAPE 2
+#define AICAS_ERR_ALIGN 3
+#define AICAS_ERR_CUDA 4
+
+typedef struct CUstream_st* aicas_stream_t; /* == cudaStream_t */
+
+AICAS_API int aicas_abi_version(void);
+AICAS_API const char* aicas_error_string(int code);
+/* Bytes of the scratch block (sizeof(AicasScratch)). */
+AICAS_API size_t aicas_scratch_bytes(void);
+/* Struct sizes/offsets for binding checks; returns the number of values. */
+AICAS_API int aicas_layout_signature(int64_t* out, int n);
+/* CTAs of one persistent launch on `device` (= its SM count, <= 256), or a
+ * negative error code. */
+AICAS_API int aicas_num_ctas(int device);
+/* 1 (default): launch the persistent kernel as a cooperative launch, which
+ * fails instead of running when the grid cannot be co-resident. */
+AICAS_API int aicas_set_cooperative_launch(int enable);
+/* Host-side check of a phase list before it is copied to the device. */
+AICAS_API int aicas_validate_phases(const AicasPhase* phases, int n);
+
+/* y[n] = W[n,k] x[k] (+ bias[n]); fp32 accumulation, fp16 output.
+ * k % 8 == 0, k <= 8192, x/W 16-byte aligned.
+ * Replaces `nosplit_matvec_half` (cuda_decode_gemv_ops/matvec.py:274-321;
+ * kernels cuda_extensions/decode_gemv_kernel_matvec.cuh:209-343). */
+AICAS_API int aicas_gemv_f16(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t k,
+                             void* scratch, aicas_stream_t stream);
+
+/* y = W_qkv * RMSNorm(x) (HF rounding: norm in fp32, rounded to fp16, times
+ * the fp16 weight, rounded).  Replaces `fused_rmsnorm_qkv_half`
+ * (cuda_decode_gemv_ops/fused.py:71-105; kernel
+ * cuda_extensions/decode_gemv_kernel_fused.cuh:99-185). */
+AICAS_API int aicas_rmsnorm_qkv_f16(const void* x, const void* norm_w, const void* w, const void* bias, void* y,
+                                    int64_t n, int64_t k, float eps, void* scratch, aicas_stream_t stream);
+
+/* h = residual + attn_out; act = SiLU(W_gate RMSNorm(h)) * (W_up RMSNorm(h));
+ * out = h + W_down act (+ bias).  act_out [inter] receives the activation
+ * (the reference's `hidden_out`).  gate_up_w is [2*inter, hidden] with the
+ * gate rows first.  One persistent launch, two phases, one grid barrier.
+ * Replaces `fused_post_attn_mlp_softsync_half`
+ * (cuda_decode_gemv_ops/fused.py:261-337; kernel
+ * cuda_extensions/decode_gemv_kernel_fused.cuh:850-1076). */
+AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out, const void* norm_w,
+                                      const void* gate_up_w, const void* down_w, const void* bias, void* act_out,
+                                      void* out, int64_t hidden, int64_t inter, float eps, void* scratch,
+                                      aicas_stream_t stream);
+
+/* Decode attention for one query token: out[q_heads,128] =
+ * softmax(q K^T * scale) V over cache slots [0, *cache_position] (int64 on
+ * the device).  K/V: [kv_heads, max_len, 128] (HF StaticLayer.keys/values of
+ * batch 1); q_heads == 2 * kv_heads.  Split-KV over all SMs with a
+ * deterministic log-sum-exp merge.  Replaces
+ * `decode_attn_v4_cta_qhead_splitkv_fused` (cuda_decode_attention.py:489-558;
+ * kernel cuda_extensions/decode_attention_v4_kernel.cu:647-900). */
+AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,
+                                            const void* cache_position, float scale, void* out, int64_t q_heads,
+                                            int64_t kv_heads, int64_t max_len, void* scratch,
+                                            aicas_stream_t stream);
+
+/* Per-head RMSNorm + rotary embedding of q and k with the given cos/sin
+ * [128], k and v written to cache slot *cache_position, rotated q to q_out.
+ * q [q_heads,128], k/v [kv_heads,128], q_heads == 2 * kv_heads.  Replaces
+ * `fused_q_rope_kv_cache_update` (cuda_decode_small_ops.py:136-225; kernel
+ * cuda_extensions/decode_small_ops_kernel.cu:115-186). */
+AICAS_API int aicas_qk_norm_mrope_kvwrite_f16(const void* q, const void* k, const void* v, const void* q_norm_w,
+                                              const void* k_norm_w, const void* cos, const void* sin, void* q_out,
+                                              void* k_cache, void* v_cache, const void* cache_position, float eps,
+                                              int64_t q_heads, int64_t kv_heads, int64_t max_len,
+                                              aicas_stream_t stream);
+
+/* logits[vocab] = W x' where x' = RMSNorm(x) when norm_w is not null;
+ * *token_out (int64) = first index of the maximum fp16 logit.  logits may
+ * be null.  Replaces the tied lm_head GEMV `FastLmHead.forward`
+ * (evaluation_wrapper.py:1227-1240) plus `torch.argmax`
+ * (evaluation_wrapper.py:952). */
+AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const void* w, void* logits,
+                                       void* token_out, int64_t vocab, int64_t k, float eps, void* scratch,
+                                       aicas_stream_t stream);
+
+/* One whole decode step (all layers + final norm + lm_head + argmax) as one
+ * persistent launch running the phase list `device_phases` (device memory,
+ * built and validated on the host).  Reads its inputs from `state` and
+ * advances it (device-side greedy loop).  Replaces the graph-captured step
+ * `DecodeCudaGraphRunner._run_step` (evaluation_wrapper.py:941-952), i.e. HF's
+ * layer loop over `OptimizedDecoderLayer.forward` (optimized_layer.py:108-469). */
+AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
+                                       void* scratch, aicas_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AICAS_DECODE_H */

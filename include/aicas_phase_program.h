@@ -1,0 +1,112 @@
+// Layouts shared by the host-side program builder and the persistent
+// decode-program kernel.  Plain C structs: they are also mirrored by ctypes in
+// `aicasgc-2026_b200/_native.py` (field order and sizes must match; `aicas_layout_signature`
+// exports the sizes so the Python side can check them at load time).
+//
+// A decode step is a list of PHASES executed by one persistent launch of
+// `decode_program_kernel` (one CTA per SM).  Every phase is a memory-bound
+// sweep over one weight matrix (or over the KV cache); phases are separated by
+// bounded software grid barriers.  One warp per CTA streams the phase's tiles
+// from HBM into a shared-memory ring with bulk async copies, independently of
+// the grid barriers, so weight streaming never waits on a barrier.
+#pragma once
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum AicasPhaseKind {
+  AICAS_PH_GEMV = 1,     // out = [resid +] W x [+ bias]          (QKV, o_proj, down, generic)
+  AICAS_PH_GATEUP = 2,   // out = silu(Wg x) * (Wu x)            (fused gate_up + SiLU*up)
+  AICAS_PH_ATTN = 3,     // q/k norm + MRoPE + KV write + split-KV GQA attention + LSE merge
+  AICAS_PH_LMHEAD = 4,   // logits = E x, argmax, advance the step state
+};
+
+// Flags of a phase.
+enum AicasPhaseFlags {
+  AICAS_F_NORM = 1 << 0,         // x := RMSNorm(x) * norm_w before the sweep (HF rounding points)
+  AICAS_F_X_EMBED = 1 << 1,      // x := embedding row of the step token (x points at the table)
+  AICAS_F_RESID = 1 << 2,        // out := r16(resid + r16(acc))
+  AICAS_F_RESID_EMBED = 1 << 3,  // resid := embedding row of the step token
+  AICAS_F_BIAS = 1 << 4,         // acc += bias (fp32, before rounding)
+  AICAS_F_X_ADD = 1 << 5,        // x := r16(x + x2)   (before the optional norm)
+  AICAS_F_RESID_ADD = 1 << 6,    // resid := r16(resid + resid2)
+  AICAS_F_Q_READY = 1 << 7,      // attention: q is final (no norm/rope); no KV write
+  AICAS_F_STORE_X = 1 << 8,      // GEMV/GATEUP: CTA 0 stores the prologue vector to x_out
+};
+
+// One phase.  Pointers are device pointers (fp16 data is `__half`, passed as
+// void* so this header stays free of CUDA types).
+typedef struct AicasPhase {
+  int32_t kind;
+  int32_t flags;
+  int32_t n;        // GEMV/LMHEAD: output rows; GATEUP: intermediate size (rows of gate)
+  int32_t k;        // reduction length (multiple of 8, <= AICAS_MAX_K)
+  int32_t rot;      // CTA rotation of the row-group assignment (load balance across phases)
+  int32_t kv_heads; // attention
+  int32_t q_heads;  // attention
+  int32_t max_len;  // attention: cache slots per head
+  int32_t embed_rows; // F_X_EMBED / F_RESID_EMBED: rows of the embedding table
+  int32_t pad1;
+  const void* w;      // weight [n, k] (GATEUP: [2n, k], gate rows first)
+  const void* norm_w; // RMSNorm weight [k] (attention: q_norm weight [128])
+  const void* norm_w2;// attention: k_norm weight [128]
+  const void* x;      // input vector [k] (attention: the fused qkv vector or final q)
+  const void* x2;     // second input (F_X_ADD)
+  const void* resid;  // residual [n]
+  const void* resid2; // second residual (F_RESID_ADD)
+  const void* bias;   // [n]
+  void* out;          // output [n] fp16 (attention: [q_heads*128])
+  void* x_out;        // F_STORE_X target [k]
+  void* k_cache;      // attention: [kv_heads, max_len, 128] fp16
+  void* v_cache;
+  const void* pos_ptr;// attention: int64 cache position (null: the step state's)
+  void* idx_out;      // LMHEAD: int64 argmax output (may be null)
+  float eps;
+  float scale;        // attention softmax scale
+} AicasPhase;
+
+// Decode-step state in device memory, read by every launch and advanced by
+// the LM-head phase (device-side greedy loop: no host write between steps).
+typedef struct AicasStepState {
+  int64_t token;        // input token of the current step
+  int64_t cache_pos;    // KV slot written by this step; attention covers [0, cache_pos]
+  int64_t rope[3];      // MRoPE positions (t, h, w) of this step
+  int64_t step;         // steps executed so far
+  int64_t script_len;   // steps whose inputs come from `script` (teacher forcing / prefill)
+  const int64_t* script;// [script_len][5] = token, cache_pos, t, h, w
+  int64_t* out_tokens;  // [max_steps] argmax of every step
+  int64_t max_steps;
+  void* logits;         // optional fp16 [logits_ring][vocab]
+  int64_t logits_ring;
+  float inv_freq[64];   // rotary inverse frequencies (host computes them like HF)
+  int32_t mrope_section[3];
+  int32_t pad0;
+} AicasStepState;
+
+#define AICAS_MAX_CTAS 256
+#define AICAS_MAX_SPLITS 256
+#define AICAS_MAX_KV_HEADS 8
+#define AICAS_HEAD_DIM 128
+#define AICAS_MAX_K 8192
+
+// Scratch memory of the persistent kernel (caller allocates, zero-fills once;
+// every launch leaves it ready for the next one).
+typedef struct AicasScratch {
+  uint32_t bar_count;   // grid barrier arrivals
+  uint32_t bar_gen;     // grid barrier generation
+  int32_t error;        // first error code raised on the device (0 = none)
+  int32_t abort;        // set with `error`; every wait gives up when it is set
+  uint32_t head_done[AICAS_MAX_KV_HEADS];  // split-KV merge arrivals per KV head
+  uint32_t argmax_done;
+  uint32_t pad[3];
+  float am_val[AICAS_MAX_CTAS];
+  int32_t am_idx[AICAS_MAX_CTAS];
+  // split-KV partials: [kv head][split][group 2][M, L, acc[128]]
+  float part[AICAS_MAX_KV_HEADS][AICAS_MAX_SPLITS][2][AICAS_HEAD_DIM + 2];
+} AicasScratch;
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,111 @@
+"""GPU parity of the whole decode step (the persistent phase-program kernel).
+
+* 2-layer model vs the reference's own golden outputs (fp32 HF through the
+  reference's `GreedyDecodeEngine`): identical greedy tokens, logits within
+  5e-2 (fp16 engine vs fp32 reference).
+* 2-layer and full 28-layer models vs the fp16 oracle, teacher-forced on the
+  engine's own trajectory: logits within tolerance at every step, and every
+  token equal to the oracle's argmax unless the oracle's top-2 gap is below
+  the tolerance (a genuine near-tie that fp32 summation order may break
+  either way).
+
+Tolerances.  2 layers: max |d logit| <= 2e-2.  28 layers: max |d| <= 3e-2 and
+mean |d| <= 5e-3 per step.  The 28-layer bound is set by the fp16 model's own
+noise floor: the fp16 oracle run with float64 instead of float32 matmul
+accumulation (same fp16 rounding points) differs from itself by up to 0.018
+max / 0.0028 mean at 28 layers (300-token vision prefix, 8 steps), because
+single-ulp fp16 rounding flips propagate through 28 residual layers.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from engine import Qwen3VLDecodeEngine, hf_inv_freq
+from oracle.qwen3vl_oracle import Qwen3VLOracle
+from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state, vision_grid_positions
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+LOGIT_ATOL = 2e-2
+LOGIT_ATOL_28L = 3e-2
+LOGIT_MEAN_28L = 5e-3
+
+
+def _teacher_forced_check(eng, oracle, prompt, n_new, pos3=None, rope_delta=0, atol=LOGIT_ATOL, mean_tol=None):
+    toks = eng.generate(prompt, n_new, pos3=pos3).numpy()
+    P = len(prompt)
+    gl = np.stack([eng.step_logits(P - 1 + i).float().cpu().numpy() for i in range(n_new)])
+    otoks, ol = oracle.greedy(prompt, n_new, pos3_prompt=pos3, rope_delta=rope_delta, forced=toks)
+    diff = np.abs(gl - ol).max(axis=-1)
+    assert diff.max() <= atol, f"max logit diff per step {diff}"
+    if mean_tol is not None:
+        mean = np.abs(gl - ol).mean(axis=-1)
+        assert mean.max() <= mean_tol, f"mean logit diff per step {mean}"
+    srt = np.sort(ol, axis=-1)
+    gap = srt[:, -1] - srt[:, -2]
+    for i in range(n_new):
+        if toks[i] != otoks[i]:
+            assert gap[i] <= atol, f"step {i}: token {toks[i]} vs oracle {otoks[i]} (gap {gap[i]})"
+    # the engine's token is the first max of its own fp16 logits
+    np.testing.assert_array_equal(toks, np.argmax(gl, axis=-1))
+    return toks, gl, diff
+
+
+@pytest.fixture(scope="module")
+def state2():
+    return synthetic_state(QWEN3VL_2B.with_layers(2), seed=0)
+
+
+def test_engine_matches_reference_golden_text(cuda_device, state2):
+    g = np.load(GOLDEN / "greedy_text.npz")
+    n = len(g["tokens"])
+    eng = Qwen3VLDecodeEngine(state2, QWEN3VL_2B.with_layers(2), max_cache_len=128, logits_ring=n,
+                              max_steps=128)
+    toks = eng.generate(g["prompt"], n).numpy()
+    np.testing.assert_array_equal(toks, g["tokens"])
+    P = len(g["prompt"])
+    gl = np.stack([eng.step_logits(P - 1 + i).float().cpu().numpy() for i in range(n)])
+    assert np.abs(gl[:, g["sample_idx"]] - g["sample_logits"]).max() <= 5e-2
+
+
+def test_engine_matches_reference_golden_vision_grid(cuda_device, state2):
+    g = np.load(GOLDEN / "vision_grid.npz")
+    n = len(g["tokens"])
+    eng = Qwen3VLDecodeEngine(state2, QWEN3VL_2B.with_layers(2), max_cache_len=320, logits_ring=n,
+                              max_steps=512)
+    toks = eng.generate(g["prompt"], n, pos3=g["pos3"]).numpy()
+    np.testing.assert_array_equal(toks, g["tokens"])
+
+
+def test_engine_two_layers_teacher_forced(cuda_device, state2):
+    s16 = {k: v.half() for k, v in state2.items()}
+    prompt = synthetic_prompt(200, seed=77).numpy()
+    eng = Qwen3VLDecodeEngine(s16, QWEN3VL_2B.with_layers(2), max_cache_len=512, logits_ring=64, max_steps=512)
+    o = Qwen3VLOracle(s16, 2, mode="fp16", max_cache_len=512, inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
+    _teacher_forced_check(eng, o, prompt, 64)
+
+
+def test_engine_cuda_graph_replay_is_deterministic(cuda_device, state2):
+    prompt = synthetic_prompt(40, seed=5).numpy()
+    eng = Qwen3VLDecodeEngine(state2, QWEN3VL_2B.with_layers(2), max_cache_len=256, max_steps=256)
+    a = eng.generate(prompt, 70, graph_steps=16)
+    b = eng.generate(prompt, 70, graph_steps=1)
+    c = eng.generate(prompt, 70, graph_steps=32)
+    assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_engine_full_model_vision_prefix(cuda_device):
+    """BASELINE config 4 shapes: 28 layers, 1024-token prefix with a 16x16
+    vision grid (3-axis MRoPE), then greedy decode (64 steps here)."""
+    st = synthetic_state(QWEN3VL_2B, seed=0, dtype=torch.float16)
+    P, n = 1024, 64
+    pos3, rope_delta = vision_grid_positions(P)
+    prompt = synthetic_prompt(P, seed=1234).numpy()
+    eng = Qwen3VLDecodeEngine(st, QWEN3VL_2B, max_cache_len=P + n, logits_ring=n, max_steps=P + n)
+    o = Qwen3VLOracle(st, 28, mode="fp16", max_cache_len=P + n, inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
+    del st
+    toks, gl, diff = _teacher_forced_check(eng, o, prompt, n, pos3=pos3.numpy(), rope_delta=rope_delta,
+                                           atol=LOGIT_ATOL_28L, mean_tol=LOGIT_MEAN_28L)
+    print("full-model max logit diff", float(diff.max()))
