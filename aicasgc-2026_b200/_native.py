@@ -89,6 +89,7 @@ SIGNATURES = {
     "aicas_qk_norm_mrope_kvwrite_f16": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _P]),
     "aicas_lm_head_argmax_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_decode_program_f16": (_I, [_P, _I, _P, _P, _P]),
+    "aicas_decode_program_trace_f16": (_I, [_P, _I, _P, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

@@ -131,34 +131,48 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// Software grid barrier over `nct` co-resident CTAs, called by ONE thread per
-// CTA.  Sense by generation counter; the last arriver resets the count and
-// publishes the next generation.  Bounded: gives up after kWaitLimitNs.
-__device__ __forceinline__ bool grid_barrier(AicasScratch* s, uint32_t nct, uint32_t& gen) {
+// Software grid barrier over `nct` co-resident CTAs, split into arrive and
+// wait so a CTA can do independent work in between.  One thread per CTA
+// calls both.  The 64-bit arrival counter only grows (it never wraps and is
+// never reset), so barrier k of a launch completes when the counter reaches
+// base + (k + 1) * nct, where base = counter at launch start rounded down to
+// a multiple of nct (a CTA that reads the counter late can only see fewer than
+// nct extra arrivals: barrier 0 cannot complete without it).
+__device__ __forceinline__ void red_release_add_u64(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void grid_arrive(AicasScratch* s) {
   __threadfence();
-  const uint32_t g = gen;
-  const uint32_t prev = atomicAdd(&s->bar_count, 1u);
-  if (prev == nct - 1) {
-    atomicExch(&s->bar_count, 0u);
-    __threadfence();
-    st_release_u32(&s->bar_gen, g + 1);
-  } else {
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t it = 0;
-    while (ld_acquire_u32(&s->bar_gen) == g) {
-      if ((++it & 15u) == 0) {
-        if (ld_volatile_int(&s->abort)) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          raise_error(s, kErrBarrierTimeout);
-          return false;
-        }
+  red_release_add_u64(&s->bar_count, 1ull);
+}
+
+// Bounded wait until `target` arrivals; false on timeout or abort.
+__device__ __forceinline__ bool grid_wait(AicasScratch* s, uint64_t target) {
+  if ((int64_t)(ld_acquire_u64(&s->bar_count) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if ((int64_t)(ld_acquire_u64(&s->bar_count) - target) >= 0) return true;
+    if ((it & 31u) == 0) {
+      if (ld_volatile_int(&s->abort)) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrBarrierTimeout);
+        return false;
       }
-      __nanosleep(20);
     }
   }
-  gen = g + 1;
-  __threadfence();
-  return true;
 }
 
 // fp16 helpers -------------------------------------------------------------

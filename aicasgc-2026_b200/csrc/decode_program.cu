@@ -1,21 +1,22 @@
 // Persistent decode-program kernel for B200 (sm_100a).
 //
-// One launch runs a list of phases (phase_program.h) with one CTA per SM:
+// One launch runs a list of phases (aicas_phase_program.h) with one CTA per SM:
 //   warp 0      producer: streams every tile this CTA will consume, phase after
 //               phase, from HBM into a 12-stage shared-memory ring with bulk
 //               async copies (cp.async.bulk + mbarrier complete_tx).  It never
 //               waits on a grid barrier, so HBM keeps streaming the next
 //               phase's weights while the consumers wait for activations.
 //   warps 1..8  consumers: per phase, wait on the grid barrier, build the input
-//               vector (RMSNorm prologue with HF's fp16 rounding points), then
-//               reduce each tile against it with exact fp16 products and fp32
-//               accumulation; per-group epilogues apply rounding, residuals,
-//               SiLU*up, or the running argmax.
+//               vector slice they need (RMSNorm prologue with HF's fp16 rounding
+//               points, computed by every warp on its own: no block sync), then
+//               reduce each tile row against it with exact fp16 products and
+//               fp32 accumulation.
 //
-// GEMV tile: 4 weight rows x 2048 columns (16 KB).  Consumer warp w owns
-// columns [256w, 256w+256) of every row, lane l the 8 columns at 256w + 8l, so
-// each lane keeps its slice of the input vector in registers for the whole
-// phase and every weight byte is read from shared memory exactly once.
+// GEMV tile: 8 weight rows x 1024 columns (16 KB).  Consumer warp w owns row w
+// of every tile; lane l the columns j*256 + 8l (j = 0..3) of each 1024-column
+// chunk, so a lane keeps its slice of the input vector in registers for the
+// whole phase, every weight byte is read from shared memory exactly once
+// (conflict-free 512-byte warp accesses) and a row needs one warp reduction.
 //
 // Attention tile: K and V rows of 32 cache positions of one KV head (16 KB).
 // Work units (KV head, 32-position chunk) are split into contiguous ranges per
@@ -23,18 +24,24 @@
 // last CTA to finish a head (atomic arrival count) merges its partials in a
 // fixed order, so the result does not depend on arrival order.
 //
+// Grid barrier: split arrive / wait on a monotonic 64-bit counter.  Between
+// the two, every consumer prefetches what the next phase needs and no phase
+// of the program depends on: its norm weights (to shared memory) and its
+// residual rows (to registers).
+//
 // Reference behaviour this replaces (file:line in the reference checkout):
 //   fused RMSNorm+QKV      cuda_extensions/decode_gemv_kernel_fused.cuh:99-185
 //   o_proj GEMV            cuda_extensions/decode_gemv_kernel_matvec.cuh:276-343
 //   post-attn MLP          cuda_extensions/decode_gemv_kernel_fused.cuh:850-1076
 //   split-KV attention     cuda_extensions/decode_attention_v4_kernel.cu:647-900
+//   q/k norm+rope+KV write cuda_extensions/decode_small_ops_kernel.cu:115-186
 //   lm_head GEMV           cuda_extensions/decode_gemv_kernel_matvec.cuh:209-274
 //   argmax                 evaluation_wrapper.py:952 (torch.argmax, first max wins)
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 #include <string.h>
-#include <stddef.h>
 
 #include "aicas_device.cuh"
 #include "aicas_phase_program.h"
@@ -44,39 +51,35 @@ namespace aicas {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kRows = 4;            // weight rows per GEMV tile
-constexpr int kChunk = 2048;        // columns per GEMV tile
+constexpr int kRows = kConsumerWarps;  // weight rows per GEMV tile: one per consumer warp
+constexpr int kChunk = 1024;           // columns per GEMV tile
 constexpr int kRowBytes = kChunk * 2;
 constexpr int kStageBytes = kRows * kRowBytes;  // 16 KB
 constexpr int kStages = 12;
-constexpr int kAttnChunk = 32;      // cache positions per attention tile
+constexpr int kAttnChunk = 32;  // cache positions per attention tile
 constexpr int kHD = AICAS_HEAD_DIM;
-constexpr int kMaxChunks = AICAS_MAX_K / kChunk;
+constexpr int kMaxChunks = AICAS_MAX_K / kChunk;  // 6
+constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
+constexpr int kResidPrefetch = 4;                 // residual rows kept in registers per warp
 
 static_assert(kAttnChunk * kHD * 2 * 2 == kStageBytes, "attention tile must fill one stage");
+static_assert(AICAS_MAX_K % kChunk == 0, "max K must be whole chunks");
 
 struct AttnSmem {
-  float q[2][kHD];        // rotated queries of the head pair
-  float cs[kHD], sn[kHD]; // cos/sin (fp16 values)
-  float kf[kHD], vf[kHD]; // fresh k (normed+rotated) / v of the current position
-  float tmp[2][kHD];
+  float q[2][kHD];         // rotated queries of the head pair
+  float kf[kHD], vf[kHD];  // this step's k (normed+rotated) / v of the current KV head
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
-  float red[kConsumerWarps];
   int last;
 };
 
 struct __align__(128) Smem {
   uint8_t ring[kStages][kStageBytes];
-  union {
-    __half xbuf[AICAS_MAX_K];
-    AttnSmem at;
-  } u;
-  float red[2][kConsumerWarps][8];
-  float nred[kConsumerWarps];
-  float best_v[kRows];
-  int best_i[kRows];
+  __half nw[AICAS_MAX_K];  // norm weights of the running phase (prefetched before its barrier)
+  AttnSmem at;
+  float best_v[kConsumerWarps];
+  int best_i[kConsumerWarps];
   uint64_t full[kStages];
   uint64_t empty[kStages];
 };
@@ -85,8 +88,9 @@ struct ProgramArgs {
   const AicasPhase* phases;  // device array, or null: use `inl`
   int n_phases;
   int pad;
-  AicasStepState* state;     // may be null (op-level calls)
+  AicasStepState* state;  // may be null (op-level calls)
   AicasScratch* scratch;
+  int64_t* trace;  // optional [grid][n_phases][2] globaltimer stamps
   AicasPhase inl[4];
 };
 
@@ -126,9 +130,10 @@ __device__ __forceinline__ int phase_valid_len(const AicasPhase& d, const StepIn
   return (int)pos + 1;
 }
 
+__device__ __forceinline__ int n_chunks(const AicasPhase& d) { return (d.k + kChunk - 1) / kChunk; }
+
 __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
-  const int C = (d.k + kChunk - 1) / kChunk;
-  return d.kind == AICAS_PH_GATEUP ? 2 * C : C;
+  return d.kind == AICAS_PH_GATEUP ? 2 * n_chunks(d) : n_chunks(d);
 }
 
 // ---------------------------------------------------------------------------
@@ -173,7 +178,7 @@ __device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
       }
     } else if (d.kind == AICAS_PH_GEMV || d.kind == AICAS_PH_GATEUP || d.kind == AICAS_PH_LMHEAD) {
       const int G = (d.n + kRows - 1) / kRows;
-      const int C = (d.k + kChunk - 1) / kChunk;
+      const int C = n_chunks(d);
       const int T = tiles_per_group(d);
       const Range rg = split_range(G, nct, cta, d.rot);
       const __half* W = reinterpret_cast<const __half*>(d.w);
@@ -218,46 +223,29 @@ struct Consumer {
   Smem& sm;
   const StepIn& in;
   AicasScratch* s;
-  int tid;   // 0..255
-  int w;     // consumer warp 0..7
+  int tid;  // 0..255
+  int w;    // consumer warp 0..7
   int lane;
   int nct, cta;
   Ring r;
-  uint32_t gen;
-  bool ok = true;
+  uint64_t bar_base;
+  uint32_t bar_k = 0;
+  // residual rows of this warp's first groups of the coming phase
+  float rv_pre[kResidPrefetch];
 
   // Waits never end the consumer loop early: after a failed (timed-out or
   // aborted) wait the CTA keeps walking the same program without waiting, so
   // every named barrier is still reached by all 256 consumer threads and the
   // launch ends promptly with the error recorded in the scratch block.
-  __device__ void wait_full(int st) {
-    if (!mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout)) ok = false;
-  }
+  __device__ void wait_full(int st) { mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout); }
   __device__ void release(int st) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[st]);
     ++r.it;
   }
 
-  __device__ bool barrier() {
-    consumer_sync(kConsumerThreads);
-    if (tid == 0) sm.nred[0] = grid_barrier(s, nct, gen) ? 1.f : 0.f;
-    consumer_sync(kConsumerThreads);
-    const bool good = sm.nred[0] != 0.f;
-    consumer_sync(kConsumerThreads);
-    return ok = ok && good;
-  }
-
-  // Block-wide sum over the 256 consumer threads.
-  __device__ float block_sum(float v) {
-    v = warp_sum(v);
-    if (lane == 0) sm.nred[w] = v;
-    consumer_sync(kConsumerThreads);
-    float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < kConsumerWarps; ++i) t += sm.nred[i];
-    consumer_sync(kConsumerThreads);
-    return t;
+  __device__ void stamp(int ph, int which) {
+    if (a.trace && tid == 0) a.trace[((size_t)cta * a.n_phases + ph) * 2 + which] = (int64_t)globaltimer_ns();
   }
 
   // Token id of the step, checked against the embedding table (an
@@ -268,61 +256,6 @@ struct Consumer {
     return 0;
   }
 
-  // Builds the phase input vector into sm.u.xbuf (fp16 values):
-  //   v = x (or the token's embedding row) [+ x2, rounded]; optionally
-  //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
-  __device__ void build_x(const AicasPhase& d) {
-    const int k = d.k;
-    const __half* x = reinterpret_cast<const __half*>(d.x);
-    if (d.flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
-    const __half* x2 = reinterpret_cast<const __half*>(d.x2);
-    float ss = 0.f;
-    const int nvec = k / 8;
-    for (int v = tid; v < nvec; v += kConsumerThreads) {
-      uint4 raw = ldcg_u4(x + v * 8);
-      __half2* hp = reinterpret_cast<__half2*>(&raw);
-      if (d.flags & AICAS_F_X_ADD) {
-        uint4 raw2 = ldcg_u4(x2 + v * 8);
-        const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 fa = __half22float2(hp[j]), fb = __half22float2(hq[j]);
-          hp[j] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __half22float2(hp[j]);
-        ss += f.x * f.x + f.y * f.y;
-      }
-      *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]) = raw;
-    }
-    if (d.flags & AICAS_F_NORM) {
-      const float tot = block_sum(ss);
-      const float inv = rsqrtf(tot / (float)k + d.eps);
-      const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
-      for (int v = tid; v < nvec; v += kConsumerThreads) {
-        uint4 raw = *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]);
-        uint4 wr = __ldg(reinterpret_cast<const uint4*>(nw + v * 8));
-        __half2* hp = reinterpret_cast<__half2*>(&raw);
-        const __half2* wp = reinterpret_cast<const __half2*>(&wr);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = __half22float2(hp[j]);
-          float2 g = __half22float2(wp[j]);
-          hp[j] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
-        }
-        *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]) = raw;
-      }
-    }
-    consumer_sync(kConsumerThreads);
-    if ((d.flags & AICAS_F_STORE_X) && cta == 0 && d.x_out) {
-      __half* xo = reinterpret_cast<__half*>(d.x_out);
-      for (int v = tid; v < nvec; v += kConsumerThreads)
-        *reinterpret_cast<uint4*>(xo + v * 8) = *reinterpret_cast<uint4*>(&sm.u.xbuf[v * 8]);
-    }
-  }
-
   __device__ float resid_value(const AicasPhase& d, int row) {
     const __half* rp = reinterpret_cast<const __half*>(d.resid);
     if (d.flags & AICAS_F_RESID_EMBED) rp += (size_t)checked_token(d) * d.n;
@@ -331,71 +264,116 @@ struct Consumer {
     return rv;
   }
 
-  // Reduce-scatter of NV per-lane partials: afterwards lane l holds the warp
-  // total of value index ((l>>4)&1)*NV/2 + ... (see idx below).
-  template <int NV>
-  __device__ __forceinline__ float reduce_scatter(float (&v)[NV], int& idx) {
-    // NV in {4, 8}
-    float a[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) a[i] = v[i];
-    int half = NV / 2, base = 0;
-    // step xor 16
-    {
-      const bool hi = lane & 16;
-#pragma unroll
-      for (int i = 0; i < NV / 2; ++i) {
-        float send = hi ? a[i] : a[i + NV / 2];
-        float keep = hi ? a[i + NV / 2] : a[i];
-        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  // Work for phase `d` that depends on nothing the previous phase writes:
+  // norm weights -> shared memory, first residual rows -> registers.  Runs
+  // between this CTA's barrier arrival and its wait.
+  __device__ void prefetch(const AicasPhase& d) {
+    if (d.kind == AICAS_PH_ATTN) {
+      if (!(d.flags & AICAS_F_Q_READY) && tid < 2 * kHD / 8) {
+        const __half* src = reinterpret_cast<const __half*>(tid < kHD / 8 ? d.norm_w : d.norm_w2);
+        const int v = tid % (kHD / 8);
+        *reinterpret_cast<uint4*>(&sm.nw[(tid / (kHD / 8)) * kHD + v * 8]) =
+            __ldg(reinterpret_cast<const uint4*>(src) + v);
       }
-      base = hi ? NV / 2 : 0;
+      return;
     }
-    // step xor 8
-    {
-      const bool hi = lane & 8;
+    if (d.flags & AICAS_F_NORM) {
+      const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
+      for (int v = tid; v < d.k / 8; v += kConsumerThreads)
+        *reinterpret_cast<uint4*>(&sm.nw[v * 8]) = __ldg(reinterpret_cast<const uint4*>(nw) + v);
+    }
+    if ((d.flags & AICAS_F_RESID) && lane == 0) {
+      const Range rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
 #pragma unroll
-      for (int i = 0; i < NV / 4; ++i) {
-        float send = hi ? a[i] : a[i + NV / 4];
-        float keep = hi ? a[i + NV / 4] : a[i];
-        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      for (int i = 0; i < kResidPrefetch; ++i) {
+        const int row = (rg.start + i) * kRows + w;
+        rv_pre[i] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
       }
-      base += hi ? NV / 4 : 0;
     }
-    float t = a[0];
-    if (NV == 8) {
-      const bool hi = lane & 4;
-      float send = hi ? a[0] : a[1];
-      float keep = hi ? a[1] : a[0];
-      t = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-      base += hi ? 1 : 0;
-      t += __shfl_xor_sync(0xffffffffu, t, 2);
-      t += __shfl_xor_sync(0xffffffffu, t, 1);
-    } else {
-      t += __shfl_xor_sync(0xffffffffu, t, 4);
-      t += __shfl_xor_sync(0xffffffffu, t, 2);
-      t += __shfl_xor_sync(0xffffffffu, t, 1);
+  }
+
+  // This warp's slice of the phase input vector, in registers:
+  //   v = x (or the token's embedding row) [+ x2, rounded]; optionally
+  //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
+  // Every warp covers the whole vector across its lanes, so the sum of
+  // squares is a warp reduction and no block synchronisation is needed.
+  __device__ void build_x(const AicasPhase& d, uint4 (&xr)[kMaxChunks][kVec]) {
+    const int k = d.k, C = n_chunks(d);
+    const __half* x = reinterpret_cast<const __half*>(d.x);
+    if (d.flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
+    const __half* x2 = reinterpret_cast<const __half*>(d.x2);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int col = c * kChunk + j * 256 + lane * 8;
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (c < C && col < k) {
+          raw = ldcg_u4(x + col);
+          if (d.flags & AICAS_F_X_ADD) {
+            const uint4 raw2 = ldcg_u4(x2 + col);
+            __half2* hp = reinterpret_cast<__half2*>(&raw);
+            const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 fa = __half22float2(hp[e]), fb = __half22float2(hq[e]);
+              hp[e] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+            }
+          }
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(hp[e]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+        xr[c][j] = raw;
+      }
     }
-    (void)half;
-    idx = base;
-    return t;
+    if (d.flags & AICAS_F_NORM) {
+      const float inv = rsqrtf(warp_sum(ss) / (float)k + d.eps);
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int col = c * kChunk + j * 256 + lane * 8;
+          if (c < C && col < k) {
+            const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
+            __half2* hp = reinterpret_cast<__half2*>(&xr[c][j]);
+            const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(hp[e]);
+              const float2 g = __half22float2(wp[e]);
+              hp[e] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
+            }
+          }
+        }
+      }
+    }
+    if ((d.flags & AICAS_F_STORE_X) && cta == 0 && w == 0 && d.x_out) {
+      __half* xo = reinterpret_cast<__half*>(d.x_out);
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          const int col = c * kChunk + j * 256 + lane * 8;
+          if (c < C && col < k) *reinterpret_cast<uint4*>(xo + col) = xr[c][j];
+        }
+    }
   }
 
   // GEMV / GATEUP / LMHEAD phase.
   __device__ void run_matvec(const AicasPhase& d) {
-    build_x(d);
-    const int C = (d.k + kChunk - 1) / kChunk;
+    uint4 xr[kMaxChunks][kVec];
+    build_x(d, xr);
+    const int C = n_chunks(d);
     const int G = (d.n + kRows - 1) / kRows;
     const Range rg = split_range(G, nct, cta, d.rot);
-    const int col_in_chunk = 256 * w + 8 * lane;
-    uint4 xr[kMaxChunks];
-#pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      const int col = c * kChunk + col_in_chunk;
-      xr[c] = (c < C && col < d.k) ? *reinterpret_cast<const uint4*>(&sm.u.xbuf[col]) : make_uint4(0, 0, 0, 0);
-    }
     const bool gateup = d.kind == AICAS_PH_GATEUP;
     const bool lm = d.kind == AICAS_PH_LMHEAD;
+    const bool resid = d.flags & AICAS_F_RESID;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     __half* logits = nullptr;
@@ -403,11 +381,22 @@ struct Consumer {
       const int64_t ring = a.state->logits_ring > 0 ? a.state->logits_ring : 1;
       logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * d.n;
     }
-    int buf = 0;
-    for (int g = rg.start; g < rg.start + rg.count; ++g) {
-      float acc[8];
+    __half* out = reinterpret_cast<__half*>(d.out);
+    for (int gi = 0; gi < rg.count; ++gi) {
+      const int g = rg.start + gi;
+      const int row = g * kRows + w;
+      const bool vrow = row < d.n;  // warp-uniform
+      float rv = 0.f;
+      if (resid && lane == 0 && vrow) {
+        if (gi < kResidPrefetch) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+          for (int i = 0; i < kResidPrefetch; ++i)
+            if (i == gi) rv = rv_pre[i];
+        } else {
+          rv = resid_value(d, row);
+        }
+      }
+      float acc[2] = {0.f, 0.f};
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         if (part == 1 && !gateup) break;
@@ -416,75 +405,58 @@ struct Consumer {
           if (c < C) {
             const int st = r.stage();
             wait_full(st);
-            const int clen = min(kChunk, d.k - c * kChunk);
-            if (col_in_chunk < clen) {
-              const uint8_t* base = sm.ring[st] + col_in_chunk * 2;
+            if (vrow) {
+              const uint8_t* base = sm.ring[st] + w * kRowBytes + lane * 16;
 #pragma unroll
-              for (int i = 0; i < kRows; ++i) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(base + i * kRowBytes);
-                acc[part * 4 + i] = dot8_f16(wv, xr[c], acc[part * 4 + i]);
+              for (int j = 0; j < kVec; ++j) {
+                if (c * kChunk + j * 256 + lane * 8 < d.k) {
+                  const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
+                  acc[part] = dot8_f16(wv, xr[c][j], acc[part]);
+                }
               }
             }
             release(st);
           }
         }
       }
-      int idx;
-      if (gateup) {
-        float t = reduce_scatter<8>(acc, idx);
-        if ((lane & 3) == 0) sm.red[buf][w][idx] = t;
-      } else {
-        float a4[4] = {acc[0], acc[1], acc[2], acc[3]};
-        float t = reduce_scatter<4>(a4, idx);
-        if ((lane & 7) == 0) sm.red[buf][w][idx] = t;
-      }
-      consumer_sync(kConsumerThreads);
-      if (tid < kRows) {
-        const int row = g * kRows + tid;
-        if (row < d.n) {
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < kConsumerWarps; ++i) sum += sm.red[buf][i][tid];
-          __half* out = reinterpret_cast<__half*>(d.out);
-          if (gateup) {
-            float up = 0.f;
-#pragma unroll
-            for (int i = 0; i < kConsumerWarps; ++i) up += sm.red[buf][i][4 + tid];
-            const float gq = r16(sum), uq = r16(up);
-            const float sl = r16(gq / (1.0f + expf(-gq)));
-            out[row] = __float2half_rn(sl * uq);
-          } else {
-            if (d.flags & AICAS_F_BIAS) sum += __half2float(reinterpret_cast<const __half*>(d.bias)[row]);
-            float y = r16(sum);
-            if (d.flags & AICAS_F_RESID) y = r16(resid_value(d, row) + y);
-            if (lm) {
-              if (logits) logits[row] = __float2half_rn(y);
-              if (d.out) out[row] = __float2half_rn(y);
-              if (y > best_v) {  // rows ascend: strict > keeps the first max
-                best_v = y;
-                best_i = row;
-              }
-            } else {
-              out[row] = __float2half_rn(y);
+      acc[0] = warp_sum(acc[0]);
+      if (gateup) acc[1] = warp_sum(acc[1]);
+      if (lane == 0 && vrow) {
+        if (gateup) {
+          const float gq = r16(acc[0]), uq = r16(acc[1]);
+          const float sl = r16(gq / (1.0f + expf(-gq)));
+          out[row] = __float2half_rn(sl * uq);
+        } else {
+          float sum = acc[0];
+          if (d.flags & AICAS_F_BIAS) sum += __half2float(reinterpret_cast<const __half*>(d.bias)[row]);
+          float y = r16(sum);
+          if (resid) y = r16(rv + y);
+          if (lm) {
+            if (logits) logits[row] = __float2half_rn(y);
+            if (out) out[row] = __float2half_rn(y);
+            if (y > best_v) {  // this warp's rows ascend: strict > keeps the first max
+              best_v = y;
+              best_i = row;
             }
+          } else {
+            out[row] = __float2half_rn(y);
           }
         }
       }
-      buf ^= 1;
     }
     if (lm) finish_argmax(d, best_v, best_i);
   }
 
   __device__ void finish_argmax(const AicasPhase& d, float bv, int bi) {
-    if (tid < kRows) {
-      sm.best_v[tid] = bv;
-      sm.best_i[tid] = bi;
+    if (lane == 0) {
+      sm.best_v[w] = bv;
+      sm.best_i[w] = bi;
     }
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
       float v = sm.best_v[0];
       int i = sm.best_i[0];
-      for (int t = 1; t < kRows; ++t) {
+      for (int t = 1; t < kConsumerWarps; ++t) {
         if (sm.best_v[t] > v || (sm.best_v[t] == v && sm.best_i[t] < i)) {
           v = sm.best_v[t];
           i = sm.best_i[t];
@@ -532,34 +504,30 @@ struct Consumer {
         }
       }
     }
-    consumer_sync(kConsumerThreads);
   }
 
-  // q/k RMSNorm over one head (128 threads: t in [0,128) of group `grp`) and
-  // rotary embedding; returns the rotated fp16 value as float.
-  // (modeling_qwen3_vl.py:398-403 per head, then :124-128 + :427-431)
-  __device__ float norm_rope_128(float v, const __half* nw, int grp, int t, float eps, bool rope) {
-    AttnSmem& at = sm.u.at;
-    float ss = warp_sum(v * v);
-    if (lane == 0) at.red[w] = ss;
-    consumer_sync(kConsumerThreads);
-    const float tot = at.red[grp * 4 + 0] + at.red[grp * 4 + 1] + at.red[grp * 4 + 2] + at.red[grp * 4 + 3];
-    const float n = r16(v * rsqrtf(tot / (float)kHD + eps));
-    const float qn = r16(__half2float(nw[t]) * n);
-    if (!rope) {
-      consumer_sync(kConsumerThreads);
-      return qn;
+  // One 128-dim head per warp (lane l holds dims 4l..4l+3): per-head RMSNorm
+  // (modeling_qwen3_vl.py:398-403) and rotary embedding (:124-128, :427-431).
+  // rotate_half's partner of dim d is d +- 64, held by lane l ^ 16.
+  __device__ void norm_rope_head(float (&v)[4], const __half* nw, float eps, const float (&cs)[4],
+                                 const float (&sn)[4]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
+    const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
+    float xn[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) xn[e] = r16(__half2float(nw[lane * 4 + e]) * r16(v[e] * inv));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
+      const float rot = lane < 16 ? -p : p;
+      v[e] = r16(r16(xn[e] * cs[e]) + r16(rot * sn[e]));
     }
-    at.tmp[grp][t] = qn;
-    consumer_sync(kConsumerThreads);
-    const float rot = t < kHD / 2 ? -at.tmp[grp][t + kHD / 2] : at.tmp[grp][t - kHD / 2];
-    const float outv = r16(r16(qn * at.cs[t]) + r16(rot * at.sn[t]));
-    consumer_sync(kConsumerThreads);
-    return outv;
   }
 
   __device__ void run_attention(const AicasPhase& d) {
-    AttnSmem& at = sm.u.at;
+    AttnSmem& at = sm.at;
     const bool q_ready = d.flags & AICAS_F_Q_READY;
     const int valid = phase_valid_len(d, in);
     if (valid == 0) {
@@ -574,19 +542,23 @@ struct Consumer {
     __half* kc = reinterpret_cast<__half*>(d.k_cache);
     __half* vc = reinterpret_cast<__half*>(d.v_cache);
     const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
-    if (!q_ready && tid < kHD) {
-      // interleaved MRoPE (modeling_qwen3_vl.py:352-386)
-      const int i = tid % (kHD / 2);
+    // interleaved MRoPE cos/sin of this lane's 4 dims (modeling_qwen3_vl.py:352-386)
+    float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+    if (!q_ready) {
       const AicasStepState* stt = a.state;
-      int axis = 0;
-      if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
-      else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
-      const float ang = stt->inv_freq[i] * (float)in.rope[axis];
-      at.cs[tid] = r16(cosf(ang));
-      at.sn[tid] = r16(sinf(ang));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = (lane * 4 + e) % (kHD / 2);
+        int axis = 0;
+        if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
+        else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
+        const float ang = stt->inv_freq[i] * (float)in.rope[axis];
+        cs[e] = r16(cosf(ang));
+        sn[e] = r16(sinf(ang));
+      }
     }
-    consumer_sync(kConsumerThreads);
     const float scale = d.scale;
+    const int jpos = pos / kAttnChunk;
     const int grp = tid / kHD, t = tid % kHD;
     // per-warp online-softmax state for the 2 query heads of the current KV head
     float m[2], l[2], acc[2][4];
@@ -595,21 +567,29 @@ struct Consumer {
       const int h = u / cph, j = u % cph;
       const bool seg_start = (u == rg.start) || (j == 0);
       const bool seg_end = (u == rg.start + rg.count - 1) || (j == cph - 1);
-      const int jpos = pos / kAttnChunk;
       if (seg_start) {
         const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
         const bool has_pos = !q_ready && jpos >= j && jpos <= last_j;
-        // queries of heads 2h, 2h+1
-        const int qh = h * 2 + grp;
-        float qv = ldcg_half(qkv + qh * kHD + t);
-        if (!q_ready) qv = norm_rope_128(qv, reinterpret_cast<const __half*>(d.norm_w), grp, t, d.eps, true);
-        at.q[grp][t] = qv;
-        if (has_pos) {
-          // fresh k (group 0 threads) and v (group 1 threads) of this head
-          const float raw = ldcg_half(qkv + qsz + (grp == 0 ? 0 : kvsz) + h * kHD + t);
-          const float kv = norm_rope_128(raw, reinterpret_cast<const __half*>(d.norm_w2), grp, t, d.eps, true);
-          if (grp == 0) at.kf[t] = kv;
-          else at.vf[t] = raw;
+        if (w < 2) {  // query heads 2h, 2h+1
+          const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(qkv + (h * 2 + w) * kHD + lane * 4));
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+          if (!q_ready) norm_rope_head(v, sm.nw, d.eps, cs, sn);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) at.q[w][lane * 4 + e] = v[e];
+        } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
+          const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
+          const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(qkv + off));
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+          if (w == 2) norm_rope_head(v, sm.nw + kHD, d.eps, cs, sn);
+          float* dst = w == 2 ? at.kf : at.vf;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
+          __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
+          __half* cache = w == 2 ? kc : vc;
+          *reinterpret_cast<uint2*>(cache + ((size_t)h * d.max_len + pos) * kHD + lane * 4) =
+              *reinterpret_cast<uint2*>(o);
         }
         consumer_sync(kConsumerThreads);
 #pragma unroll
@@ -625,53 +605,41 @@ struct Consumer {
       const int st = r.stage();
       wait_full(st);
       const int p0 = j * kAttnChunk;
-      uint8_t* kt = sm.ring[st];
-      uint8_t* vt = sm.ring[st] + kStageBytes / 2;
-      if (!q_ready && j == jpos) {
-        // write the current position into the tile and into the cache
-        const int rr = pos - p0;
-        if (grp == 0) {
-          const __half hv = __float2half_rn(at.kf[t]);
-          reinterpret_cast<__half*>(kt)[rr * kHD + t] = hv;
-          kc[((size_t)h * d.max_len + pos) * kHD + t] = hv;
-        } else {
-          const __half hv = __float2half_rn(at.vf[t]);
-          reinterpret_cast<__half*>(vt)[rr * kHD + t] = hv;
-          vc[((size_t)h * d.max_len + pos) * kHD + t] = hv;
-        }
-        fence_proxy_async_smem();
-        consumer_sync(kConsumerThreads);
-      }
-      // scores of this warp's 4 positions for both query heads
-      float sc[8];
+      const uint8_t* kt = sm.ring[st];
+      const uint8_t* vt = sm.ring[st] + kStageBytes / 2;
+      // this warp's 4 positions; the current position comes from registers-
+      // staged smem (at.kf / at.vf), never from the (stale) cache tile
+      float kv4[4][4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int pr = w * 4 + i;
-        const uint2 kv = *reinterpret_cast<const uint2*>(kt + pr * kHD * 2 + lane * 8);
-        const __half2* kh = reinterpret_cast<const __half2*>(&kv);
-        const float2 k01 = __half22float2(kh[0]), k23 = __half22float2(kh[1]);
+        const int p = p0 + w * 4 + i;
+        if (!q_ready && p == pos) {
 #pragma unroll
-        for (int g = 0; g < 2; ++g)
-          sc[i * 2 + g] = qreg[g][0] * k01.x + qreg[g][1] * k01.y + qreg[g][2] * k23.x + qreg[g][3] * k23.y;
+          for (int e = 0; e < 4; ++e) kv4[i][e] = at.kf[lane * 4 + e];
+        } else {
+          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * 4 + i) * kHD * 2 + lane * 8);
+          const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+          kv4[i][0] = __low2float(kh[0]);
+          kv4[i][1] = __high2float(kh[0]);
+          kv4[i][2] = __low2float(kh[1]);
+          kv4[i][3] = __high2float(kh[1]);
+        }
       }
-      int idx;
-      const float tot = reduce_scatter<8>(sc, idx);
-      // broadcast all 8 scores: value v lives in lane ((v>>2)&1)<<4 | ((v>>1)&1)<<3 | (v&1)<<2
-      float s8[8];
+      float sc[2][4];
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const int src = (((v >> 2) & 1) << 4) | (((v >> 1) & 1) << 3) | ((v & 1) << 2);
-        s8[v] = __shfl_sync(0xffffffffu, tot, src);
-      }
-      (void)idx;
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          sc[g][i] = warp_sum(qreg[g][0] * kv4[i][0] + qreg[g][1] * kv4[i][1] + qreg[g][2] * kv4[i][2] +
+                              qreg[g][3] * kv4[i][3]);
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
         float cmax = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int p = p0 + w * 4 + i;
-          s8[i * 2 + g] = (p < valid) ? s8[i * 2 + g] * scale : -INFINITY;
-          cmax = fmaxf(cmax, s8[i * 2 + g]);
+          sc[g][i] = (p < valid) ? sc[g][i] * scale : -INFINITY;
+          cmax = fmaxf(cmax, sc[g][i]);
         }
         const float mn = fmaxf(m[g], cmax);
         if (mn == -INFINITY) continue;
@@ -684,15 +652,22 @@ struct Consumer {
         for (int i = 0; i < 4; ++i) {
           const int p = p0 + w * 4 + i;
           if (p < valid) {
-            const float pr = expf(s8[i * 2 + g] - mn);
+            const float pr = expf(sc[g][i] - mn);
             l[g] += pr;
-            const uint2 vv = *reinterpret_cast<const uint2*>(vt + (w * 4 + i) * kHD * 2 + lane * 8);
-            const __half2* vh = reinterpret_cast<const __half2*>(&vv);
-            const float2 v01 = __half22float2(vh[0]), v23 = __half22float2(vh[1]);
-            acc[g][0] += pr * v01.x;
-            acc[g][1] += pr * v01.y;
-            acc[g][2] += pr * v23.x;
-            acc[g][3] += pr * v23.y;
+            float vv[4];
+            if (!q_ready && p == pos) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
+            } else {
+              const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * 4 + i) * kHD * 2 + lane * 8);
+              const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+              vv[0] = __low2float(vh[0]);
+              vv[1] = __high2float(vh[0]);
+              vv[2] = __low2float(vh[1]);
+              vv[3] = __high2float(vh[1]);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[g][e] += pr * vv[e];
           }
         }
       }
@@ -763,10 +738,20 @@ struct Consumer {
 
   __device__ void run(const AicasPhase* P, int n_phases) {
     for (int ph = 0; ph < n_phases; ++ph) {
-      if (ph > 0) barrier();
       const AicasPhase& d = P[ph];
+      if (ph > 0) {
+        consumer_sync(kConsumerThreads);  // every warp's outputs of phase ph-1 are written
+        if (tid == 0) grid_arrive(s);
+      }
+      prefetch(d);
+      if (ph > 0) {
+        if (tid == 0) grid_wait(s, bar_base + (uint64_t)(++bar_k) * nct);
+      }
+      consumer_sync(kConsumerThreads);  // barrier passed; prefetched norm weights visible
+      stamp(ph, 0);
       if (d.kind == AICAS_PH_ATTN) run_attention(d);
       else run_matvec(d);
+      stamp(ph, 1);
     }
   }
 };
@@ -804,7 +789,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   c.lane = threadIdx.x & 31;
   c.nct = gridDim.x;
   c.cta = blockIdx.x;
-  c.gen = *reinterpret_cast<volatile uint32_t*>(&a.scratch->bar_gen);
+  const uint64_t now = ld_relaxed_u64(&a.scratch->bar_count);
+  c.bar_base = now - now % (uint64_t)gridDim.x;
   c.run(P, a.n_phases);
 }
 
@@ -970,6 +956,20 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
   a.n_phases = n_phases;
   a.state = state;
   a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  return launch_program(a, stream);
+}
+
+AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
+                                             AicasStepState* state, void* scratch, int64_t* trace,
+                                             cudaStream_t stream) {
+  if (!device_phases || n_phases < 1 || !state || !trace) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  a.phases = device_phases;
+  a.n_phases = n_phases;
+  a.state = state;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  a.trace = trace;
   return launch_program(a, stream);
 }
 

@@ -206,6 +206,25 @@ class Qwen3VLDecodeEngine:
                                                     ctypes.c_void_p(self.scratch.data_ptr()), stream)
             check(rc, "aicas_decode_program_f16")
 
+    def launch_traced(self) -> torch.Tensor:
+        """One step with per-CTA per-phase %globaltimer stamps; returns the
+        trace [num_ctas, n_phases, 2] (ns) after synchronising."""
+        trace = torch.zeros((self.num_ctas, self.n_phases, 2), dtype=torch.int64, device=self.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        rc = self._lib.aicas_decode_program_trace_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
+                                                      ctypes.c_void_p(self.state_dev.data_ptr()),
+                                                      ctypes.c_void_p(self.scratch.data_ptr()),
+                                                      ctypes.c_void_p(trace.data_ptr()), stream)
+        check(rc, "aicas_decode_program_trace_f16")
+        torch.cuda.synchronize(self.device)
+        return trace.cpu()
+
+    def phase_names(self) -> list[str]:
+        names = []
+        for li in range(self.shape.num_layers):
+            names += [f"L{li}.qkv", f"L{li}.attn", f"L{li}.o_proj", f"L{li}.gate_up", f"L{li}.down"]
+        return names + ["lm_head"]
+
     def graph(self, steps: int) -> torch.cuda.CUDAGraph:
         """A CUDA graph of `steps` consecutive decode steps (captured once;
         replays advance the device step state)."""

@@ -251,6 +251,9 @@ def run_ours(args, rank: int, world: int):
     barrier()
     e2e_ok = bool(torch.equal(out_host, toks))
 
+    if args.trace and rank == 0:
+        write_trace_summary(eng, start_state, args.trace)
+
     # ---- max over ranks
     vals = torch.tensor([ms, e2e_ms], dtype=torch.float64)
     if world > 1:
@@ -293,6 +296,36 @@ def run_ours(args, rank: int, world: int):
         dist.destroy_process_group()
 
 
+def write_trace_summary(eng, start_state, path):
+    """One traced decode step at cache slot 1024: per phase, the time from
+    the first CTA passing its barrier to the last CTA finishing (span), the
+    mean per-CTA busy time, and the barrier gap to the next phase."""
+    import torch
+
+    eng.restore(start_state)
+    tr = eng.launch_traced().double()  # [cta, phase, 2] ns
+    names = eng.phase_names()
+    t0 = tr[:, 0, 0].min()
+    start, end = tr[:, :, 0] - t0, tr[:, :, 1] - t0
+    span = end.max(0).values - start.min(0).values
+    busy = (end - start).mean(0)
+    gap = torch.zeros_like(span)
+    gap[:-1] = start.min(0).values[1:] - end.max(0).values[:-1]
+    kinds = {}
+    for i, nm in enumerate(names):
+        k = nm.split(".")[-1]
+        e = kinds.setdefault(k, {"n": 0, "span_us": 0.0, "busy_us": 0.0, "gap_after_us": 0.0})
+        e["n"] += 1
+        e["span_us"] += float(span[i]) / 1e3
+        e["busy_us"] += float(busy[i]) / 1e3
+        e["gap_after_us"] += float(gap[i]) / 1e3
+    total = float(end.max() - start.min()) / 1e3
+    summary = {"step_us": total, "by_kind_total_us": kinds,
+               "per_phase_span_us": [round(float(x) / 1e3, 2) for x in span]}
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    Path(path).write_text(json.dumps(summary, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -301,6 +334,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--trace", default="", help="write a per-phase timeline summary (JSON) to this path")
     ap.add_argument("--layers", type=int, default=28,
                     help="profiling case only: a smaller model (the headline is 28 layers)")
     args = ap.parse_args()

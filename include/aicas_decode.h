@@ -66,7 +66,7 @@ AICAS_API int aicas_set_cooperative_launch(int enable);
 AICAS_API int aicas_validate_phases(const AicasPhase* phases, int n);
 
 /* y[n] = W[n,k] x[k] (+ bias[n]); fp32 accumulation, fp16 output.
- * k % 8 == 0, k <= 8192, x/W 16-byte aligned.
+ * k % 8 == 0, k <= 6144, x/W 16-byte aligned.
  * Replaces `nosplit_matvec_half` (cuda_decode_gemv_ops/matvec.py:274-321;
  * kernels cuda_extensions/decode_gemv_kernel_matvec.cuh:209-343). */
 AICAS_API int aicas_gemv_f16(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t k,
@@ -131,6 +131,16 @@ AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const 
  * layer loop over `OptimizedDecoderLayer.forward` (optimized_layer.py:108-469). */
 AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
                                        void* scratch, aicas_stream_t stream);
+
+/* Profiling variant of aicas_decode_program_f16: additionally writes, per
+ * CTA and phase, the %globaltimer (ns) when the phase's consumers passed its
+ * grid barrier and when they finished it, to trace[cta][phase][2] (int64,
+ * aicas_num_ctas() * n_phases * 2 entries).  The reference records the same
+ * kind of per-block timelines in its `*_profile_*` kernel variants
+ * (cuda_extensions/decode_gemv_kernel_common.cuh:174-188). */
+AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
+                                             AicasStepState* state, void* scratch, int64_t* trace,
+                                             aicas_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -42,7 +42,7 @@ typedef struct AicasPhase {
   int32_t kind;
   int32_t flags;
   int32_t n;        // GEMV/LMHEAD: output rows; GATEUP: intermediate size (rows of gate)
-  int32_t k;        // reduction length (multiple of 8, <= AICAS_MAX_K)
+  int32_t k;        // reduction length (multiple of 8, <= AICAS_MAX_K = 6144)
   int32_t rot;      // CTA rotation of the row-group assignment (load balance across phases)
   int32_t kv_heads; // attention
   int32_t q_heads;  // attention
@@ -89,13 +89,12 @@ typedef struct AicasStepState {
 #define AICAS_MAX_SPLITS 256
 #define AICAS_MAX_KV_HEADS 8
 #define AICAS_HEAD_DIM 128
-#define AICAS_MAX_K 8192
+#define AICAS_MAX_K 6144
 
 // Scratch memory of the persistent kernel (caller allocates, zero-fills once;
 // every launch leaves it ready for the next one).
 typedef struct AicasScratch {
-  uint32_t bar_count;   // grid barrier arrivals
-  uint32_t bar_gen;     // grid barrier generation
+  uint64_t bar_count;   // grid barrier arrivals (monotonic across launches)
   int32_t error;        // first error code raised on the device (0 = none)
   int32_t abort;        // set with `error`; every wait gives up when it is set
   uint32_t head_done[AICAS_MAX_KV_HEADS];  // split-KV merge arrivals per KV head
