@@ -25,6 +25,7 @@ F_X_ADD = 1 << 5
 F_RESID_ADD = 1 << 6
 F_Q_READY = 1 << 7
 F_STORE_X = 1 << 8
+F_KBLOCKED = 1 << 9
 
 DEVICE_ERRORS = {
     10: "grid barrier timed out",

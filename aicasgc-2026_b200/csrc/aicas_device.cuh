@@ -154,17 +154,27 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
   return v;
 }
 
-__device__ __forceinline__ void grid_arrive(AicasScratch* s) {
-  __threadfence();
-  red_release_add_u64(&s->bar_count, 1ull);
-}
+// Arrival: a release reduction, called by one thread after a CTA-wide
+// barrier, so every write the CTA made before the barrier is visible to a
+// thread that observes the new count (release is cumulative over the
+// writes ordered before it by bar.sync).
+__device__ __forceinline__ void grid_arrive(AicasScratch* s) { red_release_add_u64(&s->bar_count, 1ull); }
 
-// Bounded wait until `target` arrivals; false on timeout or abort.
+__device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Bounded wait until `target` arrivals (relaxed polling, one acquire fence
+// on success); false on timeout or abort.
 __device__ __forceinline__ bool grid_wait(AicasScratch* s, uint64_t target) {
-  if ((int64_t)(ld_acquire_u64(&s->bar_count) - target) >= 0) return true;
+  if ((int64_t)(ld_relaxed_u64(&s->bar_count) - target) >= 0) {
+    fence_acquire_gpu();
+    return true;
+  }
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if ((int64_t)(ld_acquire_u64(&s->bar_count) - target) >= 0) return true;
+    if ((int64_t)(ld_relaxed_u64(&s->bar_count) - target) >= 0) {
+      fence_acquire_gpu();
+      return true;
+    }
     if ((it & 31u) == 0) {
       if (ld_volatile_int(&s->abort)) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {

@@ -2,7 +2,7 @@
 //
 // One launch runs a list of phases (aicas_phase_program.h) with one CTA per SM:
 //   warp 0      producer: streams every tile this CTA will consume, phase after
-//               phase, from HBM into a 12-stage shared-memory ring with bulk
+//               phase, from HBM into a 6-stage shared-memory ring with bulk
 //               async copies (cp.async.bulk + mbarrier complete_tx).  It never
 //               waits on a grid barrier, so HBM keeps streaming the next
 //               phase's weights while the consumers wait for activations.
@@ -12,13 +12,17 @@
 //               reduce each tile row against it with exact fp16 products and
 //               fp32 accumulation.
 //
-// GEMV tile: 8 weight rows x 1024 columns (16 KB).  Consumer warp w owns row w
-// of every tile; lane l the columns j*256 + 8l (j = 0..3) of each 1024-column
-// chunk, so a lane keeps its slice of the input vector in registers for the
-// whole phase, every weight byte is read from shared memory exactly once
-// (conflict-free 512-byte warp accesses) and a row needs one warp reduction.
+// GEMV tile: 8 weight rows x 2048 columns (32 KB), fetched with ONE bulk copy
+// (rows are contiguous when k <= 2048; the engine stores down_proj K-blocked,
+// [k/2048][n][2048], so its tiles are contiguous too: bulk copies of 8 KB and
+// more are what reach full HBM bandwidth on B200, 2 KB copies top out near
+// 4 TB/s).  Consumer warp w owns row w of every tile; lane l the columns
+// j*256 + 8l (j = 0..7) of each 2048-column chunk, so a lane keeps its slice
+// of the input vector in registers for the whole phase, every weight byte is
+// read from shared memory exactly once (conflict-free 512-byte warp accesses)
+// and a row needs one warp reduction.
 //
-// Attention tile: K and V rows of 32 cache positions of one KV head (16 KB).
+// Attention tile: K and V rows of 64 cache positions of one KV head (32 KB).
 // Work units (KV head, 32-position chunk) are split into contiguous ranges per
 // CTA; each CTA's segment of a head yields one (max, sum, acc) partial, and the
 // last CTA to finish a head (atomic arrival count) merges its partials in a
@@ -52,13 +56,14 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kRows = kConsumerWarps;  // weight rows per GEMV tile: one per consumer warp
-constexpr int kChunk = 1024;           // columns per GEMV tile
+constexpr int kChunk = 2048;           // columns per GEMV tile
 constexpr int kRowBytes = kChunk * 2;
-constexpr int kStageBytes = kRows * kRowBytes;  // 16 KB
-constexpr int kStages = 12;
-constexpr int kAttnChunk = 32;  // cache positions per attention tile
+constexpr int kStageBytes = kRows * kRowBytes;  // 32 KB: one bulk copy per tile
+constexpr int kStages = 6;
+constexpr int kAttnChunk = 64;  // cache positions per attention tile
+constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
-constexpr int kMaxChunks = AICAS_MAX_K / kChunk;  // 6
+constexpr int kMaxChunks = AICAS_MAX_K / kChunk;  // 3
 constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
 constexpr int kResidPrefetch = 4;                 // residual rows kept in registers per warp
 
@@ -192,8 +197,15 @@ __device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
           const int col0 = c * kChunk;
           const uint32_t bytes = min(kChunk, d.k - col0) * 2;
           mbar_arrive_expect_tx(&sm.full[st], nrows * bytes);
-          for (int i = 0; i < nrows; ++i)
-            bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
+          if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
+            bulk_g2s(sm.ring[st], W + (size_t)row0 * d.k, nrows * bytes, &sm.full[st], pol);
+          } else if (d.flags & AICAS_F_KBLOCKED) {  // block c of rows row0.. is contiguous
+            const int rows_total = d.kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
+            bulk_g2s(sm.ring[st], W + ((size_t)c * rows_total + row0) * kChunk, nrows * bytes, &sm.full[st], pol);
+          } else {  // row-major with k > 2048: one copy per row piece
+            for (int i = 0; i < nrows; ++i)
+              bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
+          }
           ++r.it;
         }
       }
@@ -364,6 +376,46 @@ struct Consumer {
     }
   }
 
+  // Reduce-scatter of NV per-lane partial sums (NV = 2, 4, 8 or 16) across the
+  // warp: halve the kept values at lane offsets 16, 8, ... then finish with a
+  // full butterfly.  Lane l ends with the warp total of value index
+  // sum over steps of (lane bit set ? half : 0), see scatter_lane.
+  template <int NV>
+  __device__ __forceinline__ float reduce_scatter(float (&a)[NV], int& idx) {
+    int base = 0;
+    int o = 16;
+#pragma unroll
+    for (int n = NV; n > 1; n >>= 1, o >>= 1) {
+      const bool hi = lane & o;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = hi ? a[i] : a[i + n / 2];
+        const float keep = hi ? a[i + n / 2] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+      base += hi ? n / 2 : 0;
+    }
+    float t = a[0];
+#pragma unroll
+    for (; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    idx = base;
+    return t;
+  }
+
+  // A lane that holds value index v after reduce_scatter<NV>.
+  template <int NV>
+  __device__ __forceinline__ static int scatter_lane(int v) {
+    int lane_bits = 0, o = 16;
+#pragma unroll
+    for (int n = NV; n > 1; n >>= 1, o >>= 1) {
+      if (v >= n / 2) {
+        lane_bits |= o;
+        v -= n / 2;
+      }
+    }
+    return lane_bits;
+  }
+
   // GEMV / GATEUP / LMHEAD phase.
   __device__ void run_matvec(const AicasPhase& d) {
     uint4 xr[kMaxChunks][kVec];
@@ -406,7 +458,7 @@ struct Consumer {
             const int st = r.stage();
             wait_full(st);
             if (vrow) {
-              const uint8_t* base = sm.ring[st] + w * kRowBytes + lane * 16;
+              const uint8_t* base = sm.ring[st] + w * (C == 1 ? d.k * 2 : kRowBytes) + lane * 16;
 #pragma unroll
               for (int j = 0; j < kVec; ++j) {
                 if (c * kChunk + j * 256 + lane * 8 < d.k) {
@@ -607,37 +659,47 @@ struct Consumer {
       const int p0 = j * kAttnChunk;
       const uint8_t* kt = sm.ring[st];
       const uint8_t* vt = sm.ring[st] + kStageBytes / 2;
-      // this warp's 4 positions; the current position comes from registers-
-      // staged smem (at.kf / at.vf), never from the (stale) cache tile
-      float kv4[4][4];
+      // this warp's kPosPerWarp positions; the current position's k/v come
+      // from shared memory (at.kf / at.vf), never from the cache tile
+      float kv[kPosPerWarp][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int p = p0 + w * 4 + i;
+      for (int i = 0; i < kPosPerWarp; ++i) {
+        const int p = p0 + w * kPosPerWarp + i;
         if (!q_ready && p == pos) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) kv4[i][e] = at.kf[lane * 4 + e];
+          for (int e = 0; e < 4; ++e) kv[i][e] = at.kf[lane * 4 + e];
         } else {
-          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * 4 + i) * kHD * 2 + lane * 8);
+          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
           const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-          kv4[i][0] = __low2float(kh[0]);
-          kv4[i][1] = __high2float(kh[0]);
-          kv4[i][2] = __low2float(kh[1]);
-          kv4[i][3] = __high2float(kh[1]);
+          kv[i][0] = __low2float(kh[0]);
+          kv[i][1] = __high2float(kh[0]);
+          kv[i][2] = __low2float(kh[1]);
+          kv[i][3] = __high2float(kh[1]);
         }
       }
-      float sc[2][4];
+      // partial dots of the lane's 4 dims; value index v = g * kPosPerWarp + i
+      float part[2 * kPosPerWarp];
 #pragma unroll
       for (int g = 0; g < 2; ++g)
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          sc[g][i] = warp_sum(qreg[g][0] * kv4[i][0] + qreg[g][1] * kv4[i][1] + qreg[g][2] * kv4[i][2] +
-                              qreg[g][3] * kv4[i][3]);
+        for (int i = 0; i < kPosPerWarp; ++i)
+          part[g * kPosPerWarp + i] =
+              qreg[g][0] * kv[i][0] + qreg[g][1] * kv[i][1] + qreg[g][2] * kv[i][2] + qreg[g][3] * kv[i][3];
+      int vidx;
+      const float tot = reduce_scatter<2 * kPosPerWarp>(part, vidx);
+      (void)vidx;
+      float sc[2][kPosPerWarp];
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int i = 0; i < kPosPerWarp; ++i)
+          sc[g][i] = __shfl_sync(0xffffffffu, tot, scatter_lane<2 * kPosPerWarp>(g * kPosPerWarp + i));
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
         float cmax = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int p = p0 + w * 4 + i;
+        for (int i = 0; i < kPosPerWarp; ++i) {
+          const int p = p0 + w * kPosPerWarp + i;
           sc[g][i] = (p < valid) ? sc[g][i] * scale : -INFINITY;
           cmax = fmaxf(cmax, sc[g][i]);
         }
@@ -649,8 +711,8 @@ struct Consumer {
         for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
         m[g] = mn;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int p = p0 + w * 4 + i;
+        for (int i = 0; i < kPosPerWarp; ++i) {
+          const int p = p0 + w * kPosPerWarp + i;
           if (p < valid) {
             const float pr = expf(sc[g][i] - mn);
             l[g] += pr;
@@ -659,7 +721,7 @@ struct Consumer {
 #pragma unroll
               for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
             } else {
-              const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * 4 + i) * kHD * 2 + lane * 8);
+              const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
               const __half2* vh = reinterpret_cast<const __half2*>(&vr);
               vv[0] = __low2float(vh[0]);
               vv[1] = __high2float(vh[0]);
@@ -844,6 +906,7 @@ static int validate_phase(const AicasPhase& d) {
       if ((d.flags & AICAS_F_STORE_X) && (!d.x_out || !aligned16(d.x_out))) return AICAS_ERR_ALIGN;
       if (d.kind != AICAS_PH_LMHEAD && !d.out) return AICAS_ERR_ARG;
       if (d.kind == AICAS_PH_GATEUP && (d.flags & (AICAS_F_RESID | AICAS_F_BIAS))) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_KBLOCKED) && d.k % 2048 != 0) return AICAS_ERR_SHAPE;
       return AICAS_OK;
     case AICAS_PH_ATTN:
       if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
@@ -956,20 +1019,6 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
   a.n_phases = n_phases;
   a.state = state;
   a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
-AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
-                                             AicasStepState* state, void* scratch, int64_t* trace,
-                                             cudaStream_t stream) {
-  if (!device_phases || n_phases < 1 || !state || !trace) return AICAS_ERR_ARG;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  a.phases = device_phases;
-  a.n_phases = n_phases;
-  a.state = state;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  a.trace = trace;
   return launch_program(a, stream);
 }
 

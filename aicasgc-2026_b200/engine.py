@@ -29,7 +29,7 @@ import math
 
 import torch
 
-from _native import (F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED, PH_ATTN, PH_GATEUP, PH_GEMV,
+from _native import (F_KBLOCKED, F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED, PH_ATTN, PH_GATEUP, PH_GEMV,
                      PH_LMHEAD, AicasError, AicasPhase, AicasStepState, check, lib, scratch_bytes)
 from _ops import device_error
 from qwen3vl_config import QWEN3VL_2B, Qwen3VLTextShape
@@ -67,6 +67,10 @@ class Qwen3VLDecodeEngine:
         def W(key):
             return state[key].to(**f16).contiguous()
 
+        def kblock(w):
+            n, k = w.shape
+            return w.view(n, k // 2048, 2048).permute(1, 0, 2).contiguous()
+
         with torch.cuda.device(dev):
             self.embed = W("embed_tokens.weight")
             self.final_norm = W("norm.weight")
@@ -83,7 +87,8 @@ class Qwen3VLDecodeEngine:
                     "ln2": W(p + "post_attention_layernorm.weight"),
                     "gate_up": torch.cat([W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight")],
                                          0).contiguous(),
-                    "down": W(p + "mlp.down_proj.weight"),
+                    # K-blocked [k/2048][n][2048]: every 8-row tile is one contiguous 32 KB copy
+                    "down": kblock(W(p + "mlp.down_proj.weight")),
                 })
             # StaticCache-layout KV: [layers][1, KVH, Lmax, 128]
             kv_shape = (s.num_layers, 1, s.num_kv_heads, max_cache_len, s.head_dim)
@@ -124,7 +129,7 @@ class Qwen3VLDecodeEngine:
             p = AicasPhase()
             p.kind, p.flags, p.n, p.k = kind, flags, n, k
             p.rot = extra % nct
-            groups = -(-n // 4)
+            groups = -(-n // 8)
             extra += groups % nct
             p.w, p.x, p.out = ptr(w), ptr(x), ptr(out)
             p.norm_w = ptr(norm_w) if norm_w is not None else None
@@ -149,7 +154,8 @@ class Qwen3VLDecodeEngine:
                       self.h_mid, resid=self.embed if first else self.h)
             gemv_like(PH_GATEUP, F_NORM, s.intermediate, s.hidden, L["gate_up"], self.h_mid, self.act,
                       norm_w=L["ln2"])
-            gemv_like(PH_GEMV, F_RESID, s.hidden, s.intermediate, L["down"], self.act, self.h, resid=self.h_mid)
+            gemv_like(PH_GEMV, F_RESID | F_KBLOCKED, s.hidden, s.intermediate, L["down"], self.act, self.h,
+                      resid=self.h_mid)
         gemv_like(PH_LMHEAD, F_NORM, s.vocab, s.hidden, self.embed, self.h, self.h, norm_w=self.final_norm)
         phases[-1].out = None
         arr = (AicasPhase * len(phases))(*phases)

@@ -34,6 +34,8 @@ enum AicasPhaseFlags {
   AICAS_F_RESID_ADD = 1 << 6,    // resid := r16(resid + resid2)
   AICAS_F_Q_READY = 1 << 7,      // attention: q is final (no norm/rope); no KV write
   AICAS_F_STORE_X = 1 << 8,      // GEMV/GATEUP: CTA 0 stores the prologue vector to x_out
+  AICAS_F_KBLOCKED = 1 << 9,     // W is stored K-blocked: [k/2048][n][2048] (k % 2048 == 0), so every
+                                 // 8-row x 2048-column tile is one contiguous 32 KB block
 };
 
 // One phase.  Pointers are device pointers (fp16 data is `__half`, passed as
@@ -49,7 +51,7 @@ typedef struct AicasPhase {
   int32_t max_len;  // attention: cache slots per head
   int32_t embed_rows; // F_X_EMBED / F_RESID_EMBED: rows of the embedding table
   int32_t pad1;
-  const void* w;      // weight [n, k] (GATEUP: [2n, k], gate rows first)
+  const void* w;      // weight [n, k] row-major (GATEUP: [2n, k], gate rows first), or K-blocked
   const void* norm_w; // RMSNorm weight [k] (attention: q_norm weight [128])
   const void* norm_w2;// attention: k_norm weight [128]
   const void* x;      // input vector [k] (attention: the fused qkv vector or final q)
