@@ -1022,6 +1022,20 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
   return launch_program(a, stream);
 }
 
+AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
+                                             AicasStepState* state, void* scratch, int64_t* trace,
+                                             cudaStream_t stream) {
+  if (!device_phases || n_phases < 1 || !state || !trace) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  a.phases = device_phases;
+  a.n_phases = n_phases;
+  a.state = state;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  a.trace = trace;
+  return launch_program(a, stream);
+}
+
 AICAS_API int aicas_gemv_f16(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t k,
                              void* scratch, cudaStream_t stream) {
   if (n < 1 || n > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
