@@ -95,7 +95,7 @@ struct ProgramArgs {
   int pad;
   AicasStepState* state;  // may be null (op-level calls)
   AicasScratch* scratch;
-  int64_t* trace;  // optional [grid][n_phases][2] globaltimer stamps
+  int64_t* trace;  // optional [grid][n_phases][4]: start, end, consumer tile-wait ns, producer slot-wait ns
   AicasPhase inl[4];
 };
 
@@ -157,11 +157,22 @@ __device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
   Ring r;
   bool ok = true;
   const AicasPhase* P = a.phases ? a.phases : a.inl;
+  uint64_t slot_wait = 0;  // trace only
   auto acquire = [&](int st) -> bool {
     if (r.round() == 0) return true;
+    if (a.trace) {
+      const uint64_t t0 = globaltimer_ns();
+      const bool good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+      slot_wait += globaltimer_ns() - t0;
+      return good;
+    }
     return mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
   };
   for (int ph = 0; ph < a.n_phases && ok; ++ph) {
+    if (a.trace && ph > 0) {
+      a.trace[((size_t)cta * a.n_phases + ph - 1) * 4 + 3] = (int64_t)slot_wait;
+      slot_wait = 0;
+    }
     const AicasPhase& d = P[ph];
     if (d.kind == AICAS_PH_ATTN) {
       const int valid = phase_valid_len(d, in);
@@ -211,6 +222,7 @@ __device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
       }
     }
   }
+  if (a.trace) a.trace[((size_t)cta * a.n_phases + a.n_phases - 1) * 4 + 3] = (int64_t)slot_wait;
   // Drain: every issued copy must land before this CTA may exit.  In the
   // normal path the consumers already waited for all of them.
   const uint32_t issued = r.it;
@@ -249,7 +261,16 @@ struct Consumer {
   // aborted) wait the CTA keeps walking the same program without waiting, so
   // every named barrier is still reached by all 256 consumer threads and the
   // launch ends promptly with the error recorded in the scratch block.
-  __device__ void wait_full(int st) { mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout); }
+  uint64_t wait_ns = 0;  // trace only: time consumer warp 0 spent waiting for tiles in this phase
+  __device__ void wait_full(int st) {
+    if (a.trace && tid == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout);
+      wait_ns += globaltimer_ns() - t0;
+      return;
+    }
+    mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout);
+  }
   __device__ void release(int st) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[st]);
@@ -257,7 +278,14 @@ struct Consumer {
   }
 
   __device__ void stamp(int ph, int which) {
-    if (a.trace && tid == 0) a.trace[((size_t)cta * a.n_phases + ph) * 2 + which] = (int64_t)globaltimer_ns();
+    if (a.trace && tid == 0) {
+      int64_t* t = a.trace + ((size_t)cta * a.n_phases + ph) * 4;
+      t[which] = (int64_t)globaltimer_ns();
+      if (which == 1) {
+        t[2] = (int64_t)wait_ns;
+        wait_ns = 0;
+      }
+    }
   }
 
   // Token id of the step, checked against the embedding table (an

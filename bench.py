@@ -303,19 +303,24 @@ def write_trace_summary(eng, start_state, path):
     import torch
 
     eng.restore(start_state)
-    tr = eng.launch_traced().double()  # [cta, phase, 2] ns
+    tr = eng.launch_traced().double()  # [cta, phase, 4] ns
     names = eng.phase_names()
     t0 = tr[:, 0, 0].min()
     start, end = tr[:, :, 0] - t0, tr[:, :, 1] - t0
     span = end.max(0).values - start.min(0).values
     busy = (end - start).mean(0)
+    cwait = tr[:, :, 2].mean(0)
+    pwait = tr[:, :, 3].mean(0)
     gap = torch.zeros_like(span)
     gap[:-1] = start.min(0).values[1:] - end.max(0).values[:-1]
     kinds = {}
     for i, nm in enumerate(names):
         k = nm.split(".")[-1]
-        e = kinds.setdefault(k, {"n": 0, "span_us": 0.0, "busy_us": 0.0, "gap_after_us": 0.0})
+        e = kinds.setdefault(k, {"n": 0, "span_us": 0.0, "busy_us": 0.0, "gap_after_us": 0.0,
+                                 "consumer_tile_wait_us": 0.0, "producer_slot_wait_us": 0.0})
         e["n"] += 1
+        e["consumer_tile_wait_us"] += float(cwait[i]) / 1e3
+        e["producer_slot_wait_us"] += float(pwait[i]) / 1e3
         e["span_us"] += float(span[i]) / 1e3
         e["busy_us"] += float(busy[i]) / 1e3
         e["gap_after_us"] += float(gap[i]) / 1e3
