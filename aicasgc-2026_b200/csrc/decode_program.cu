@@ -150,7 +150,7 @@ struct Ring {
   __device__ __forceinline__ uint32_t round() const { return it / kStages; }
 };
 
-__device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+__device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
   AicasScratch* s = a.scratch;
   const int nct = gridDim.x, cta = blockIdx.x;
   const uint64_t pol = l2_evict_first_policy();
@@ -245,7 +245,7 @@ __device__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
 struct Consumer {
   const ProgramArgs& a;
   Smem& sm;
-  const StepIn& in;
+  const StepIn in;
   AicasScratch* s;
   int tid;  // 0..255
   int w;    // consumer warp 0..7
@@ -262,7 +262,16 @@ struct Consumer {
   // every named barrier is still reached by all 256 consumer threads and the
   // launch ends promptly with the error recorded in the scratch block.
   uint64_t wait_ns = 0;  // trace only: time consumer warp 0 spent waiting for tiles in this phase
-  __device__ void wait_full(int st) {
+  __device__ __forceinline__ void wait_full_at(int st, uint32_t round) {
+    if (a.trace && tid == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      mbar_wait_bounded(&sm.full[st], round & 1u, s, kErrFullTimeout);
+      wait_ns += globaltimer_ns() - t0;
+      return;
+    }
+    mbar_wait_bounded(&sm.full[st], round & 1u, s, kErrFullTimeout);
+  }
+  __device__ __forceinline__ void wait_full(int st) {
     if (a.trace && tid == 0) {
       const uint64_t t0 = globaltimer_ns();
       mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout);
@@ -271,13 +280,13 @@ struct Consumer {
     }
     mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout);
   }
-  __device__ void release(int st) {
+  __device__ __forceinline__ void release(int st) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[st]);
     ++r.it;
   }
 
-  __device__ void stamp(int ph, int which) {
+  __device__ __forceinline__ void stamp(int ph, int which) {
     if (a.trace && tid == 0) {
       int64_t* t = a.trace + ((size_t)cta * a.n_phases + ph) * 4;
       t[which] = (int64_t)globaltimer_ns();
@@ -290,13 +299,13 @@ struct Consumer {
 
   // Token id of the step, checked against the embedding table (an
   // out-of-range id raises kErrBadInput and reads row 0 instead).
-  __device__ int64_t checked_token(const AicasPhase& d) {
+  __device__ __forceinline__ int64_t checked_token(const AicasPhase& d) {
     if (in.token >= 0 && in.token < d.embed_rows) return in.token;
     if (tid == 0) raise_error(s, kErrBadInput);
     return 0;
   }
 
-  __device__ float resid_value(const AicasPhase& d, int row) {
+  __device__ __forceinline__ float resid_value(const AicasPhase& d, int row) {
     const __half* rp = reinterpret_cast<const __half*>(d.resid);
     if (d.flags & AICAS_F_RESID_EMBED) rp += (size_t)checked_token(d) * d.n;
     float rv = ldcg_half(rp + row);
@@ -307,7 +316,7 @@ struct Consumer {
   // Work for phase `d` that depends on nothing the previous phase writes:
   // norm weights -> shared memory, first residual rows -> registers.  Runs
   // between this CTA's barrier arrival and its wait.
-  __device__ void prefetch(const AicasPhase& d) {
+  __device__ __forceinline__ void prefetch(const AicasPhase& d) {
     if (d.kind == AICAS_PH_ATTN) {
       if (!(d.flags & AICAS_F_Q_READY) && tid < 2 * kHD / 8) {
         const __half* src = reinterpret_cast<const __half*>(tid < kHD / 8 ? d.norm_w : d.norm_w2);
@@ -337,69 +346,72 @@ struct Consumer {
   //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
   // Every warp covers the whole vector across its lanes, so the sum of
   // squares is a warp reduction and no block synchronisation is needed.
-  __device__ void build_x(const AicasPhase& d, uint4 (&xr)[kMaxChunks][kVec]) {
-    const int k = d.k, C = n_chunks(d);
+  // Columns at or beyond k read as zero.
+  template <int C>
+  __device__ __forceinline__ void build_x(const AicasPhase& d, uint4 (&xr)[kMaxChunks][kVec]) {
+    const int k = d.k, flags = d.flags;
+    const float eps = d.eps;
     const __half* x = reinterpret_cast<const __half*>(d.x);
-    if (d.flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
+    if (flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
     const __half* x2 = reinterpret_cast<const __half*>(d.x2);
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < C; ++c) {
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
         const int col = c * kChunk + j * 256 + lane * 8;
         uint4 raw = make_uint4(0, 0, 0, 0);
-        if (c < C && col < k) {
+        if (col < k) {
           raw = ldcg_u4(x + col);
-          if (d.flags & AICAS_F_X_ADD) {
+          if (flags & AICAS_F_X_ADD) {
             const uint4 raw2 = ldcg_u4(x2 + col);
             __half2* hp = reinterpret_cast<__half2*>(&raw);
             const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 fa = __half22float2(hp[e]), fb = __half22float2(hq[e]);
-              hp[e] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+            for (int q = 0; q < 4; ++q) {
+              const float2 fa = __half22float2(hp[q]), fb = __half22float2(hq[q]);
+              hp[q] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
             }
           }
           const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(hp[e]);
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(hp[q]);
             ss += f.x * f.x + f.y * f.y;
           }
         }
         xr[c][j] = raw;
       }
     }
-    if (d.flags & AICAS_F_NORM) {
-      const float inv = rsqrtf(warp_sum(ss) / (float)k + d.eps);
+    if (flags & AICAS_F_NORM) {
+      const float inv = rsqrtf(warp_sum(ss) / (float)k + eps);
 #pragma unroll
-      for (int c = 0; c < kMaxChunks; ++c) {
+      for (int c = 0; c < C; ++c) {
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
           const int col = c * kChunk + j * 256 + lane * 8;
-          if (c < C && col < k) {
+          if (col < k) {
             const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
             __half2* hp = reinterpret_cast<__half2*>(&xr[c][j]);
             const __half2* wp = reinterpret_cast<const __half2*>(&wr);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(hp[e]);
-              const float2 g = __half22float2(wp[e]);
-              hp[e] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
+            for (int q = 0; q < 4; ++q) {
+              const float2 f = __half22float2(hp[q]);
+              const float2 g = __half22float2(wp[q]);
+              hp[q] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
             }
           }
         }
       }
     }
-    if ((d.flags & AICAS_F_STORE_X) && cta == 0 && w == 0 && d.x_out) {
+    if ((flags & AICAS_F_STORE_X) && cta == 0 && w == 0 && d.x_out) {
       __half* xo = reinterpret_cast<__half*>(d.x_out);
 #pragma unroll
-      for (int c = 0; c < kMaxChunks; ++c)
+      for (int c = 0; c < C; ++c)
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
           const int col = c * kChunk + j * 256 + lane * 8;
-          if (c < C && col < k) *reinterpret_cast<uint4*>(xo + col) = xr[c][j];
+          if (col < k) *reinterpret_cast<uint4*>(xo + col) = xr[c][j];
         }
     }
   }
@@ -444,28 +456,37 @@ struct Consumer {
     return lane_bits;
   }
 
-  // GEMV / GATEUP / LMHEAD phase.
-  __device__ void run_matvec(const AicasPhase& d) {
+  // GEMV / GATEUP / LMHEAD phase, C = number of 2048-column chunks of k.
+  template <int C>
+  __device__ __forceinline__ void matvec(const AicasPhase& d) {
     uint4 xr[kMaxChunks][kVec];
-    build_x(d, xr);
-    const int C = n_chunks(d);
-    const int G = (d.n + kRows - 1) / kRows;
-    const Range rg = split_range(G, nct, cta, d.rot);
-    const bool gateup = d.kind == AICAS_PH_GATEUP;
-    const bool lm = d.kind == AICAS_PH_LMHEAD;
-    const bool resid = d.flags & AICAS_F_RESID;
+    build_x<C>(d, xr);
+    // descriptor fields in registers (the waits below clobber memory)
+    const int n = d.n, k = d.k, flags = d.flags, kind = d.kind;
+    const bool gateup = kind == AICAS_PH_GATEUP;
+    const bool lm = kind == AICAS_PH_LMHEAD;
+    const bool resid = flags & AICAS_F_RESID;
+    const bool has_bias = flags & AICAS_F_BIAS;
+    __half* const out = reinterpret_cast<__half*>(d.out);
+    const __half* const bias = reinterpret_cast<const __half*>(d.bias);
+    const Range rg = split_range((n + kRows - 1) / kRows, nct, cta, d.rot);
+    const int row_stride = C == 1 ? k * 2 : kRowBytes;
+    // lanes whose columns of the last chunk lie beyond k skip them
+    const int last_len = k - (C - 1) * kChunk;
+    unsigned jvalid = 0;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) jvalid |= (j * 256 + lane * 8 < last_len ? 1u : 0u) << j;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     __half* logits = nullptr;
     if (lm && a.state && a.state->logits) {
       const int64_t ring = a.state->logits_ring > 0 ? a.state->logits_ring : 1;
-      logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * d.n;
+      logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * n;
     }
-    __half* out = reinterpret_cast<__half*>(d.out);
+    uint32_t it = r.it;
     for (int gi = 0; gi < rg.count; ++gi) {
-      const int g = rg.start + gi;
-      const int row = g * kRows + w;
-      const bool vrow = row < d.n;  // warp-uniform
+      const int row = (rg.start + gi) * kRows + w;
+      const bool vrow = row < n;  // warp-uniform
       float rv = 0.f;
       if (resid && lane == 0 && vrow) {
         if (gi < kResidPrefetch) {
@@ -476,40 +497,44 @@ struct Consumer {
           rv = resid_value(d, row);
         }
       }
-      float acc[2] = {0.f, 0.f};
+      float acc[2][4];
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[p][q] = 0.f;
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         if (part == 1 && !gateup) break;
 #pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) {
-          if (c < C) {
-            const int st = r.stage();
-            wait_full(st);
-            if (vrow) {
-              const uint8_t* base = sm.ring[st] + w * (C == 1 ? d.k * 2 : kRowBytes) + lane * 16;
+        for (int c = 0; c < C; ++c) {
+          const int st = it % kStages;
+          wait_full_at(st, it / kStages);
+          if (vrow) {
+            const uint8_t* base = sm.ring[st] + w * row_stride + lane * 16;
 #pragma unroll
-              for (int j = 0; j < kVec; ++j) {
-                if (c * kChunk + j * 256 + lane * 8 < d.k) {
-                  const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
-                  acc[part] = dot8_f16(wv, xr[c][j], acc[part]);
-                }
+            for (int j = 0; j < kVec; ++j) {
+              if (c < C - 1 || ((jvalid >> j) & 1u)) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
+                acc[part][j & 3] = dot8_f16(wv, xr[c][j], acc[part][j & 3]);
               }
             }
-            release(st);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.empty[st]);
+          ++it;
         }
       }
-      acc[0] = warp_sum(acc[0]);
-      if (gateup) acc[1] = warp_sum(acc[1]);
+      float sum0 = warp_sum((acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]));
+      float sum1 = 0.f;
+      if (gateup) sum1 = warp_sum((acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3]));
       if (lane == 0 && vrow) {
         if (gateup) {
-          const float gq = r16(acc[0]), uq = r16(acc[1]);
+          const float gq = r16(sum0), uq = r16(sum1);
           const float sl = r16(gq / (1.0f + expf(-gq)));
           out[row] = __float2half_rn(sl * uq);
         } else {
-          float sum = acc[0];
-          if (d.flags & AICAS_F_BIAS) sum += __half2float(reinterpret_cast<const __half*>(d.bias)[row]);
-          float y = r16(sum);
+          if (has_bias) sum0 += __half2float(bias[row]);
+          float y = r16(sum0);
           if (resid) y = r16(rv + y);
           if (lm) {
             if (logits) logits[row] = __float2half_rn(y);
@@ -524,10 +549,18 @@ struct Consumer {
         }
       }
     }
+    r.it = it;
     if (lm) finish_argmax(d, best_v, best_i);
   }
 
-  __device__ void finish_argmax(const AicasPhase& d, float bv, int bi) {
+  __device__ __forceinline__ void run_matvec(const AicasPhase& d) {
+    const int C = n_chunks(d);
+    if (C == 1) matvec<1>(d);
+    else if (C == 2) matvec<2>(d);
+    else matvec<3>(d);
+  }
+
+  __device__ __forceinline__ void finish_argmax(const AicasPhase& d, float bv, int bi) {
     if (lane == 0) {
       sm.best_v[w] = bv;
       sm.best_i[w] = bi;
@@ -589,7 +622,7 @@ struct Consumer {
   // One 128-dim head per warp (lane l holds dims 4l..4l+3): per-head RMSNorm
   // (modeling_qwen3_vl.py:398-403) and rotary embedding (:124-128, :427-431).
   // rotate_half's partner of dim d is d +- 64, held by lane l ^ 16.
-  __device__ void norm_rope_head(float (&v)[4], const __half* nw, float eps, const float (&cs)[4],
+  __device__ __forceinline__ void norm_rope_head(float (&v)[4], const __half* nw, float eps, const float (&cs)[4],
                                  const float (&sn)[4]) {
     float ss = 0.f;
 #pragma unroll
@@ -606,7 +639,7 @@ struct Consumer {
     }
   }
 
-  __device__ void run_attention(const AicasPhase& d) {
+  __device__ __forceinline__ void run_attention(const AicasPhase& d) {
     AttnSmem& at = sm.at;
     const bool q_ready = d.flags & AICAS_F_Q_READY;
     const int valid = phase_valid_len(d, in);
@@ -826,7 +859,7 @@ struct Consumer {
     }
   }
 
-  __device__ void run(const AicasPhase* P, int n_phases) {
+  __device__ __forceinline__ void run(const AicasPhase* P, int n_phases) {
     for (int ph = 0; ph < n_phases; ++ph) {
       const AicasPhase& d = P[ph];
       if (ph > 0) {
@@ -846,7 +879,7 @@ struct Consumer {
   }
 };
 
-__global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
+__global__ void __maxnreg__(224) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if (threadIdx.x == 0) {
