@@ -78,6 +78,8 @@ _I = ctypes.c_int
 SIGNATURES = {
     "aicas_abi_version": (_I, []),
     "aicas_error_string": (ctypes.c_char_p, [_I]),
+    "aicas_last_cuda_error": (_I, []),
+    "aicas_cuda_error_string": (ctypes.c_char_p, [_I]),
     "aicas_scratch_bytes": (ctypes.c_size_t, []),
     "aicas_layout_signature": (_I, [ctypes.POINTER(_I64), _I]),
     "aicas_num_ctas": (_I, [_I]),
@@ -125,7 +127,11 @@ def lib() -> ctypes.CDLL:
 
 def check(rc: int, what: str) -> None:
     if rc != 0:
-        msg = lib().aicas_error_string(rc).decode()
+        L = lib()
+        msg = L.aicas_error_string(rc).decode()
+        if rc == 4:  # AICAS_ERR_CUDA
+            ce = L.aicas_last_cuda_error()
+            msg += f": {L.aicas_cuda_error_string(ce).decode()} (cudaError {ce})"
         raise AicasError(f"{what} failed: {msg} (code {rc})")
 
 

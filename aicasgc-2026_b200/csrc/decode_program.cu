@@ -6,23 +6,25 @@
 //               async copies (cp.async.bulk + mbarrier complete_tx).  It never
 //               waits on a grid barrier, so HBM keeps streaming the next
 //               phase's weights while the consumers wait for activations.
-//   warps 1..8  consumers: per phase, wait on the grid barrier, build the input
+//   warps 1..4  consumers: per phase, wait on the grid barrier, build the input
 //               vector slice they need (RMSNorm prologue with HF's fp16 rounding
 //               points, computed by every warp on its own: no block sync), then
 //               reduce each tile row against it with exact fp16 products and
-//               fp32 accumulation.
+//               fp32 accumulation (two rows per warp, four independent
+//               accumulation chains per row).
 //
 // GEMV tile: 8 weight rows x 2048 columns (32 KB), fetched with ONE bulk copy
 // (rows are contiguous when k <= 2048; the engine stores down_proj K-blocked,
 // [k/2048][n][2048], so its tiles are contiguous too: bulk copies of 8 KB and
 // more are what reach full HBM bandwidth on B200, 2 KB copies top out near
-// 4 TB/s).  Consumer warp w owns row w of every tile; lane l the columns
+// 4 TB/s).  Consumer warp w owns rows w and w+4 of every tile; lane l the columns
 // j*256 + 8l (j = 0..7) of each 2048-column chunk, so a lane keeps its slice
 // of the input vector in registers for the whole phase, every weight byte is
 // read from shared memory exactly once (conflict-free 512-byte warp accesses)
 // and a row needs one warp reduction.
 //
-// Attention tile: K and V rows of 64 cache positions of one KV head (32 KB).
+// Attention tile: K and V rows of 64 cache positions of one KV head (32 KB),
+// 16 positions per consumer warp.
 // Work units (KV head, 32-position chunk) are split into contiguous ranges per
 // CTA; each CTA's segment of a head yields one (max, sum, acc) partial, and the
 // last CTA to finish a head (atomic arrival count) merges its partials in a
@@ -52,10 +54,11 @@
 
 namespace aicas {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 4;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kRows = kConsumerWarps;  // weight rows per GEMV tile: one per consumer warp
+constexpr int kThreads = kConsumerThreads + 32;  // 160: leaves up to 255 registers per thread
+constexpr int kRowsPerWarp = 2;
+constexpr int kRows = kConsumerWarps * kRowsPerWarp;  // weight rows per GEMV tile
 constexpr int kChunk = 2048;           // columns per GEMV tile
 constexpr int kRowBytes = kChunk * 2;
 constexpr int kStageBytes = kRows * kRowBytes;  // 32 KB: one bulk copy per tile
@@ -255,7 +258,7 @@ struct Consumer {
   uint64_t bar_base;
   uint32_t bar_k = 0;
   // residual rows of this warp's first groups of the coming phase
-  float rv_pre[kResidPrefetch];
+  float rv_pre[kResidPrefetch][kRowsPerWarp];
 
   // Waits never end the consumer loop early: after a failed (timed-out or
   // aborted) wait the CTA keeps walking the same program without waiting, so
@@ -334,10 +337,12 @@ struct Consumer {
     if ((d.flags & AICAS_F_RESID) && lane == 0) {
       const Range rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
 #pragma unroll
-      for (int i = 0; i < kResidPrefetch; ++i) {
-        const int row = (rg.start + i) * kRows + w;
-        rv_pre[i] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
-      }
+      for (int i = 0; i < kResidPrefetch; ++i)
+#pragma unroll
+        for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+          const int row = (rg.start + i) * kRows + rr * kConsumerWarps + w;
+          rv_pre[i][rr] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
+        }
     }
   }
 
@@ -485,23 +490,33 @@ struct Consumer {
     }
     uint32_t it = r.it;
     for (int gi = 0; gi < rg.count; ++gi) {
-      const int row = (rg.start + gi) * kRows + w;
-      const bool vrow = row < n;  // warp-uniform
-      float rv = 0.f;
-      if (resid && lane == 0 && vrow) {
-        if (gi < kResidPrefetch) {
+      // this warp's rows of the group: w and w + 4
+      int rows[kRowsPerWarp];
+      bool vrow[kRowsPerWarp];
+      float rv[kRowsPerWarp];
 #pragma unroll
-          for (int i = 0; i < kResidPrefetch; ++i)
-            if (i == gi) rv = rv_pre[i];
-        } else {
-          rv = resid_value(d, row);
+      for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+        rows[rr] = (rg.start + gi) * kRows + rr * kConsumerWarps + w;
+        vrow[rr] = rows[rr] < n;  // warp-uniform
+        rv[rr] = 0.f;
+        if (resid && lane == 0 && vrow[rr]) {
+          if (gi < kResidPrefetch) {
+#pragma unroll
+            for (int i = 0; i < kResidPrefetch; ++i)
+              if (i == gi) rv[rr] = rv_pre[i][rr];
+          } else {
+            rv[rr] = resid_value(d, rows[rr]);
+          }
         }
       }
-      float acc[2][4];
+      // acc[part][row][4 independent chains]
+      float acc[2][kRowsPerWarp][4];
 #pragma unroll
       for (int p = 0; p < 2; ++p)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) acc[p][q] = 0.f;
+        for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[p][rr][q] = 0.f;
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         if (part == 1 && !gateup) break;
@@ -509,13 +524,16 @@ struct Consumer {
         for (int c = 0; c < C; ++c) {
           const int st = it % kStages;
           wait_full_at(st, it / kStages);
-          if (vrow) {
-            const uint8_t* base = sm.ring[st] + w * row_stride + lane * 16;
 #pragma unroll
-            for (int j = 0; j < kVec; ++j) {
-              if (c < C - 1 || ((jvalid >> j) & 1u)) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
-                acc[part][j & 3] = dot8_f16(wv, xr[c][j], acc[part][j & 3]);
+          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+            if (vrow[rr]) {
+              const uint8_t* base = sm.ring[st] + (rr * kConsumerWarps + w) * row_stride + lane * 16;
+#pragma unroll
+              for (int j = 0; j < kVec; ++j) {
+                if (c < C - 1 || ((jvalid >> j) & 1u)) {
+                  const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
+                  acc[part][rr][j & 3] = dot8_f16(wv, xr[c][j], acc[part][rr][j & 3]);
+                }
               }
             }
           }
@@ -524,27 +542,32 @@ struct Consumer {
           ++it;
         }
       }
-      float sum0 = warp_sum((acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]));
-      float sum1 = 0.f;
-      if (gateup) sum1 = warp_sum((acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3]));
-      if (lane == 0 && vrow) {
-        if (gateup) {
-          const float gq = r16(sum0), uq = r16(sum1);
-          const float sl = r16(gq / (1.0f + expf(-gq)));
-          out[row] = __float2half_rn(sl * uq);
-        } else {
-          if (has_bias) sum0 += __half2float(bias[row]);
-          float y = r16(sum0);
-          if (resid) y = r16(rv + y);
-          if (lm) {
-            if (logits) logits[row] = __float2half_rn(y);
-            if (out) out[row] = __float2half_rn(y);
-            if (y > best_v) {  // this warp's rows ascend: strict > keeps the first max
-              best_v = y;
-              best_i = row;
-            }
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+        float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
+        float sum1 = 0.f;
+        if (gateup) sum1 = warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3]));
+        const int row = rows[rr];
+        if (lane == 0 && vrow[rr]) {
+          if (gateup) {
+            const float gq = r16(sum0), uq = r16(sum1);
+            const float sl = r16(gq / (1.0f + expf(-gq)));
+            out[row] = __float2half_rn(sl * uq);
           } else {
-            out[row] = __float2half_rn(y);
+            if (has_bias) sum0 += __half2float(bias[row]);
+            float y = r16(sum0);
+            if (resid) y = r16(rv[rr] + y);
+            if (lm) {
+              if (logits) logits[row] = __float2half_rn(y);
+              if (out) out[row] = __float2half_rn(y);
+              // this lane's rows ascend (row w before row w+4, groups ascend): strict > keeps the first max
+              if (y > best_v) {
+                best_v = y;
+                best_i = row;
+              }
+            } else {
+              out[row] = __float2half_rn(y);
+            }
           }
         }
       }
@@ -672,7 +695,6 @@ struct Consumer {
     }
     const float scale = d.scale;
     const int jpos = pos / kAttnChunk;
-    const int grp = tid / kHD, t = tid % kHD;
     // per-warp online-softmax state for the 2 query heads of the current KV head
     float m[2], l[2], acc[2][4];
     float qreg[2][4];
@@ -808,29 +830,33 @@ struct Consumer {
 #pragma unroll
           for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
         consumer_sync(kConsumerThreads);
-        float M = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][grp]);
-        float L = 0.f, A = 0.f;
-#pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) {
-          const float mi = at.wm[i][grp];
-          if (mi != -INFINITY) {
-            const float f = expf(mi - M);
-            L += at.wl[i][grp] * f;
-            A += at.wacc[i][grp][t] * f;
-          }
-        }
         const int first_owner = owner_of(h * cph, U, nct);
         const int last_owner = owner_of(h * cph + cph - 1, U, nct);
         const int split = cta - first_owner;
         const int nsplit = last_owner - first_owner + 1;
-        float* pp = &s->part[h][split][grp][0];
-        if (t == 0) {
-          pp[0] = M;
-          pp[1] = L;
+        const int t = tid;  // head dim; every thread handles dim t of both query heads
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          float M = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
+          float L = 0.f, A = 0.f;
+#pragma unroll
+          for (int i = 0; i < kConsumerWarps; ++i) {
+            const float mi = at.wm[i][g];
+            if (mi != -INFINITY) {
+              const float f = expf(mi - M);
+              L += at.wl[i][g] * f;
+              A += at.wacc[i][g][t] * f;
+            }
+          }
+          float* pp = &s->part[h][split][g][0];
+          if (t == 0) {
+            pp[0] = M;
+            pp[1] = L;
+          }
+          pp[2 + t] = A;
         }
-        pp[2 + t] = A;
         __threadfence();
         consumer_sync(kConsumerThreads);
         if (tid == 0) {
@@ -843,16 +869,19 @@ struct Consumer {
         }
         consumer_sync(kConsumerThreads);
         if (at.last) {
-          float Mg = -INFINITY;
-          for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, __ldcg(&s->part[h][sp][grp][0]));
-          float Lg = 0.f, Ag = 0.f;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float* q = &s->part[h][sp][grp][0];
-            const float f = expf(__ldcg(q) - Mg);
-            Lg += __ldcg(q + 1) * f;
-            Ag += __ldcg(q + 2 + t) * f;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            float Mg = -INFINITY;
+            for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, __ldcg(&s->part[h][sp][g][0]));
+            float Lg = 0.f, Ag = 0.f;
+            for (int sp = 0; sp < nsplit; ++sp) {
+              const float* q = &s->part[h][sp][g][0];
+              const float f = expf(__ldcg(q) - Mg);
+              Lg += __ldcg(q + 1) * f;
+              Ag += __ldcg(q + 2 + t) * f;
+            }
+            reinterpret_cast<__half*>(d.out)[(h * 2 + g) * kHD + t] = __float2half_rn(Ag / Lg);
           }
-          reinterpret_cast<__half*>(d.out)[(h * 2 + grp) * kHD + t] = __float2half_rn(Ag / Lg);
         }
         consumer_sync(kConsumerThreads);
       }
@@ -879,7 +908,7 @@ struct Consumer {
   }
 };
 
-__global__ void __maxnreg__(224) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if (threadIdx.x == 0) {
@@ -927,6 +956,12 @@ __global__ void __maxnreg__(224) decode_program_kernel(const __grid_constant__ P
 namespace aicas {
 
 static constexpr int kMaxDevices = 64;
+static thread_local int g_last_cuda_error = 0;
+
+static int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  return AICAS_ERR_CUDA;
+}
 static int g_attr_done[kMaxDevices];
 static int g_num_sms[kMaxDevices];
 static int g_cooperative = 1;
@@ -936,9 +971,13 @@ static int device_setup(int* dev_out) {
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
   if (!g_attr_done[dev]) {
-    if (cudaFuncSetAttribute(decode_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(Smem)) != cudaSuccess)
-      return AICAS_ERR_CUDA;
+    cudaError_t e = cudaFuncSetAttribute(decode_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(Smem));
+    if (e != cudaSuccess) return cuda_fail(e);
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_program_kernel, kThreads, sizeof(Smem));
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (per_sm < 1) return cuda_fail(cudaErrorLaunchOutOfResources);
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
     g_num_sms[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
@@ -1007,7 +1046,7 @@ static int launch_program(ProgramArgs& a, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, decode_program_kernel, a);
-  return e == cudaSuccess ? AICAS_OK : AICAS_ERR_CUDA;
+  return e == cudaSuccess ? AICAS_OK : cuda_fail(e);
 }
 
 
@@ -1018,6 +1057,10 @@ using namespace aicas;
 extern "C" {
 
 AICAS_API int aicas_abi_version(void) { return AICAS_ABI_VERSION; }
+
+AICAS_API int aicas_last_cuda_error(void) { return g_last_cuda_error; }
+
+AICAS_API const char* aicas_cuda_error_string(int err) { return cudaGetErrorString((cudaError_t)err); }
 
 AICAS_API size_t aicas_scratch_bytes(void) { return sizeof(AicasScratch); }
 

@@ -52,6 +52,10 @@ typedef struct CUstream_st* aicas_stream_t; /* == cudaStream_t */
 
 AICAS_API int aicas_abi_version(void);
 AICAS_API const char* aicas_error_string(int code);
+/* cudaError_t of the last AICAS_ERR_CUDA returned on this host thread, and
+ * its CUDA description. */
+AICAS_API int aicas_last_cuda_error(void);
+AICAS_API const char* aicas_cuda_error_string(int err);
 /* Bytes of the scratch block (sizeof(AicasScratch)). */
 AICAS_API size_t aicas_scratch_bytes(void);
 /* Struct sizes/offsets for binding checks; returns the number of values. */
