@@ -64,6 +64,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Variants addressed by 32-bit shared-window addresses (kept in registers by
+// the hot loops, so a memory clobber never forces them to be reloaded).
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive_s(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (bulk copy) accesses of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -121,6 +151,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (ld_volatile_int(&s->abort)) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, err);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait on the mbarrier at shared address `bar` (see mbar_wait_bounded).
+__device__ __forceinline__ bool mbar_wait_bounded_s(uint32_t bar, uint32_t parity, AicasScratch* s, int err) {
+  if (mbar_try_wait_s(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_s(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (ld_volatile_int(&s->abort)) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {

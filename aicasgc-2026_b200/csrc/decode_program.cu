@@ -79,6 +79,8 @@ struct AttnSmem {
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
+  float mm[AICAS_MAX_SPLITS][2];  // final merge: per-split max / sum
+  float ll[AICAS_MAX_SPLITS][2];
   int last;
 };
 
@@ -488,18 +490,26 @@ struct Consumer {
       const int64_t ring = a.state->logits_ring > 0 ? a.state->logits_ring : 1;
       logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * n;
     }
+    // everything the tile loop touches lives in registers
+    const uint32_t ring_s = smem_addr(&sm.ring[0][0]);
+    const uint32_t full_s = smem_addr(&sm.full[0]);
+    const uint32_t empty_s = smem_addr(&sm.empty[0]);
+    AicasScratch* const scr = s;
+    const int ln = lane, wp = w;
+    const bool timing = a.trace != nullptr && tid == 0;
+    uint64_t waited = 0;
     uint32_t it = r.it;
     for (int gi = 0; gi < rg.count; ++gi) {
-      // this warp's rows of the group: w and w + 4
+      // this warp's rows of the group: wp and wp + 4
       int rows[kRowsPerWarp];
       bool vrow[kRowsPerWarp];
       float rv[kRowsPerWarp];
 #pragma unroll
       for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-        rows[rr] = (rg.start + gi) * kRows + rr * kConsumerWarps + w;
+        rows[rr] = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
         vrow[rr] = rows[rr] < n;  // warp-uniform
         rv[rr] = 0.f;
-        if (resid && lane == 0 && vrow[rr]) {
+        if (resid && ln == 0 && vrow[rr]) {
           if (gi < kResidPrefetch) {
 #pragma unroll
             for (int i = 0; i < kResidPrefetch; ++i)
@@ -522,23 +532,29 @@ struct Consumer {
         if (part == 1 && !gateup) break;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
-          const int st = it % kStages;
-          wait_full_at(st, it / kStages);
+          const uint32_t st = it % kStages;
+          if (timing) {
+            const uint64_t t0 = globaltimer_ns();
+            mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
+            waited += globaltimer_ns() - t0;
+          } else {
+            mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
+          }
+          uint4 wv[kRowsPerWarp][kVec];
 #pragma unroll
           for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-            if (vrow[rr]) {
-              const uint8_t* base = sm.ring[st] + (rr * kConsumerWarps + w) * row_stride + lane * 16;
+            const uint32_t base = ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16;
 #pragma unroll
-              for (int j = 0; j < kVec; ++j) {
-                if (c < C - 1 || ((jvalid >> j) & 1u)) {
-                  const uint4 wv = *reinterpret_cast<const uint4*>(base + j * 512);
-                  acc[part][rr][j & 3] = dot8_f16(wv, xr[c][j], acc[part][rr][j & 3]);
-                }
-              }
-            }
+            for (int j = 0; j < kVec; ++j)
+              wv[rr][j] = (vrow[rr] && (c < C - 1 || ((jvalid >> j) & 1u))) ? lds_u4(base + j * 512)
+                                                                           : make_uint4(0, 0, 0, 0);
           }
+#pragma unroll
+          for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+            for (int j = 0; j < kVec; ++j) acc[part][rr][j & 3] = dot8_f16(wv[rr][j], xr[c][j], acc[part][rr][j & 3]);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[st]);
+          if (ln == 0) mbar_arrive_s(empty_s + st * 8);
           ++it;
         }
       }
@@ -548,7 +564,7 @@ struct Consumer {
         float sum1 = 0.f;
         if (gateup) sum1 = warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3]));
         const int row = rows[rr];
-        if (lane == 0 && vrow[rr]) {
+        if (ln == 0 && vrow[rr]) {
           if (gateup) {
             const float gq = r16(sum0), uq = r16(sum1);
             const float sl = r16(gq / (1.0f + expf(-gq)));
@@ -572,6 +588,7 @@ struct Consumer {
         }
       }
     }
+    wait_ns += waited;
     r.it = it;
     if (lm) finish_argmax(d, best_v, best_i);
   }
@@ -869,16 +886,32 @@ struct Consumer {
         }
         consumer_sync(kConsumerThreads);
         if (at.last) {
+          // (M, L) of every split into shared memory with one parallel round
+          // of loads, then per dim all splits' acc values (loads issued in
+          // batches of 8 before they are combined), combined in split order.
+          for (int i = tid; i < 2 * nsplit; i += kConsumerThreads) {
+            const int sp = i >> 1, g = i & 1;
+            at.mm[sp][g] = __ldcg(&s->part[h][sp][g][0]);
+            at.ll[sp][g] = __ldcg(&s->part[h][sp][g][1]);
+          }
+          consumer_sync(kConsumerThreads);
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
             float Mg = -INFINITY;
-            for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, __ldcg(&s->part[h][sp][g][0]));
+            for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, at.mm[sp][g]);
             float Lg = 0.f, Ag = 0.f;
-            for (int sp = 0; sp < nsplit; ++sp) {
-              const float* q = &s->part[h][sp][g][0];
-              const float f = expf(__ldcg(q) - Mg);
-              Lg += __ldcg(q + 1) * f;
-              Ag += __ldcg(q + 2 + t) * f;
+            for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
+              float av[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) av[q] = sp0 + q < nsplit ? __ldcg(&s->part[h][sp0 + q][g][2 + t]) : 0.f;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (sp0 + q < nsplit) {
+                  const float f = expf(at.mm[sp0 + q][g] - Mg);
+                  Lg += at.ll[sp0 + q][g] * f;
+                  Ag += av[q] * f;
+                }
+              }
             }
             reinterpret_cast<__half*>(d.out)[(h * 2 + g) * kHD + t] = __float2half_rn(Ag / Lg);
           }
