@@ -66,7 +66,6 @@ constexpr int kStages = 6;
 constexpr int kAttnChunk = 64;  // cache positions per attention tile
 constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
-constexpr int kMaxChunks = AICAS_MAX_K / kChunk;  // 3
 constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
 constexpr int kResidPrefetch = 4;                 // residual rows kept in registers per warp
 
@@ -146,6 +145,15 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
   return d.kind == AICAS_PH_GATEUP ? 2 * n_chunks(d) : n_chunks(d);
 }
 
+// Phases with k > 2048 and few row groups per CTA stream their tiles
+// chunk-major (all groups' chunk 0, then chunk 1, ...), so only one chunk of
+// the input vector is needed in fp32 registers at a time.  Producer and
+// consumers both call this to agree on the tile order.
+constexpr int kMaxCmajorGroups = 4;
+__device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
+  return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
+}
+
 // ---------------------------------------------------------------------------
 // Producer (warp 0, lane 0)
 // ---------------------------------------------------------------------------
@@ -203,27 +211,33 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
       const int T = tiles_per_group(d);
       const Range rg = split_range(G, nct, cta, d.rot);
       const __half* W = reinterpret_cast<const __half*>(d.w);
-      for (int g = rg.start; g < rg.start + rg.count && ok; ++g) {
+      auto issue = [&](int g, int t) -> bool {
+        const int st = r.stage();
+        if (!acquire(st)) return false;
         const int nrows = min(kRows, d.n - g * kRows);
-        for (int t = 0; t < T; ++t) {
-          const int st = r.stage();
-          if (!(ok = acquire(st))) break;
-          const int c = t % C;
-          const int row0 = g * kRows + (t >= C ? d.n : 0);
-          const int col0 = c * kChunk;
-          const uint32_t bytes = min(kChunk, d.k - col0) * 2;
-          mbar_arrive_expect_tx(&sm.full[st], nrows * bytes);
-          if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
-            bulk_g2s(sm.ring[st], W + (size_t)row0 * d.k, nrows * bytes, &sm.full[st], pol);
-          } else if (d.flags & AICAS_F_KBLOCKED) {  // block c of rows row0.. is contiguous
-            const int rows_total = d.kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
-            bulk_g2s(sm.ring[st], W + ((size_t)c * rows_total + row0) * kChunk, nrows * bytes, &sm.full[st], pol);
-          } else {  // row-major with k > 2048: one copy per row piece
-            for (int i = 0; i < nrows; ++i)
-              bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
-          }
-          ++r.it;
+        const int c = t % C;
+        const int row0 = g * kRows + (t >= C ? d.n : 0);
+        const int col0 = c * kChunk;
+        const uint32_t bytes = min(kChunk, d.k - col0) * 2;
+        mbar_arrive_expect_tx(&sm.full[st], nrows * bytes);
+        if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
+          bulk_g2s(sm.ring[st], W + (size_t)row0 * d.k, nrows * bytes, &sm.full[st], pol);
+        } else if (d.flags & AICAS_F_KBLOCKED) {  // block c of rows row0.. is contiguous
+          const int rows_total = d.kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
+          bulk_g2s(sm.ring[st], W + ((size_t)c * rows_total + row0) * kChunk, nrows * bytes, &sm.full[st], pol);
+        } else {  // row-major with k > 2048: one copy per row piece
+          for (int i = 0; i < nrows; ++i)
+            bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
         }
+        ++r.it;
+        return true;
+      };
+      if (chunk_major(C, d.kind, rg.count)) {
+        for (int c = 0; c < C && ok; ++c)
+          for (int g = rg.start; g < rg.start + rg.count && ok; ++g) ok = issue(g, c);
+      } else {
+        for (int g = rg.start; g < rg.start + rg.count && ok; ++g)
+          for (int t = 0; t < T && ok; ++t) ok = issue(g, t);
       }
     }
   }
@@ -348,16 +362,18 @@ struct Consumer {
     }
   }
 
-  // This warp's slice of the phase input vector, in registers:
+  // This warp's slice of the phase input vector:
   //   v = x (or the token's embedding row) [+ x2, rounded]; optionally
   //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
   // Every warp covers the whole vector across its lanes, so the sum of
   // squares is a warp reduction and no block synchronisation is needed.
+  // C == 1: the lane's 64 values stay in registers (x0).  C > 1: they go to
+  // sm.nw (each lane later reads back only what it wrote; all warps write
+  // the same values) -- the norm prologue is limited to k <= 2048.
   // Columns at or beyond k read as zero.
   template <int C>
-  __device__ __forceinline__ void build_x(const AicasPhase& d, uint4 (&xr)[kMaxChunks][kVec]) {
+  __device__ __forceinline__ void build_x(const AicasPhase& d, uint4 (&x0)[kVec]) {
     const int k = d.k, flags = d.flags;
-    const float eps = d.eps;
     const __half* x = reinterpret_cast<const __half*>(d.x);
     if (flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
     const __half* x2 = reinterpret_cast<const __half*>(d.x2);
@@ -380,33 +396,33 @@ struct Consumer {
               hp[q] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
             }
           }
-          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __half22float2(hp[q]);
-            ss += f.x * f.x + f.y * f.y;
-          }
-        }
-        xr[c][j] = raw;
-      }
-    }
-    if (flags & AICAS_F_NORM) {
-      const float inv = rsqrtf(warp_sum(ss) / (float)k + eps);
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-          const int col = c * kChunk + j * 256 + lane * 8;
-          if (col < k) {
-            const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
-            __half2* hp = reinterpret_cast<__half2*>(&xr[c][j]);
-            const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+          if (C == 1) {
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float2 f = __half22float2(hp[q]);
-              const float2 g = __half22float2(wp[q]);
-              hp[q] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
+              ss += f.x * f.x + f.y * f.y;
             }
+          }
+        }
+        if (C == 1) x0[j] = raw;
+        else if (col < k) *reinterpret_cast<uint4*>(&sm.nw[col]) = raw;
+      }
+    }
+    if (C == 1 && (flags & AICAS_F_NORM)) {
+      const float inv = rsqrtf(warp_sum(ss) / (float)k + d.eps);
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int col = j * 256 + lane * 8;
+        if (col < k) {
+          const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
+          __half2* hp = reinterpret_cast<__half2*>(&x0[j]);
+          const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(hp[q]);
+            const float2 g = __half22float2(wp[q]);
+            hp[q] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
           }
         }
       }
@@ -418,8 +434,19 @@ struct Consumer {
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
           const int col = c * kChunk + j * 256 + lane * 8;
-          if (col < k) *reinterpret_cast<uint4*>(xo + col) = xr[c][j];
+          if (col < k) *reinterpret_cast<uint4*>(xo + col) = C == 1 ? x0[j] : *reinterpret_cast<const uint4*>(&sm.nw[col]);
         }
+    }
+  }
+
+  // This lane's 8 fp16 x vectors of chunk c (registers for C == 1, else
+  // read back from sm.nw).
+  template <int C>
+  __device__ __forceinline__ void x_chunk(int c, int k, const uint4 (&x0)[kVec], uint4 (&xc)[kVec]) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int col = c * kChunk + j * 256 + lane * 8;
+      xc[j] = C == 1 ? x0[j] : (col < k ? *reinterpret_cast<const uint4*>(&sm.nw[col]) : make_uint4(0, 0, 0, 0));
     }
   }
 
@@ -463,34 +490,93 @@ struct Consumer {
     return lane_bits;
   }
 
+  // fp32 copy of this lane's 64 input values of chunk c (x stays fp16 in
+  // xr between chunks; conversion uses the packed f16x2 -> f32 path).
+  __device__ __forceinline__ static void x_to_f32(const uint4 (&xc)[kVec], float (&xf)[kVec * 8]) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const __half2* hp = reinterpret_cast<const __half2*>(&xc[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(hp[q]);
+        xf[j * 8 + 2 * q] = f.x;
+        xf[j * 8 + 2 * q + 1] = f.y;
+      }
+    }
+  }
+
+  // acc[0..3] += one tile row (this lane's 64 columns at shared address
+  // `row_s`) . xf; products exact (fp16 x fp16 in fp32), fp32 accumulation
+  // in 4 independent chains.  `jmask` skips columns beyond k.
+  __device__ __forceinline__ static void row_dot(uint32_t row_s, const float (&xf)[kVec * 8], float (&acc)[4],
+                                                 unsigned jmask) {
+    uint4 wv[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) wv[j] = ((jmask >> j) & 1u) ? lds_u4(row_s + j * 512) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const __half2* hp = reinterpret_cast<const __half2*>(&wv[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(hp[q]);
+        acc[j & 3] = fmaf(f.x, xf[j * 8 + 2 * q], acc[j & 3]);
+        acc[j & 3] = fmaf(f.y, xf[j * 8 + 2 * q + 1], acc[j & 3]);
+      }
+    }
+  }
+
+  // Epilogue of one output row (lane 0): rounding points of HF's fp16 path.
+  __device__ __forceinline__ void finish_row(int kind, int flags, int row, float sum0, float sum1, float rv,
+                                             __half* out, const __half* bias, __half* logits, float& best_v,
+                                             int& best_i) {
+    if (kind == AICAS_PH_GATEUP) {
+      const float gq = r16(sum0), uq = r16(sum1);
+      const float sl = r16(gq / (1.0f + expf(-gq)));
+      out[row] = __float2half_rn(sl * uq);
+      return;
+    }
+    if (flags & AICAS_F_BIAS) sum0 += __half2float(bias[row]);
+    float y = r16(sum0);
+    if (flags & AICAS_F_RESID) y = r16(rv + y);
+    if (kind == AICAS_PH_LMHEAD) {
+      if (logits) logits[row] = __float2half_rn(y);
+      if (out) out[row] = __float2half_rn(y);
+      // this lane's rows ascend (row w before row w+4, groups ascend): strict > keeps the first max
+      if (y > best_v) {
+        best_v = y;
+        best_i = row;
+      }
+    } else {
+      out[row] = __float2half_rn(y);
+    }
+  }
+
   // GEMV / GATEUP / LMHEAD phase, C = number of 2048-column chunks of k.
   template <int C>
   __device__ __forceinline__ void matvec(const AicasPhase& d) {
-    uint4 xr[kMaxChunks][kVec];
-    build_x<C>(d, xr);
+    uint4 x0[kVec];
+    build_x<C>(d, x0);
     // descriptor fields in registers (the waits below clobber memory)
     const int n = d.n, k = d.k, flags = d.flags, kind = d.kind;
     const bool gateup = kind == AICAS_PH_GATEUP;
-    const bool lm = kind == AICAS_PH_LMHEAD;
     const bool resid = flags & AICAS_F_RESID;
-    const bool has_bias = flags & AICAS_F_BIAS;
     __half* const out = reinterpret_cast<__half*>(d.out);
     const __half* const bias = reinterpret_cast<const __half*>(d.bias);
     const Range rg = split_range((n + kRows - 1) / kRows, nct, cta, d.rot);
     const int row_stride = C == 1 ? k * 2 : kRowBytes;
     // lanes whose columns of the last chunk lie beyond k skip them
     const int last_len = k - (C - 1) * kChunk;
-    unsigned jvalid = 0;
+    unsigned jlast = 0;
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) jvalid |= (j * 256 + lane * 8 < last_len ? 1u : 0u) << j;
+    for (int j = 0; j < kVec; ++j) jlast |= (j * 256 + lane * 8 < last_len ? 1u : 0u) << j;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     __half* logits = nullptr;
-    if (lm && a.state && a.state->logits) {
+    if (kind == AICAS_PH_LMHEAD && a.state && a.state->logits) {
       const int64_t ring = a.state->logits_ring > 0 ? a.state->logits_ring : 1;
       logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * n;
     }
-    // everything the tile loop touches lives in registers
+    // everything the tile loops touch lives in registers
     const uint32_t ring_s = smem_addr(&sm.ring[0][0]);
     const uint32_t full_s = smem_addr(&sm.full[0]);
     const uint32_t empty_s = smem_addr(&sm.empty[0]);
@@ -499,98 +585,123 @@ struct Consumer {
     const bool timing = a.trace != nullptr && tid == 0;
     uint64_t waited = 0;
     uint32_t it = r.it;
-    for (int gi = 0; gi < rg.count; ++gi) {
-      // this warp's rows of the group: wp and wp + 4
-      int rows[kRowsPerWarp];
-      bool vrow[kRowsPerWarp];
-      float rv[kRowsPerWarp];
-#pragma unroll
-      for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-        rows[rr] = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
-        vrow[rr] = rows[rr] < n;  // warp-uniform
-        rv[rr] = 0.f;
-        if (resid && ln == 0 && vrow[rr]) {
-          if (gi < kResidPrefetch) {
-#pragma unroll
-            for (int i = 0; i < kResidPrefetch; ++i)
-              if (i == gi) rv[rr] = rv_pre[i][rr];
-          } else {
-            rv[rr] = resid_value(d, rows[rr]);
-          }
-        }
+    auto take = [&](uint32_t& st) {
+      st = it % kStages;
+      if (timing) {
+        const uint64_t t0 = globaltimer_ns();
+        mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
+        waited += globaltimer_ns() - t0;
+      } else {
+        mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
       }
-      // acc[part][row][4 independent chains]
-      float acc[2][kRowsPerWarp][4];
+    };
+    auto give = [&](uint32_t st) {
+      __syncwarp();
+      if (ln == 0) mbar_arrive_s(empty_s + st * 8);
+      ++it;
+    };
+    auto resid_of = [&](int gi, int rr, int row) -> float {
+      if (!resid || ln != 0 || row >= n) return 0.f;
+      float v = 0.f;
+      if (gi < kResidPrefetch) {
 #pragma unroll
-      for (int p = 0; p < 2; ++p)
+        for (int i = 0; i < kResidPrefetch; ++i)
+          if (i == gi) v = rv_pre[i][rr];
+        return v;
+      }
+      return resid_value(d, row);
+    };
+    float xf[kVec * 8];
+    if (chunk_major(C, kind, rg.count)) {
+      float acc[kMaxCmajorGroups][kRowsPerWarp][4];
+#pragma unroll
+      for (int g = 0; g < kMaxCmajorGroups; ++g)
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[p][rr][q] = 0.f;
+          for (int q = 0; q < 4; ++q) acc[g][rr][q] = 0.f;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        if (part == 1 && !gateup) break;
+      for (int c = 0; c < C; ++c) {
+        {
+          uint4 xc[kVec];
+          x_chunk<C>(c, k, x0, xc);
+          x_to_f32(xc, xf);
+        }
+        const unsigned jmask = c < C - 1 ? 0xffu : jlast;
 #pragma unroll
-        for (int c = 0; c < C; ++c) {
-          const uint32_t st = it % kStages;
-          if (timing) {
-            const uint64_t t0 = globaltimer_ns();
-            mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
-            waited += globaltimer_ns() - t0;
-          } else {
-            mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
+        for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
+          if (gi < rg.count) {
+            uint32_t st;
+            take(st);
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+              const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+              if (row < n)
+                row_dot(ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16, xf,
+                        acc[gi][rr], jmask);
+            }
+            give(st);
           }
-          uint4 wv[kRowsPerWarp][kVec];
-#pragma unroll
-          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-            const uint32_t base = ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16;
-#pragma unroll
-            for (int j = 0; j < kVec; ++j)
-              wv[rr][j] = (vrow[rr] && (c < C - 1 || ((jvalid >> j) & 1u))) ? lds_u4(base + j * 512)
-                                                                           : make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int rr = 0; rr < kRowsPerWarp; ++rr)
-#pragma unroll
-            for (int j = 0; j < kVec; ++j) acc[part][rr][j & 3] = dot8_f16(wv[rr][j], xr[c][j], acc[part][rr][j & 3]);
-          __syncwarp();
-          if (ln == 0) mbar_arrive_s(empty_s + st * 8);
-          ++it;
         }
       }
 #pragma unroll
-      for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-        float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
-        float sum1 = 0.f;
-        if (gateup) sum1 = warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3]));
-        const int row = rows[rr];
-        if (ln == 0 && vrow[rr]) {
-          if (gateup) {
-            const float gq = r16(sum0), uq = r16(sum1);
-            const float sl = r16(gq / (1.0f + expf(-gq)));
-            out[row] = __float2half_rn(sl * uq);
-          } else {
-            if (has_bias) sum0 += __half2float(bias[row]);
-            float y = r16(sum0);
-            if (resid) y = r16(rv[rr] + y);
-            if (lm) {
-              if (logits) logits[row] = __float2half_rn(y);
-              if (out) out[row] = __float2half_rn(y);
-              // this lane's rows ascend (row w before row w+4, groups ascend): strict > keeps the first max
-              if (y > best_v) {
-                best_v = y;
-                best_i = row;
-              }
-            } else {
-              out[row] = __float2half_rn(y);
-            }
+      for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
+        if (gi < rg.count) {
+#pragma unroll
+          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+            const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+            const float rv = resid_of(gi, rr, row);
+            const float sum = warp_sum((acc[gi][rr][0] + acc[gi][rr][1]) + (acc[gi][rr][2] + acc[gi][rr][3]));
+            if (ln == 0 && row < n) finish_row(kind, flags, row, sum, 0.f, rv, out, bias, logits, best_v, best_i);
           }
+        }
+      }
+    } else {
+      if (C == 1) x_to_f32(x0, xf);
+      for (int gi = 0; gi < rg.count; ++gi) {
+        float acc[2][kRowsPerWarp][4];
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[p][rr][q] = 0.f;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          if (part == 1 && !gateup) break;
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            if (C > 1) {
+              uint4 xc[kVec];
+              x_chunk<C>(c, k, x0, xc);
+              x_to_f32(xc, xf);
+            }
+            const unsigned jmask = c < C - 1 ? 0xffu : jlast;
+            uint32_t st;
+            take(st);
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+              const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+              if (row < n)
+                row_dot(ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16, xf,
+                        acc[part][rr], jmask);
+            }
+            give(st);
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+          const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+          const float rv = resid_of(gi, rr, row);
+          const float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
+          const float sum1 = gateup ? warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3])) : 0.f;
+          if (ln == 0 && row < n) finish_row(kind, flags, row, sum0, sum1, rv, out, bias, logits, best_v, best_i);
         }
       }
     }
     wait_ns += waited;
     r.it = it;
-    if (lm) finish_argmax(d, best_v, best_i);
+    if (kind == AICAS_PH_LMHEAD) finish_argmax(d, best_v, best_i);
   }
 
   __device__ __forceinline__ void run_matvec(const AicasPhase& d) {
@@ -1032,6 +1143,7 @@ static int validate_phase(const AicasPhase& d) {
       if (!d.x || !aligned16(d.x)) return AICAS_ERR_ALIGN;
       if ((d.flags & AICAS_F_X_ADD) && (!d.x2 || !aligned16(d.x2))) return AICAS_ERR_ALIGN;
       if ((d.flags & AICAS_F_NORM) && (!d.norm_w || !aligned16(d.norm_w))) return AICAS_ERR_ALIGN;
+      if ((d.flags & AICAS_F_NORM) && d.k > 2048) return AICAS_ERR_SHAPE;  // norm prologue: k <= 2048
       if ((d.flags & (AICAS_F_X_EMBED | AICAS_F_RESID_EMBED)) && d.embed_rows < 1) return AICAS_ERR_ARG;
       if ((d.flags & AICAS_F_RESID) && !d.resid) return AICAS_ERR_ARG;
       if ((d.flags & AICAS_F_RESID_ADD) && !d.resid2) return AICAS_ERR_ARG;
