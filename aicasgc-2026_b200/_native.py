@@ -26,6 +26,10 @@ F_RESID_ADD = 1 << 6
 F_Q_READY = 1 << 7
 F_STORE_X = 1 << 8
 F_KBLOCKED = 1 << 9
+F_BARRIER = 1 << 10
+F_LL_IN = 1 << 11
+F_LL_OUT = 1 << 12
+F_LL_RESID = 1 << 13
 
 DEVICE_ERRORS = {
     10: "grid barrier timed out",
@@ -45,7 +49,7 @@ class AicasPhase(ctypes.Structure):
     _fields_ = [
         ("kind", ctypes.c_int32), ("flags", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
         ("rot", ctypes.c_int32), ("kv_heads", ctypes.c_int32), ("q_heads", ctypes.c_int32),
-        ("max_len", ctypes.c_int32), ("embed_rows", ctypes.c_int32), ("pad1", ctypes.c_int32),
+        ("max_len", ctypes.c_int32), ("embed_rows", ctypes.c_int32), ("x_src", ctypes.c_int32),
         ("w", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_w2", ctypes.c_void_p),
         ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("resid", ctypes.c_void_p),
         ("resid2", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),

@@ -19,6 +19,7 @@ enum : int {
   kErrDrainTimeout = 13,     // in-flight copies did not land before exit
   kErrBadPhase = 14,         // unknown phase kind / bad descriptor
   kErrBadInput = 15,         // token id or cache position out of range
+  kErrInputTimeout = 16,     // an LL input vector did not arrive in time
 };
 
 // Wait limit: two seconds of %globaltimer.  Far above any legal phase time
@@ -229,6 +230,72 @@ __device__ __forceinline__ bool grid_wait(AicasScratch* s, uint64_t target) {
       }
     }
   }
+}
+
+// LL vectors (aicas_phase_program.h): 64-bit words {half2 data, uint32 epoch}.
+__device__ __forceinline__ void ll_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ll_load1(const uint64_t* p) {
+  uint64_t a;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+
+__device__ __forceinline__ void ll_store(uint64_t* p, uint32_t data, uint32_t epoch) {
+  const uint64_t v = ((uint64_t)epoch << 32) | data;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Bounded poll of the 4 LL words holding 8 fp16 values starting at value
+// index `col` (col % 8 == 0); returns them packed.  On timeout or abort the
+// error is recorded and whatever was read last is returned.
+__device__ __forceinline__ uint4 ll_poll8(const uint64_t* words, int col, uint32_t epoch, AicasScratch* s) {
+  const uint64_t* p = words + col / 2;
+  uint64_t w0, w1, w2, w3;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    ll_load2(p, w0, w1);
+    ll_load2(p + 2, w2, w3);
+    if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch && (uint32_t)(w2 >> 32) == epoch &&
+        (uint32_t)(w3 >> 32) == epoch)
+      break;
+    if (it == 0) t0 = globaltimer_ns();
+    if ((it & 31u) == 31u) {
+      if (ld_volatile_int(&s->abort)) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrInputTimeout);
+        break;
+      }
+    }
+  }
+  return make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
+}
+
+// Same for the 2 words holding 4 fp16 values at `col` (col % 4 == 0).
+__device__ __forceinline__ uint2 ll_poll4(const uint64_t* words, int col, uint32_t epoch, AicasScratch* s) {
+  const uint64_t* p = words + col / 2;
+  uint64_t w0, w1;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    ll_load2(p, w0, w1);
+    if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch) break;
+    if (it == 0) t0 = globaltimer_ns();
+    if ((it & 31u) == 31u) {
+      if (ld_volatile_int(&s->abort)) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrInputTimeout);
+        break;
+      }
+    }
+  }
+  return make_uint2((uint32_t)w0, (uint32_t)w1);
 }
 
 // fp16 helpers -------------------------------------------------------------

@@ -273,6 +273,8 @@ struct Consumer {
   Ring r;
   uint64_t bar_base;
   uint32_t bar_k = 0;
+  uint32_t epoch_base;  // LL epoch of phase p = epoch_base + p + 1
+  int ph = 0;           // running phase index
   // residual rows of this warp's first groups of the coming phase
   float rv_pre[kResidPrefetch][kRowsPerWarp];
 
@@ -325,6 +327,11 @@ struct Consumer {
   }
 
   __device__ __forceinline__ float resid_value(const AicasPhase& d, int row) {
+    if (d.flags & AICAS_F_LL_RESID) {  // complete before this phase: data only
+      const uint32_t bits = (uint32_t)ll_load1(reinterpret_cast<const uint64_t*>(d.resid) + row / 2);
+      const __half2 h2 = *reinterpret_cast<const __half2*>(&bits);
+      return (row & 1) ? __high2float(h2) : __low2float(h2);
+    }
     const __half* rp = reinterpret_cast<const __half*>(d.resid);
     if (d.flags & AICAS_F_RESID_EMBED) rp += (size_t)checked_token(d) * d.n;
     float rv = ldcg_half(rp + row);
@@ -356,7 +363,7 @@ struct Consumer {
       for (int i = 0; i < kResidPrefetch; ++i)
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = (rg.start + i) * kRows + rr * kConsumerWarps + w;
+          const int row = (rg.start + i) * kRows + 2 * w + rr;
           rv_pre[i][rr] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
         }
     }
@@ -377,6 +384,9 @@ struct Consumer {
     const __half* x = reinterpret_cast<const __half*>(d.x);
     if (flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
     const __half* x2 = reinterpret_cast<const __half*>(d.x2);
+    const bool ll = flags & AICAS_F_LL_IN;
+    const uint64_t* xw = reinterpret_cast<const uint64_t*>(d.x);
+    const uint32_t x_epoch = epoch_base + (uint32_t)d.x_src + 1;
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
@@ -384,8 +394,9 @@ struct Consumer {
       for (int j = 0; j < kVec; ++j) {
         const int col = c * kChunk + j * 256 + lane * 8;
         uint4 raw = make_uint4(0, 0, 0, 0);
-        if (col < k) {
-          raw = ldcg_u4(x + col);
+        // C > 1: the 4 warps split the columns and share them through sm.nw
+        if (col < k && (C == 1 || (c * kVec + j) % kConsumerWarps == w)) {
+          raw = ll ? ll_poll8(xw, col, x_epoch, s) : ldcg_u4(x + col);
           if (flags & AICAS_F_X_ADD) {
             const uint4 raw2 = ldcg_u4(x2 + col);
             __half2* hp = reinterpret_cast<__half2*>(&raw);
@@ -406,9 +417,10 @@ struct Consumer {
           }
         }
         if (C == 1) x0[j] = raw;
-        else if (col < k) *reinterpret_cast<uint4*>(&sm.nw[col]) = raw;
+        else if (col < k && (c * kVec + j) % kConsumerWarps == w) *reinterpret_cast<uint4*>(&sm.nw[col]) = raw;
       }
     }
+    if (C > 1) consumer_sync(kConsumerThreads);
     if (C == 1 && (flags & AICAS_F_NORM)) {
       const float inv = rsqrtf(warp_sum(ss) / (float)k + d.eps);
 #pragma unroll
@@ -525,29 +537,39 @@ struct Consumer {
     }
   }
 
-  // Epilogue of one output row (lane 0): rounding points of HF's fp16 path.
-  __device__ __forceinline__ void finish_row(int kind, int flags, int row, float sum0, float sum1, float rv,
-                                             __half* out, const __half* bias, __half* logits, float& best_v,
-                                             int& best_i) {
+  // Output value of one row (lane 0) with the rounding points of HF's fp16
+  // path; the LM head also stores the logit and updates the running argmax.
+  __device__ __forceinline__ static float row_value(int kind, int flags, int row, float sum0, float sum1, float rv,
+                                                    const __half* bias, __half* logits, float& best_v, int& best_i) {
     if (kind == AICAS_PH_GATEUP) {
       const float gq = r16(sum0), uq = r16(sum1);
       const float sl = r16(gq / (1.0f + expf(-gq)));
-      out[row] = __float2half_rn(sl * uq);
-      return;
+      return r16(sl * uq);
     }
     if (flags & AICAS_F_BIAS) sum0 += __half2float(bias[row]);
     float y = r16(sum0);
     if (flags & AICAS_F_RESID) y = r16(rv + y);
     if (kind == AICAS_PH_LMHEAD) {
       if (logits) logits[row] = __float2half_rn(y);
-      if (out) out[row] = __float2half_rn(y);
-      // this lane's rows ascend (row w before row w+4, groups ascend): strict > keeps the first max
+      // this lane's rows ascend (row 2w before 2w+1, groups ascend): strict > keeps the first max
       if (y > best_v) {
         best_v = y;
         best_i = row;
       }
+    }
+    return y;
+  }
+
+  // Lane 0 stores the warp's two adjacent output rows (row0, row0 + 1):
+  // one LL word, or plain fp16 stores.
+  __device__ __forceinline__ void store_pair(int flags, int n, int row0, float y0, float y1, __half* out) {
+    if (!out) return;
+    if (flags & AICAS_F_LL_OUT) {
+      ll_store(reinterpret_cast<uint64_t*>(out) + row0 / 2, half2_bits(y0, row0 + 1 < n ? y1 : 0.f),
+               epoch_base + (uint32_t)ph + 1);
     } else {
-      out[row] = __float2half_rn(y);
+      out[row0] = __float2half_rn(y0);
+      if (row0 + 1 < n) out[row0 + 1] = __float2half_rn(y1);
     }
   }
 
@@ -635,9 +657,9 @@ struct Consumer {
             take(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+              const int row = (rg.start + gi) * kRows + 2 * wp + rr;
               if (row < n)
-                row_dot(ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16, xf,
+                row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
                         acc[gi][rr], jmask);
             }
             give(st);
@@ -647,13 +669,17 @@ struct Consumer {
 #pragma unroll
       for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
         if (gi < rg.count) {
+          float y[kRowsPerWarp];
+          const int row0 = (rg.start + gi) * kRows + 2 * wp;
 #pragma unroll
           for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-            const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+            const int row = row0 + rr;
             const float rv = resid_of(gi, rr, row);
             const float sum = warp_sum((acc[gi][rr][0] + acc[gi][rr][1]) + (acc[gi][rr][2] + acc[gi][rr][3]));
-            if (ln == 0 && row < n) finish_row(kind, flags, row, sum, 0.f, rv, out, bias, logits, best_v, best_i);
+            y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum, 0.f, rv, bias, logits, best_v, best_i)
+                                         : 0.f;
           }
+          if (ln == 0 && row0 < n) store_pair(flags, n, row0, y[0], y[1], out);
         }
       }
     } else {
@@ -681,22 +707,26 @@ struct Consumer {
             take(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+              const int row = (rg.start + gi) * kRows + 2 * wp + rr;
               if (row < n)
-                row_dot(ring_s + st * kStageBytes + (rr * kConsumerWarps + wp) * row_stride + ln * 16, xf,
+                row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
                         acc[part][rr], jmask);
             }
             give(st);
           }
         }
+        float y[kRowsPerWarp];
+        const int row0 = (rg.start + gi) * kRows + 2 * wp;
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = (rg.start + gi) * kRows + rr * kConsumerWarps + wp;
+          const int row = row0 + rr;
           const float rv = resid_of(gi, rr, row);
           const float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
           const float sum1 = gateup ? warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3])) : 0.f;
-          if (ln == 0 && row < n) finish_row(kind, flags, row, sum0, sum1, rv, out, bias, logits, best_v, best_i);
+          y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum0, sum1, rv, bias, logits, best_v, best_i)
+                                       : 0.f;
         }
+        if (ln == 0 && row0 < n) store_pair(flags, n, row0, y[0], y[1], out);
       }
     }
     wait_ns += waited;
@@ -803,6 +833,9 @@ struct Consumer {
     const int U = d.kv_heads * cph;
     const Range rg = split_range(U, nct, cta, 0);
     const __half* qkv = reinterpret_cast<const __half*>(d.x);
+    const bool ll_in = d.flags & AICAS_F_LL_IN;
+    const uint64_t* qkv_w = reinterpret_cast<const uint64_t*>(d.x);
+    const uint32_t x_epoch = epoch_base + (uint32_t)d.x_src + 1;
     __half* kc = reinterpret_cast<__half*>(d.k_cache);
     __half* vc = reinterpret_cast<__half*>(d.v_cache);
     const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
@@ -834,7 +867,8 @@ struct Consumer {
         const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
         const bool has_pos = !q_ready && jpos >= j && jpos <= last_j;
         if (w < 2) {  // query heads 2h, 2h+1
-          const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(qkv + (h * 2 + w) * kHD + lane * 4));
+          const int col = (h * 2 + w) * kHD + lane * 4;
+          const uint2 raw = ll_in ? ll_poll4(qkv_w, col, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + col));
           const __half2* hp = reinterpret_cast<const __half2*>(&raw);
           float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
           if (!q_ready) norm_rope_head(v, sm.nw, d.eps, cs, sn);
@@ -842,7 +876,7 @@ struct Consumer {
           for (int e = 0; e < 4; ++e) at.q[w][lane * 4 + e] = v[e];
         } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
           const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
-          const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(qkv + off));
+          const uint2 raw = ll_in ? ll_poll4(qkv_w, off, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + off));
           const __half2* hp = reinterpret_cast<const __half2*>(&raw);
           float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
           if (w == 2) norm_rope_head(v, sm.nw + kHD, d.eps, cs, sn);
@@ -1006,25 +1040,35 @@ struct Consumer {
             at.ll[sp][g] = __ldcg(&s->part[h][sp][g][1]);
           }
           consumer_sync(kConsumerThreads);
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
+          {
+            // thread t: query head 2h + g, dims dd and dd + 1 (one LL word)
+            const int g = t / (kHD / 2), dd = 2 * (t % (kHD / 2));
             float Mg = -INFINITY;
             for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, at.mm[sp][g]);
-            float Lg = 0.f, Ag = 0.f;
+            float Lg = 0.f, A0 = 0.f, A1 = 0.f;
             for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
-              float av[8];
+              float2 av[8];
 #pragma unroll
-              for (int q = 0; q < 8; ++q) av[q] = sp0 + q < nsplit ? __ldcg(&s->part[h][sp0 + q][g][2 + t]) : 0.f;
+              for (int q = 0; q < 8; ++q)
+                av[q] = sp0 + q < nsplit ? __ldcg(reinterpret_cast<const float2*>(&s->part[h][sp0 + q][g][2 + dd]))
+                                         : make_float2(0.f, 0.f);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 if (sp0 + q < nsplit) {
                   const float f = expf(at.mm[sp0 + q][g] - Mg);
                   Lg += at.ll[sp0 + q][g] * f;
-                  Ag += av[q] * f;
+                  A0 += av[q].x * f;
+                  A1 += av[q].y * f;
                 }
               }
             }
-            reinterpret_cast<__half*>(d.out)[(h * 2 + g) * kHD + t] = __float2half_rn(Ag / Lg);
+            const int o = (h * 2 + g) * kHD + dd;
+            if (d.flags & AICAS_F_LL_OUT) {
+              ll_store(reinterpret_cast<uint64_t*>(d.out) + o / 2, half2_bits(A0 / Lg, A1 / Lg),
+                       epoch_base + (uint32_t)ph + 1);
+            } else {
+              reinterpret_cast<__half2*>(d.out)[o / 2] = __floats2half2_rn(A0 / Lg, A1 / Lg);
+            }
           }
         }
         consumer_sync(kConsumerThreads);
@@ -1033,21 +1077,29 @@ struct Consumer {
   }
 
   __device__ __forceinline__ void run(const AicasPhase* P, int n_phases) {
-    for (int ph = 0; ph < n_phases; ++ph) {
+    for (ph = 0; ph < n_phases; ++ph) {
       const AicasPhase& d = P[ph];
-      if (ph > 0) {
-        consumer_sync(kConsumerThreads);  // every warp's outputs of phase ph-1 are written
-        if (tid == 0) grid_arrive(s);
-      }
+      // every warp is done with the previous phase's shared buffers
+      consumer_sync(kConsumerThreads);
+      const bool barrier = ph > 0 && (d.flags & AICAS_F_BARRIER);
+      if (barrier && tid == 0) grid_arrive(s);
       prefetch(d);
-      if (ph > 0) {
-        if (tid == 0) grid_wait(s, bar_base + (uint64_t)(++bar_k) * nct);
-      }
-      consumer_sync(kConsumerThreads);  // barrier passed; prefetched norm weights visible
+      if (barrier && tid == 0) grid_wait(s, bar_base + (uint64_t)(++bar_k) * nct);
+      consumer_sync(kConsumerThreads);  // prefetched norm weights visible; barrier passed
       stamp(ph, 0);
       if (d.kind == AICAS_PH_ATTN) run_attention(d);
       else run_matvec(d);
       stamp(ph, 1);
+    }
+    // the last CTA to finish moves the LL epoch base past this launch
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(&s->exit_count, 1u) == (uint32_t)nct - 1) {
+        s->exit_count = 0;
+        s->epoch = epoch_base + (uint32_t)n_phases + 1;
+        __threadfence();
+      }
     }
   }
 };
@@ -1087,6 +1139,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   c.cta = blockIdx.x;
   const uint64_t now = ld_relaxed_u64(&a.scratch->bar_count);
   c.bar_base = now - now % (uint64_t)gridDim.x;
+  c.epoch_base = *reinterpret_cast<volatile uint32_t*>(&a.scratch->epoch);
   c.run(P, a.n_phases);
 }
 
@@ -1152,6 +1205,8 @@ static int validate_phase(const AicasPhase& d) {
       if (d.kind != AICAS_PH_LMHEAD && !d.out) return AICAS_ERR_ARG;
       if (d.kind == AICAS_PH_GATEUP && (d.flags & (AICAS_F_RESID | AICAS_F_BIAS))) return AICAS_ERR_ARG;
       if ((d.flags & AICAS_F_KBLOCKED) && d.k % 2048 != 0) return AICAS_ERR_SHAPE;
+      if ((d.flags & AICAS_F_LL_IN) && ((d.flags & (AICAS_F_X_ADD | AICAS_F_X_EMBED)) || d.x_src < 0))
+        return AICAS_ERR_ARG;
       return AICAS_OK;
     case AICAS_PH_ATTN:
       if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
@@ -1159,6 +1214,7 @@ static int validate_phase(const AicasPhase& d) {
       if (!d.k_cache || !d.v_cache || !aligned16(d.k_cache) || !aligned16(d.v_cache)) return AICAS_ERR_ALIGN;
       if (!d.x || !d.out) return AICAS_ERR_ARG;
       if (!(d.flags & AICAS_F_Q_READY) && (!d.norm_w || !d.norm_w2)) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_LL_IN) && ((d.flags & AICAS_F_Q_READY) || d.x_src < 0)) return AICAS_ERR_ARG;
       return AICAS_OK;
     default:
       return AICAS_ERR_ARG;
@@ -1354,6 +1410,7 @@ AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out
   dn.resid2 = attn_out;
   dn.bias = bias;
   dn.out = out;
+  dn.flags |= AICAS_F_BARRIER;  // act comes from the gate_up phase of this launch
   dn.rot = 37;  // the down sweep's extra row groups land on other CTAs than gate_up's
   a.n_phases = 2;
   a.scratch = reinterpret_cast<AicasScratch*>(scratch);

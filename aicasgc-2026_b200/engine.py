@@ -29,8 +29,9 @@ import math
 
 import torch
 
-from _native import (F_KBLOCKED, F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED, PH_ATTN, PH_GATEUP, PH_GEMV,
-                     PH_LMHEAD, AicasError, AicasPhase, AicasStepState, check, lib, scratch_bytes)
+from _native import (F_KBLOCKED, F_LL_IN, F_LL_OUT, F_LL_RESID, F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED,
+                     PH_ATTN, PH_GATEUP, PH_GEMV, PH_LMHEAD, AicasError, AicasPhase, AicasStepState, check, lib,
+                     scratch_bytes)
 from _ops import device_error
 from qwen3vl_config import QWEN3VL_2B, Qwen3VLTextShape
 
@@ -94,11 +95,13 @@ class Qwen3VLDecodeEngine:
             kv_shape = (s.num_layers, 1, s.num_kv_heads, max_cache_len, s.head_dim)
             self.k_cache = torch.zeros(kv_shape, **f16)
             self.v_cache = torch.zeros(kv_shape, **f16)
-            self.h = torch.zeros(s.hidden, **f16)
-            self.h_mid = torch.zeros(s.hidden, **f16)
-            self.qkv = torch.zeros(s.qkv_rows, **f16)
-            self.attn = torch.zeros(s.q_size, **f16)
-            self.act = torch.zeros(s.intermediate, **f16)
+            # activations between phases as LL vectors: word i = {fp16 pair (2i, 2i+1), epoch}
+            ll = dict(dtype=torch.int64, device=dev)
+            self.h = torch.zeros(s.hidden // 2, **ll)
+            self.h_mid = torch.zeros(s.hidden // 2, **ll)
+            self.qkv = torch.zeros(s.qkv_rows // 2, **ll)
+            self.attn = torch.zeros(s.q_size // 2, **ll)
+            self.act = torch.zeros(s.intermediate // 2, **ll)
             self.out_tokens = torch.full((max_steps,), -1, dtype=torch.int64, device=dev)
             self.logits_ring = int(logits_ring)
             self.logits = (torch.zeros((logits_ring, s.vocab), **f16) if logits_ring > 0 else None)
@@ -116,6 +119,12 @@ class Qwen3VLDecodeEngine:
 
     # ------------------------------------------------------------------ program
     def _build_program(self):
+        """28 x [QKV, ATTN, O_PROJ, GATE_UP, DOWN] + LM_HEAD.  Activations flow
+        through LL vectors (each phase polls exactly the words it consumes),
+        so the program has no grid barrier at all.  Reusing one buffer per
+        vector is safe because every GEMV phase gives every CTA rows to
+        compute (checked below) and each GEMV consumes a whole vector: no CTA
+        can write a buffer again before every CTA has consumed it."""
         s, nct = self.shape, self.num_ctas
         eps = float(s.rms_eps)
         phases = []
@@ -124,40 +133,49 @@ class Qwen3VLDecodeEngine:
         def ptr(t):
             return t.data_ptr()
 
-        def gemv_like(kind, flags, n, k, w, x, out, norm_w=None, resid=None):
+        def gemv_like(kind, flags, n, k, w, x, out, norm_w=None, resid=None, x_src=-1):
             nonlocal extra
+            groups = -(-n // 8)
+            if groups < nct:
+                raise AicasError(f"phase with {groups} row groups < {nct} CTAs breaks LL buffer reuse")
             p = AicasPhase()
             p.kind, p.flags, p.n, p.k = kind, flags, n, k
             p.rot = extra % nct
-            groups = -(-n // 8)
             extra += groups % nct
-            p.w, p.x, p.out = ptr(w), ptr(x), ptr(out)
+            p.w, p.x = ptr(w), ptr(x)
+            p.out = ptr(out) if out is not None else None
             p.norm_w = ptr(norm_w) if norm_w is not None else None
             p.resid = ptr(resid) if resid is not None else None
             p.embed_rows = s.vocab
+            p.x_src = x_src
             p.eps = eps
             phases.append(p)
 
         for li, L in enumerate(self.layers):
             first = li == 0
-            gemv_like(PH_GEMV, F_NORM | (F_X_EMBED if first else 0), s.qkv_rows, s.hidden, L["qkv"],
-                      self.embed if first else self.h, self.qkv, norm_w=L["ln1"])
+            base = 5 * li
+            if first:
+                gemv_like(PH_GEMV, F_NORM | F_X_EMBED | F_LL_OUT, s.qkv_rows, s.hidden, L["qkv"], self.embed,
+                          self.qkv, norm_w=L["ln1"])
+            else:
+                gemv_like(PH_GEMV, F_NORM | F_LL_IN | F_LL_OUT, s.qkv_rows, s.hidden, L["qkv"], self.h, self.qkv,
+                          norm_w=L["ln1"], x_src=base - 1)
             a = AicasPhase()
-            a.kind, a.flags = PH_ATTN, 0
+            a.kind, a.flags = PH_ATTN, F_LL_IN | F_LL_OUT
             a.kv_heads, a.q_heads, a.max_len = s.num_kv_heads, s.num_heads, self.max_cache_len
-            a.x, a.out = ptr(self.qkv), ptr(self.attn)
+            a.x, a.out, a.x_src = ptr(self.qkv), ptr(self.attn), base
             a.norm_w, a.norm_w2 = ptr(L["qn"]), ptr(L["kn"])
             a.k_cache, a.v_cache = ptr(self.k_cache[li]), ptr(self.v_cache[li])
             a.eps, a.scale = eps, float(s.head_dim ** -0.5)
             phases.append(a)
-            gemv_like(PH_GEMV, F_RESID | (F_RESID_EMBED if first else 0), s.hidden, s.q_size, L["o"], self.attn,
-                      self.h_mid, resid=self.embed if first else self.h)
-            gemv_like(PH_GATEUP, F_NORM, s.intermediate, s.hidden, L["gate_up"], self.h_mid, self.act,
-                      norm_w=L["ln2"])
-            gemv_like(PH_GEMV, F_RESID | F_KBLOCKED, s.hidden, s.intermediate, L["down"], self.act, self.h,
-                      resid=self.h_mid)
-        gemv_like(PH_LMHEAD, F_NORM, s.vocab, s.hidden, self.embed, self.h, self.h, norm_w=self.final_norm)
-        phases[-1].out = None
+            gemv_like(PH_GEMV, F_LL_IN | F_LL_OUT | F_RESID | (F_RESID_EMBED if first else F_LL_RESID), s.hidden,
+                      s.q_size, L["o"], self.attn, self.h_mid, resid=self.embed if first else self.h, x_src=base + 1)
+            gemv_like(PH_GATEUP, F_NORM | F_LL_IN | F_LL_OUT, s.intermediate, s.hidden, L["gate_up"], self.h_mid,
+                      self.act, norm_w=L["ln2"], x_src=base + 2)
+            gemv_like(PH_GEMV, F_LL_IN | F_LL_OUT | F_RESID | F_LL_RESID | F_KBLOCKED, s.hidden, s.intermediate,
+                      L["down"], self.act, self.h, resid=self.h_mid, x_src=base + 3)
+        gemv_like(PH_LMHEAD, F_NORM | F_LL_IN, s.vocab, s.hidden, self.embed, self.h, None, norm_w=self.final_norm,
+                  x_src=5 * s.num_layers - 1)
         arr = (AicasPhase * len(phases))(*phases)
         check(self._lib.aicas_validate_phases(arr, len(phases)), "aicas_validate_phases")
         raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
@@ -307,8 +325,14 @@ class Qwen3VLDecodeEngine:
     def check_error(self):
         code = device_error(self.scratch)
         if code:
-            self.scratch.zero_()
+            self.reset_device_state()
             raise AicasError(f"device error {code}: {self._lib.aicas_error_string(code).decode()}")
+
+    def reset_device_state(self):
+        """After a device error: zero the scratch block and the LL vectors
+        (their epochs restart with the scratch's)."""
+        for t in (self.scratch, self.h, self.h_mid, self.qkv, self.attn, self.act):
+            t.zero_()
 
     def step_logits(self, step: int) -> torch.Tensor:
         if self.logits is None:

@@ -36,7 +36,19 @@ enum AicasPhaseFlags {
   AICAS_F_STORE_X = 1 << 8,      // GEMV/GATEUP: CTA 0 stores the prologue vector to x_out
   AICAS_F_KBLOCKED = 1 << 9,     // W is stored K-blocked: [k/2048][n][2048] (k % 2048 == 0), so every
                                  // 8-row x 2048-column tile is one contiguous 32 KB block
+  AICAS_F_BARRIER = 1 << 10,     // grid barrier before this phase (inputs written by the previous phase)
+  AICAS_F_LL_IN = 1 << 11,       // x is an LL vector written by phase `x_src` of this launch (see below)
+  AICAS_F_LL_OUT = 1 << 12,      // out is an LL vector
+  AICAS_F_LL_RESID = 1 << 13,    // resid is an LL vector (complete before this phase starts)
 };
+
+// LL ("flag in data") vectors carry inter-phase activations without grid
+// barriers: value pair (2i, 2i+1) of an fp16 vector lives in 64-bit word i as
+// {half2 data, uint32 epoch}, written with one 8-byte store.  A consumer
+// polls the words it needs until every epoch equals the producing phase's
+// epoch (launch epoch base + phase index + 1), so the data, the completion
+// flag and the memory ordering arrive together.  Epochs grow by n_phases + 1
+// per launch (AicasScratch::epoch), so a stale word never matches.
 
 // One phase.  Pointers are device pointers (fp16 data is `__half`, passed as
 // void* so this header stays free of CUDA types).
@@ -50,7 +62,7 @@ typedef struct AicasPhase {
   int32_t q_heads;  // attention
   int32_t max_len;  // attention: cache slots per head
   int32_t embed_rows; // F_X_EMBED / F_RESID_EMBED: rows of the embedding table
-  int32_t pad1;
+  int32_t x_src;      // F_LL_IN: index of the phase (in this program) that writes x
   const void* w;      // weight [n, k] row-major (GATEUP: [2n, k], gate rows first), or K-blocked
   const void* norm_w; // RMSNorm weight [k] (attention: q_norm weight [128])
   const void* norm_w2;// attention: k_norm weight [128]
@@ -101,7 +113,9 @@ typedef struct AicasScratch {
   int32_t abort;        // set with `error`; every wait gives up when it is set
   uint32_t head_done[AICAS_MAX_KV_HEADS];  // split-KV merge arrivals per KV head
   uint32_t argmax_done;
-  uint32_t pad[3];
+  uint32_t epoch;       // LL epoch base of the next launch
+  uint32_t exit_count;  // CTAs finished in the running launch
+  uint32_t pad;
   float am_val[AICAS_MAX_CTAS];
   int32_t am_idx[AICAS_MAX_CTAS];
   // split-KV partials: [kv head][split][group 2][M, L, acc[128]]
