@@ -99,9 +99,11 @@ struct ProgramArgs {
   int pad;
   AicasStepState* state;  // may be null (op-level calls)
   AicasScratch* scratch;
-  int64_t* trace;  // optional [grid][n_phases][4]: start, end, consumer tile-wait ns, producer slot-wait ns
+  int64_t* trace;  // optional [grid][n_phases][kTraceFields] (see aicas_decode_program_trace_f16)
   AicasPhase inl[4];
 };
+
+constexpr int kTraceFields = 6;  // start, inputs ready, end, consumer tile-wait ns, producer slot-wait ns, tiles
 
 struct StepIn {
   int64_t token;
@@ -183,7 +185,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   };
   for (int ph = 0; ph < a.n_phases && ok; ++ph) {
     if (a.trace && ph > 0) {
-      a.trace[((size_t)cta * a.n_phases + ph - 1) * 4 + 3] = (int64_t)slot_wait;
+      a.trace[((size_t)cta * a.n_phases + ph - 1) * kTraceFields + 4] = (int64_t)slot_wait;
       slot_wait = 0;
     }
     const AicasPhase& d = P[ph];
@@ -241,7 +243,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
       }
     }
   }
-  if (a.trace) a.trace[((size_t)cta * a.n_phases + a.n_phases - 1) * 4 + 3] = (int64_t)slot_wait;
+  if (a.trace) a.trace[((size_t)cta * a.n_phases + a.n_phases - 1) * kTraceFields + 4] = (int64_t)slot_wait;
   // Drain: every issued copy must land before this CTA may exit.  In the
   // normal path the consumers already waited for all of them.
   const uint32_t issued = r.it;
@@ -307,12 +309,17 @@ struct Consumer {
     ++r.it;
   }
 
-  __device__ __forceinline__ void stamp(int ph, int which) {
+  uint32_t it_at_start = 0;
+  // which: 0 = phase start, 1 = inputs ready, 2 = phase end (also records
+  // the tile-wait time and the number of tiles consumed)
+  __device__ __forceinline__ void stamp(int phase, int which) {
     if (a.trace && tid == 0) {
-      int64_t* t = a.trace + ((size_t)cta * a.n_phases + ph) * 4;
+      int64_t* t = a.trace + ((size_t)cta * a.n_phases + phase) * kTraceFields;
       t[which] = (int64_t)globaltimer_ns();
-      if (which == 1) {
-        t[2] = (int64_t)wait_ns;
+      if (which == 0) it_at_start = r.it;
+      if (which == 2) {
+        t[3] = (int64_t)wait_ns;
+        t[5] = (int64_t)(r.it - it_at_start);
         wait_ns = 0;
       }
     }
@@ -537,6 +544,20 @@ struct Consumer {
     }
   }
 
+  // Residual of one output row (lane 0 only): prefetched for the first
+  // groups, loaded otherwise.
+  __device__ __forceinline__ float resid_row(const AicasPhase& d, bool resid, int gi, int rr, int row, int n) {
+    if (!resid || lane != 0 || row >= n) return 0.f;
+    if (gi < kResidPrefetch) {
+      float v = 0.f;
+#pragma unroll
+      for (int i = 0; i < kResidPrefetch; ++i)
+        if (i == gi) v = rv_pre[i][rr];
+      return v;
+    }
+    return resid_value(d, row);
+  }
+
   // Output value of one row (lane 0) with the rounding points of HF's fp16
   // path; the LM head also stores the logit and updates the running argmax.
   __device__ __forceinline__ static float row_value(int kind, int flags, int row, float sum0, float sum1, float rv,
@@ -578,6 +599,7 @@ struct Consumer {
   __device__ __forceinline__ void matvec(const AicasPhase& d) {
     uint4 x0[kVec];
     build_x<C>(d, x0);
+    stamp(ph, 1);
     // descriptor fields in registers (the waits below clobber memory)
     const int n = d.n, k = d.k, flags = d.flags, kind = d.kind;
     const bool gateup = kind == AICAS_PH_GATEUP;
@@ -607,32 +629,23 @@ struct Consumer {
     const bool timing = a.trace != nullptr && tid == 0;
     uint64_t waited = 0;
     uint32_t it = r.it;
-    auto take = [&](uint32_t& st) {
-      st = it % kStages;
-      if (timing) {
-        const uint64_t t0 = globaltimer_ns();
-        mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
-        waited += globaltimer_ns() - t0;
-      } else {
-        mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);
-      }
-    };
-    auto give = [&](uint32_t st) {
-      __syncwarp();
-      if (ln == 0) mbar_arrive_s(empty_s + st * 8);
-      ++it;
-    };
-    auto resid_of = [&](int gi, int rr, int row) -> float {
-      if (!resid || ln != 0 || row >= n) return 0.f;
-      float v = 0.f;
-      if (gi < kResidPrefetch) {
-#pragma unroll
-        for (int i = 0; i < kResidPrefetch; ++i)
-          if (i == gi) v = rv_pre[i][rr];
-        return v;
-      }
-      return resid_value(d, row);
-    };
+#define AICAS_TAKE(st)                                                                          \
+  do {                                                                                          \
+    st = it % kStages;                                                                          \
+    if (timing) {                                                                               \
+      const uint64_t t0_ = globaltimer_ns();                                                    \
+      mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);          \
+      waited += globaltimer_ns() - t0_;                                                         \
+    } else {                                                                                    \
+      mbar_wait_bounded_s(full_s + st * 8, (it / kStages) & 1u, scr, kErrFullTimeout);          \
+    }                                                                                           \
+  } while (0)
+#define AICAS_GIVE(st)                        \
+  do {                                        \
+    __syncwarp();                             \
+    if (ln == 0) mbar_arrive_s(empty_s + st * 8); \
+    ++it;                                     \
+  } while (0)
     float xf[kVec * 8];
     if (chunk_major(C, kind, rg.count)) {
       float acc[kMaxCmajorGroups][kRowsPerWarp][4];
@@ -654,7 +667,7 @@ struct Consumer {
         for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
           if (gi < rg.count) {
             uint32_t st;
-            take(st);
+            AICAS_TAKE(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
               const int row = (rg.start + gi) * kRows + 2 * wp + rr;
@@ -662,7 +675,7 @@ struct Consumer {
                 row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
                         acc[gi][rr], jmask);
             }
-            give(st);
+            AICAS_GIVE(st);
           }
         }
       }
@@ -674,7 +687,7 @@ struct Consumer {
 #pragma unroll
           for (int rr = 0; rr < kRowsPerWarp; ++rr) {
             const int row = row0 + rr;
-            const float rv = resid_of(gi, rr, row);
+            const float rv = resid_row(d, resid, gi, rr, row, n);
             const float sum = warp_sum((acc[gi][rr][0] + acc[gi][rr][1]) + (acc[gi][rr][2] + acc[gi][rr][3]));
             y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum, 0.f, rv, bias, logits, best_v, best_i)
                                          : 0.f;
@@ -704,7 +717,7 @@ struct Consumer {
             }
             const unsigned jmask = c < C - 1 ? 0xffu : jlast;
             uint32_t st;
-            take(st);
+            AICAS_TAKE(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
               const int row = (rg.start + gi) * kRows + 2 * wp + rr;
@@ -712,7 +725,7 @@ struct Consumer {
                 row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
                         acc[part][rr], jmask);
             }
-            give(st);
+            AICAS_GIVE(st);
           }
         }
         float y[kRowsPerWarp];
@@ -720,7 +733,7 @@ struct Consumer {
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
           const int row = row0 + rr;
-          const float rv = resid_of(gi, rr, row);
+          const float rv = resid_row(d, resid, gi, rr, row, n);
           const float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
           const float sum1 = gateup ? warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3])) : 0.f;
           y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum0, sum1, rv, bias, logits, best_v, best_i)
@@ -729,6 +742,8 @@ struct Consumer {
         if (ln == 0 && row0 < n) store_pair(flags, n, row0, y[0], y[1], out);
       }
     }
+#undef AICAS_TAKE
+#undef AICAS_GIVE
     wait_ns += waited;
     r.it = it;
     if (kind == AICAS_PH_LMHEAD) finish_argmax(d, best_v, best_i);
@@ -856,6 +871,7 @@ struct Consumer {
     }
     const float scale = d.scale;
     const int jpos = pos / kAttnChunk;
+    bool stamped = false;
     // per-warp online-softmax state for the 2 query heads of the current KV head
     float m[2], l[2], acc[2][4];
     float qreg[2][4];
@@ -889,6 +905,10 @@ struct Consumer {
               *reinterpret_cast<uint2*>(o);
         }
         consumer_sync(kConsumerThreads);
+        if (!stamped) {
+          stamp(ph, 1);
+          stamped = true;
+        }
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
 #pragma unroll
@@ -1089,7 +1109,7 @@ struct Consumer {
       stamp(ph, 0);
       if (d.kind == AICAS_PH_ATTN) run_attention(d);
       else run_matvec(d);
-      stamp(ph, 1);
+      stamp(ph, 2);
     }
     // the last CTA to finish moves the LL epoch base past this launch
     consumer_sync(kConsumerThreads);

@@ -297,36 +297,31 @@ def run_ours(args, rank: int, world: int):
 
 
 def write_trace_summary(eng, start_state, path):
-    """One traced decode step at cache slot 1024: per phase, the time from
-    the first CTA passing its barrier to the last CTA finishing (span), the
-    mean per-CTA busy time, and the barrier gap to the next phase."""
+    """One traced decode step at cache slot 1024.  Per phase kind (summed
+    over layers, averaged over CTAs): time waiting for inputs, time from
+    inputs to phase end, tile-wait time, producer slot-wait time, tiles per
+    CTA; plus the step's wall time."""
     import torch
 
     eng.restore(start_state)
-    tr = eng.launch_traced().double()  # [cta, phase, 4] ns
+    tr = eng.launch_traced().double()  # [cta, phase, 6]
     names = eng.phase_names()
     t0 = tr[:, 0, 0].min()
-    start, end = tr[:, :, 0] - t0, tr[:, :, 1] - t0
-    span = end.max(0).values - start.min(0).values
-    busy = (end - start).mean(0)
-    cwait = tr[:, :, 2].mean(0)
-    pwait = tr[:, :, 3].mean(0)
-    gap = torch.zeros_like(span)
-    gap[:-1] = start.min(0).values[1:] - end.max(0).values[:-1]
+    start, ready, end = tr[:, :, 0] - t0, tr[:, :, 1] - t0, tr[:, :, 2] - t0
     kinds = {}
     for i, nm in enumerate(names):
         k = nm.split(".")[-1]
-        e = kinds.setdefault(k, {"n": 0, "span_us": 0.0, "busy_us": 0.0, "gap_after_us": 0.0,
-                                 "consumer_tile_wait_us": 0.0, "producer_slot_wait_us": 0.0})
+        e = kinds.setdefault(k, {"n": 0, "input_wait_us": 0.0, "work_us": 0.0, "tile_wait_us": 0.0,
+                                 "producer_slot_wait_us": 0.0, "tiles_per_cta": 0.0, "span_us": 0.0})
         e["n"] += 1
-        e["consumer_tile_wait_us"] += float(cwait[i]) / 1e3
-        e["producer_slot_wait_us"] += float(pwait[i]) / 1e3
-        e["span_us"] += float(span[i]) / 1e3
-        e["busy_us"] += float(busy[i]) / 1e3
-        e["gap_after_us"] += float(gap[i]) / 1e3
+        e["input_wait_us"] += float((ready[:, i] - start[:, i]).mean()) / 1e3
+        e["work_us"] += float((end[:, i] - ready[:, i]).mean()) / 1e3
+        e["tile_wait_us"] += float(tr[:, i, 3].mean()) / 1e3
+        e["producer_slot_wait_us"] += float(tr[:, i, 4].mean()) / 1e3
+        e["tiles_per_cta"] += float(tr[:, i, 5].mean())
+        e["span_us"] += float(end[:, i].max() - start[:, i].min()) / 1e3
     total = float(end.max() - start.min()) / 1e3
-    summary = {"step_us": total, "by_kind_total_us": kinds,
-               "per_phase_span_us": [round(float(x) / 1e3, 2) for x in span]}
+    summary = {"step_us": total, "by_kind_total": kinds}
     Path(path).parent.mkdir(parents=True, exist_ok=True)
     Path(path).write_text(json.dumps(summary, indent=1))
 

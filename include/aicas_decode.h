@@ -137,11 +137,11 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
                                        void* scratch, aicas_stream_t stream);
 
 /* Profiling variant of aicas_decode_program_f16: additionally writes, per
- * CTA and phase, trace[cta][phase][4] (int64, aicas_num_ctas() * n_phases * 4
- * entries): the %globaltimer (ns) when the phase's consumers passed its grid
- * barrier, when they finished it, the ns one consumer warp spent waiting for
- * tiles to land, and the ns the producer spent waiting for free ring slots
- * while issuing that phase's tiles.  The reference records the same
+ * CTA and phase, trace[cta][phase][6] (int64, aicas_num_ctas() * n_phases * 6
+ * entries): the %globaltimer (ns) when the phase started, when its inputs
+ * were ready, when it finished; the ns one consumer warp spent waiting for
+ * weight/KV tiles to land; the ns the producer spent waiting for free ring
+ * slots while issuing the phase's tiles; and the number of tiles consumed.  The reference records the same
  * kind of per-block timelines in its `*_profile_*` kernel variants
  * (cuda_extensions/decode_gemv_kernel_common.cuh:174-188). */
 AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
