@@ -151,7 +151,7 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
 // chunk-major (all groups' chunk 0, then chunk 1, ...), so only one chunk of
 // the input vector is needed in fp32 registers at a time.  Producer and
 // consumers both call this to agree on the tile order.
-constexpr int kMaxCmajorGroups = 4;
+constexpr int kMaxCmajorGroups = 2;
 __device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
   return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
 }
@@ -509,39 +509,20 @@ struct Consumer {
     return lane_bits;
   }
 
-  // fp32 copy of this lane's 64 input values of chunk c (x stays fp16 in
-  // xr between chunks; conversion uses the packed f16x2 -> f32 path).
-  __device__ __forceinline__ static void x_to_f32(const uint4 (&xc)[kVec], float (&xf)[kVec * 8]) {
-#pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      const __half2* hp = reinterpret_cast<const __half2*>(&xc[j]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __half22float2(hp[q]);
-        xf[j * 8 + 2 * q] = f.x;
-        xf[j * 8 + 2 * q + 1] = f.y;
-      }
-    }
-  }
-
-  // acc[0..3] += one tile row (this lane's 64 columns at shared address
-  // `row_s`) . xf; products exact (fp16 x fp16 in fp32), fp32 accumulation
-  // in 4 independent chains.  `jmask` skips columns beyond k.
-  __device__ __forceinline__ static void row_dot(uint32_t row_s, const float (&xf)[kVec * 8], float (&acc)[4],
-                                                 unsigned jmask) {
-    uint4 wv[kVec];
+  // This lane's 64 columns of one tile row (shared address `row_s`) into
+  // registers; `jmask` skips columns beyond k.  Loading a tile completely
+  // before the math lets the stage go back to the producer immediately, so
+  // the FMAs overlap the next copies instead of lengthening the ring cycle.
+  __device__ __forceinline__ static void row_load(uint32_t row_s, unsigned jmask, uint4 (&wv)[kVec]) {
 #pragma unroll
     for (int j = 0; j < kVec; ++j) wv[j] = ((jmask >> j) & 1u) ? lds_u4(row_s + j * 512) : make_uint4(0, 0, 0, 0);
+  }
+
+  // acc[0..3] += row . x (both fp16): exact fp16 products, fp32 accumulation
+  // in 4 independent chains (PTX mixed-precision fma.rn.f32.f16).
+  __device__ __forceinline__ static void row_fma(const uint4 (&wv)[kVec], const uint4 (&xh)[kVec], float (&acc)[4]) {
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      const __half2* hp = reinterpret_cast<const __half2*>(&wv[j]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __half22float2(hp[q]);
-        acc[j & 3] = fmaf(f.x, xf[j * 8 + 2 * q], acc[j & 3]);
-        acc[j & 3] = fmaf(f.y, xf[j * 8 + 2 * q + 1], acc[j & 3]);
-      }
-    }
+    for (int j = 0; j < kVec; ++j) acc[j & 3] = dot8_f16(wv[j], xh[j], acc[j & 3]);
   }
 
   // Residual of one output row (lane 0 only): prefetched for the first
@@ -646,7 +627,7 @@ struct Consumer {
     if (ln == 0) mbar_arrive_s(empty_s + st * 8); \
     ++it;                                     \
   } while (0)
-    float xf[kVec * 8];
+    uint4 xh[kVec];  // fp16 input slice of the running chunk
     if (chunk_major(C, kind, rg.count)) {
       float acc[kMaxCmajorGroups][kRowsPerWarp][4];
 #pragma unroll
@@ -657,25 +638,23 @@ struct Consumer {
           for (int q = 0; q < 4; ++q) acc[g][rr][q] = 0.f;
 #pragma unroll
       for (int c = 0; c < C; ++c) {
-        {
-          uint4 xc[kVec];
-          x_chunk<C>(c, k, x0, xc);
-          x_to_f32(xc, xf);
-        }
+        x_chunk<C>(c, k, x0, xh);
         const unsigned jmask = c < C - 1 ? 0xffu : jlast;
 #pragma unroll
         for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
           if (gi < rg.count) {
             uint32_t st;
             AICAS_TAKE(st);
+            uint4 wv[kRowsPerWarp][kVec];
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
               const int row = (rg.start + gi) * kRows + 2 * wp + rr;
-              if (row < n)
-                row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
-                        acc[gi][rr], jmask);
+              row_load(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
+                       wv[rr]);
             }
             AICAS_GIVE(st);
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) row_fma(wv[rr], xh, acc[gi][rr]);
           }
         }
       }
@@ -696,7 +675,7 @@ struct Consumer {
         }
       }
     } else {
-      if (C == 1) x_to_f32(x0, xf);
+      if (C == 1) x_chunk<C>(0, k, x0, xh);
       for (int gi = 0; gi < rg.count; ++gi) {
         float acc[2][kRowsPerWarp][4];
 #pragma unroll
@@ -710,22 +689,20 @@ struct Consumer {
           if (part == 1 && !gateup) break;
 #pragma unroll
           for (int c = 0; c < C; ++c) {
-            if (C > 1) {
-              uint4 xc[kVec];
-              x_chunk<C>(c, k, x0, xc);
-              x_to_f32(xc, xf);
-            }
+            if (C > 1) x_chunk<C>(c, k, x0, xh);
             const unsigned jmask = c < C - 1 ? 0xffu : jlast;
             uint32_t st;
             AICAS_TAKE(st);
+            uint4 wv[kRowsPerWarp][kVec];
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
               const int row = (rg.start + gi) * kRows + 2 * wp + rr;
-              if (row < n)
-                row_dot(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, xf,
-                        acc[part][rr], jmask);
+              row_load(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
+                       wv[rr]);
             }
             AICAS_GIVE(st);
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) row_fma(wv[rr], xh, acc[part][rr]);
           }
         }
         float y[kRowsPerWarp];
