@@ -232,40 +232,45 @@ __device__ __forceinline__ bool grid_wait(AicasScratch* s, uint64_t target) {
   }
 }
 
-// LL vectors (aicas_phase_program.h): 64-bit words {half2 data, uint32 epoch}.
-__device__ __forceinline__ void ll_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+// LL vectors (aicas_phase_program.h): 32-bit words {fp16 value (low), uint16 epoch (high)}.
+__device__ __forceinline__ uint4 ll_load4w(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
 }
 
-__device__ __forceinline__ uint64_t ll_load1(const uint64_t* p) {
-  uint64_t a;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
-  return a;
+__device__ __forceinline__ uint32_t ll_load1w(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__device__ __forceinline__ void ll_store(uint64_t* p, uint32_t data, uint32_t epoch) {
-  const uint64_t v = ((uint64_t)epoch << 32) | data;
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void ll_store(uint32_t* p, float value, uint32_t epoch16) {
+  const uint32_t v = (epoch16 << 16) | (uint32_t)__half_as_ushort(__float2half_rn(value));
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
+__device__ __forceinline__ bool ll_ok(uint4 v, uint32_t e) {
+  return (v.x >> 16) == e && (v.y >> 16) == e && (v.z >> 16) == e && (v.w >> 16) == e;
 }
 
-// Bounded poll of the 4 LL words holding 8 fp16 values starting at value
-// index `col` (col % 8 == 0); returns them packed.  On timeout or abort the
-// error is recorded and whatever was read last is returned.
-__device__ __forceinline__ uint4 ll_poll8(const uint64_t* words, int col, uint32_t epoch, AicasScratch* s) {
-  const uint64_t* p = words + col / 2;
-  uint64_t w0, w1, w2, w3;
+// two LL words -> one half2 word (low halves)
+__device__ __forceinline__ uint32_t ll_pack(uint32_t lo, uint32_t hi) { return (lo & 0xffffu) | (hi << 16); }
+
+// Bounded poll of the 8 LL words holding values [col, col + 8) (col % 4 == 0
+// and the word array 16-byte aligned); returns the 8 fp16 values packed.  On
+// timeout or abort the error is recorded and the last read is returned.
+__device__ __forceinline__ uint4 ll_poll8(const uint32_t* words, int col, uint32_t epoch16, AicasScratch* s) {
+  const uint32_t* p = words + col;
+  uint4 a, b;
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
-    ll_load2(p, w0, w1);
-    ll_load2(p + 2, w2, w3);
-    if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch && (uint32_t)(w2 >> 32) == epoch &&
-        (uint32_t)(w3 >> 32) == epoch)
-      break;
+    a = ll_load4w(p);
+    b = ll_load4w(p + 4);
+    if (ll_ok(a, epoch16) && ll_ok(b, epoch16)) break;
     if (it == 0) t0 = globaltimer_ns();
     if ((it & 31u) == 31u) {
       if (ld_volatile_int(&s->abort)) break;
@@ -275,17 +280,17 @@ __device__ __forceinline__ uint4 ll_poll8(const uint64_t* words, int col, uint32
       }
     }
   }
-  return make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
+  return make_uint4(ll_pack(a.x, a.y), ll_pack(a.z, a.w), ll_pack(b.x, b.y), ll_pack(b.z, b.w));
 }
 
-// Same for the 2 words holding 4 fp16 values at `col` (col % 4 == 0).
-__device__ __forceinline__ uint2 ll_poll4(const uint64_t* words, int col, uint32_t epoch, AicasScratch* s) {
-  const uint64_t* p = words + col / 2;
-  uint64_t w0, w1;
+// Same for the 4 words holding values [col, col + 4).
+__device__ __forceinline__ uint2 ll_poll4(const uint32_t* words, int col, uint32_t epoch16, AicasScratch* s) {
+  const uint32_t* p = words + col;
+  uint4 a;
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
-    ll_load2(p, w0, w1);
-    if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch) break;
+    a = ll_load4w(p);
+    if (ll_ok(a, epoch16)) break;
     if (it == 0) t0 = globaltimer_ns();
     if ((it & 31u) == 31u) {
       if (ld_volatile_int(&s->abort)) break;
@@ -295,7 +300,7 @@ __device__ __forceinline__ uint2 ll_poll4(const uint64_t* words, int col, uint32
       }
     }
   }
-  return make_uint2((uint32_t)w0, (uint32_t)w1);
+  return make_uint2(ll_pack(a.x, a.y), ll_pack(a.z, a.w));
 }
 
 // fp16 helpers -------------------------------------------------------------

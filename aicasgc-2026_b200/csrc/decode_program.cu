@@ -54,10 +54,10 @@
 
 namespace aicas {
 
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // 160: leaves up to 255 registers per thread
-constexpr int kRowsPerWarp = 2;
+constexpr int kThreads = kConsumerThreads + 32;  // 288: two consumer warps per scheduler
+constexpr int kRowsPerWarp = 1;
 constexpr int kRows = kConsumerWarps * kRowsPerWarp;  // weight rows per GEMV tile
 constexpr int kChunk = 2048;           // columns per GEMV tile
 constexpr int kRowBytes = kChunk * 2;
@@ -335,9 +335,8 @@ struct Consumer {
 
   __device__ __forceinline__ float resid_value(const AicasPhase& d, int row) {
     if (d.flags & AICAS_F_LL_RESID) {  // complete before this phase: data only
-      const uint32_t bits = (uint32_t)ll_load1(reinterpret_cast<const uint64_t*>(d.resid) + row / 2);
-      const __half2 h2 = *reinterpret_cast<const __half2*>(&bits);
-      return (row & 1) ? __high2float(h2) : __low2float(h2);
+      const uint32_t word = ll_load1w(reinterpret_cast<const uint32_t*>(d.resid) + row);
+      return __half2float(__ushort_as_half((unsigned short)(word & 0xffffu)));
     }
     const __half* rp = reinterpret_cast<const __half*>(d.resid);
     if (d.flags & AICAS_F_RESID_EMBED) rp += (size_t)checked_token(d) * d.n;
@@ -370,7 +369,7 @@ struct Consumer {
       for (int i = 0; i < kResidPrefetch; ++i)
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = (rg.start + i) * kRows + 2 * w + rr;
+          const int row = (rg.start + i) * kRows + kRowsPerWarp * w + rr;
           rv_pre[i][rr] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
         }
     }
@@ -392,8 +391,8 @@ struct Consumer {
     if (flags & AICAS_F_X_EMBED) x += (size_t)checked_token(d) * k;
     const __half* x2 = reinterpret_cast<const __half*>(d.x2);
     const bool ll = flags & AICAS_F_LL_IN;
-    const uint64_t* xw = reinterpret_cast<const uint64_t*>(d.x);
-    const uint32_t x_epoch = epoch_base + (uint32_t)d.x_src + 1;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(d.x);
+    const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
@@ -465,7 +464,8 @@ struct Consumer {
 #pragma unroll
     for (int j = 0; j < kVec; ++j) {
       const int col = c * kChunk + j * 256 + lane * 8;
-      xc[j] = C == 1 ? x0[j] : (col < k ? *reinterpret_cast<const uint4*>(&sm.nw[col]) : make_uint4(0, 0, 0, 0));
+      // C > 1: inline-asm shared loads, so they stay after the tile wait they follow
+      xc[j] = C == 1 ? x0[j] : (col < k ? lds_u4(smem_addr(&sm.nw[col])) : make_uint4(0, 0, 0, 0));
     }
   }
 
@@ -562,16 +562,16 @@ struct Consumer {
     return y;
   }
 
-  // Lane 0 stores the warp's two adjacent output rows (row0, row0 + 1):
-  // one LL word, or plain fp16 stores.
-  __device__ __forceinline__ void store_pair(int flags, int n, int row0, float y0, float y1, __half* out) {
+  // Lane 0 stores the warp's output rows: LL words or plain fp16.
+  __device__ __forceinline__ void store_rows(int flags, int n, int row0, const float (&y)[kRowsPerWarp], __half* out) {
     if (!out) return;
-    if (flags & AICAS_F_LL_OUT) {
-      ll_store(reinterpret_cast<uint64_t*>(out) + row0 / 2, half2_bits(y0, row0 + 1 < n ? y1 : 0.f),
-               epoch_base + (uint32_t)ph + 1);
-    } else {
-      out[row0] = __float2half_rn(y0);
-      if (row0 + 1 < n) out[row0 + 1] = __float2half_rn(y1);
+#pragma unroll
+    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+      if (row0 + rr >= n) break;
+      if (flags & AICAS_F_LL_OUT)
+        ll_store(reinterpret_cast<uint32_t*>(out) + row0 + rr, y[rr], (epoch_base + (uint32_t)ph + 1) & 0xffffu);
+      else
+        out[row0 + rr] = __float2half_rn(y[rr]);
     }
   }
 
@@ -627,7 +627,7 @@ struct Consumer {
     if (ln == 0) mbar_arrive_s(empty_s + st * 8); \
     ++it;                                     \
   } while (0)
-    uint4 xh[kVec];  // fp16 input slice of the running chunk
+    uint4 xh[kVec];  // fp16 input slice of the running chunk (C > 1; C == 1 uses x0)
     if (chunk_major(C, kind, rg.count)) {
       float acc[kMaxCmajorGroups][kRowsPerWarp][4];
 #pragma unroll
@@ -648,13 +648,13 @@ struct Consumer {
             uint4 wv[kRowsPerWarp][kVec];
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + 2 * wp + rr;
-              row_load(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
+              const int row = (rg.start + gi) * kRows + kRowsPerWarp * wp + rr;
+              row_load(ring_s + st * kStageBytes + (kRowsPerWarp * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
                        wv[rr]);
             }
             AICAS_GIVE(st);
 #pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr) row_fma(wv[rr], xh, acc[gi][rr]);
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) if constexpr (C == 1) row_fma(wv[rr], x0, acc[gi][rr]); else row_fma(wv[rr], xh, acc[gi][rr]);
           }
         }
       }
@@ -662,7 +662,7 @@ struct Consumer {
       for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
         if (gi < rg.count) {
           float y[kRowsPerWarp];
-          const int row0 = (rg.start + gi) * kRows + 2 * wp;
+          const int row0 = (rg.start + gi) * kRows + kRowsPerWarp * wp;
 #pragma unroll
           for (int rr = 0; rr < kRowsPerWarp; ++rr) {
             const int row = row0 + rr;
@@ -671,11 +671,11 @@ struct Consumer {
             y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum, 0.f, rv, bias, logits, best_v, best_i)
                                          : 0.f;
           }
-          if (ln == 0 && row0 < n) store_pair(flags, n, row0, y[0], y[1], out);
+          if (ln == 0 && row0 < n) store_rows(flags, n, row0, y, out);
         }
       }
     } else {
-      if (C == 1) x_chunk<C>(0, k, x0, xh);
+
       for (int gi = 0; gi < rg.count; ++gi) {
         float acc[2][kRowsPerWarp][4];
 #pragma unroll
@@ -685,7 +685,7 @@ struct Consumer {
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[p][rr][q] = 0.f;
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {
+        for (int part = 0; part < (C == 1 ? 2 : 1); ++part) {  // gate_up: k <= 2048 (host-checked)
           if (part == 1 && !gateup) break;
 #pragma unroll
           for (int c = 0; c < C; ++c) {
@@ -696,17 +696,17 @@ struct Consumer {
             uint4 wv[kRowsPerWarp][kVec];
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + 2 * wp + rr;
-              row_load(ring_s + st * kStageBytes + (2 * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
+              const int row = (rg.start + gi) * kRows + kRowsPerWarp * wp + rr;
+              row_load(ring_s + st * kStageBytes + (kRowsPerWarp * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
                        wv[rr]);
             }
             AICAS_GIVE(st);
 #pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr) row_fma(wv[rr], xh, acc[part][rr]);
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) if constexpr (C == 1) row_fma(wv[rr], x0, acc[part][rr]); else row_fma(wv[rr], xh, acc[part][rr]);
           }
         }
         float y[kRowsPerWarp];
-        const int row0 = (rg.start + gi) * kRows + 2 * wp;
+        const int row0 = (rg.start + gi) * kRows + kRowsPerWarp * wp;
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
           const int row = row0 + rr;
@@ -716,7 +716,7 @@ struct Consumer {
           y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum0, sum1, rv, bias, logits, best_v, best_i)
                                        : 0.f;
         }
-        if (ln == 0 && row0 < n) store_pair(flags, n, row0, y[0], y[1], out);
+        if (ln == 0 && row0 < n) store_rows(flags, n, row0, y, out);
       }
     }
 #undef AICAS_TAKE
@@ -826,8 +826,8 @@ struct Consumer {
     const Range rg = split_range(U, nct, cta, 0);
     const __half* qkv = reinterpret_cast<const __half*>(d.x);
     const bool ll_in = d.flags & AICAS_F_LL_IN;
-    const uint64_t* qkv_w = reinterpret_cast<const uint64_t*>(d.x);
-    const uint32_t x_epoch = epoch_base + (uint32_t)d.x_src + 1;
+    const uint32_t* qkv_w = reinterpret_cast<const uint32_t*>(d.x);
+    const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
     __half* kc = reinterpret_cast<__half*>(d.k_cache);
     __half* vc = reinterpret_cast<__half*>(d.v_cache);
     const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
@@ -993,9 +993,9 @@ struct Consumer {
         const int last_owner = owner_of(h * cph + cph - 1, U, nct);
         const int split = cta - first_owner;
         const int nsplit = last_owner - first_owner + 1;
-        const int t = tid;  // head dim; every thread handles dim t of both query heads
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
+        // thread (g, t): query head 2h + g, head dim t
+        const int g = tid / kHD, t = tid % kHD;
+        {
           float M = -INFINITY;
 #pragma unroll
           for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
@@ -1038,34 +1038,27 @@ struct Consumer {
           }
           consumer_sync(kConsumerThreads);
           {
-            // thread t: query head 2h + g, dims dd and dd + 1 (one LL word)
-            const int g = t / (kHD / 2), dd = 2 * (t % (kHD / 2));
             float Mg = -INFINITY;
             for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, at.mm[sp][g]);
-            float Lg = 0.f, A0 = 0.f, A1 = 0.f;
+            float Lg = 0.f, Ag = 0.f;
             for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
-              float2 av[8];
+              float av[8];
 #pragma unroll
-              for (int q = 0; q < 8; ++q)
-                av[q] = sp0 + q < nsplit ? __ldcg(reinterpret_cast<const float2*>(&s->part[h][sp0 + q][g][2 + dd]))
-                                         : make_float2(0.f, 0.f);
+              for (int q = 0; q < 8; ++q) av[q] = sp0 + q < nsplit ? __ldcg(&s->part[h][sp0 + q][g][2 + t]) : 0.f;
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 if (sp0 + q < nsplit) {
                   const float f = expf(at.mm[sp0 + q][g] - Mg);
                   Lg += at.ll[sp0 + q][g] * f;
-                  A0 += av[q].x * f;
-                  A1 += av[q].y * f;
+                  Ag += av[q] * f;
                 }
               }
             }
-            const int o = (h * 2 + g) * kHD + dd;
-            if (d.flags & AICAS_F_LL_OUT) {
-              ll_store(reinterpret_cast<uint64_t*>(d.out) + o / 2, half2_bits(A0 / Lg, A1 / Lg),
-                       epoch_base + (uint32_t)ph + 1);
-            } else {
-              reinterpret_cast<__half2*>(d.out)[o / 2] = __floats2half2_rn(A0 / Lg, A1 / Lg);
-            }
+            const int o = (h * 2 + g) * kHD + t;
+            if (d.flags & AICAS_F_LL_OUT)
+              ll_store(reinterpret_cast<uint32_t*>(d.out) + o, Ag / Lg, (epoch_base + (uint32_t)ph + 1) & 0xffffu);
+            else
+              reinterpret_cast<__half*>(d.out)[o] = __float2half_rn(Ag / Lg);
           }
         }
         consumer_sync(kConsumerThreads);
@@ -1201,6 +1194,7 @@ static int validate_phase(const AicasPhase& d) {
       if ((d.flags & AICAS_F_STORE_X) && (!d.x_out || !aligned16(d.x_out))) return AICAS_ERR_ALIGN;
       if (d.kind != AICAS_PH_LMHEAD && !d.out) return AICAS_ERR_ARG;
       if (d.kind == AICAS_PH_GATEUP && (d.flags & (AICAS_F_RESID | AICAS_F_BIAS))) return AICAS_ERR_ARG;
+      if (d.kind == AICAS_PH_GATEUP && d.k > 2048) return AICAS_ERR_SHAPE;
       if ((d.flags & AICAS_F_KBLOCKED) && d.k % 2048 != 0) return AICAS_ERR_SHAPE;
       if ((d.flags & AICAS_F_LL_IN) && ((d.flags & (AICAS_F_X_ADD | AICAS_F_X_EMBED)) || d.x_src < 0))
         return AICAS_ERR_ARG;

@@ -95,13 +95,13 @@ class Qwen3VLDecodeEngine:
             kv_shape = (s.num_layers, 1, s.num_kv_heads, max_cache_len, s.head_dim)
             self.k_cache = torch.zeros(kv_shape, **f16)
             self.v_cache = torch.zeros(kv_shape, **f16)
-            # activations between phases as LL vectors: word i = {fp16 pair (2i, 2i+1), epoch}
-            ll = dict(dtype=torch.int64, device=dev)
-            self.h = torch.zeros(s.hidden // 2, **ll)
-            self.h_mid = torch.zeros(s.hidden // 2, **ll)
-            self.qkv = torch.zeros(s.qkv_rows // 2, **ll)
-            self.attn = torch.zeros(s.q_size // 2, **ll)
-            self.act = torch.zeros(s.intermediate // 2, **ll)
+            # activations between phases as LL vectors: word i = {fp16 value i, uint16 epoch}
+            ll = dict(dtype=torch.int32, device=dev)
+            self.h = torch.zeros(s.hidden, **ll)
+            self.h_mid = torch.zeros(s.hidden, **ll)
+            self.qkv = torch.zeros(s.qkv_rows, **ll)
+            self.attn = torch.zeros(s.q_size, **ll)
+            self.act = torch.zeros(s.intermediate, **ll)
             self.out_tokens = torch.full((max_steps,), -1, dtype=torch.int64, device=dev)
             self.logits_ring = int(logits_ring)
             self.logits = (torch.zeros((logits_ring, s.vocab), **f16) if logits_ring > 0 else None)

@@ -43,12 +43,13 @@ enum AicasPhaseFlags {
 };
 
 // LL ("flag in data") vectors carry inter-phase activations without grid
-// barriers: value pair (2i, 2i+1) of an fp16 vector lives in 64-bit word i as
-// {half2 data, uint32 epoch}, written with one 8-byte store.  A consumer
-// polls the words it needs until every epoch equals the producing phase's
-// epoch (launch epoch base + phase index + 1), so the data, the completion
-// flag and the memory ordering arrive together.  Epochs grow by n_phases + 1
-// per launch (AicasScratch::epoch), so a stale word never matches.
+// barriers: value i of an fp16 vector lives in 32-bit word i as {fp16 value
+// (low half), uint16 epoch (high half)}, written with one 4-byte store.  A
+// consumer polls the words it needs until every epoch equals the producing
+// phase's epoch ((launch epoch base + phase index + 1) mod 2^16), so the data,
+// the completion flag and the memory ordering arrive together.  Epochs grow
+// by n_phases + 1 per launch (AicasScratch::epoch) and every word is rewritten
+// every launch, so a stale word never matches.
 
 // One phase.  Pointers are device pointers (fp16 data is `__half`, passed as
 // void* so this header stays free of CUDA types).
