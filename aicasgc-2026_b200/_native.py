@@ -93,6 +93,7 @@ SIGNATURES = {
     "aicas_rmsnorm_qkv_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_post_attn_mlp_f16": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_decode_attn_splitkv_f16": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, _P]),
+    "aicas_decode_attn_splitkv_f16_noalloc": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, _P]),
     "aicas_qk_norm_mrope_kvwrite_f16": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _P]),
     "aicas_lm_head_argmax_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_decode_program_f16": (_I, [_P, _I, _P, _P, _P]),

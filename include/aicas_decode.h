@@ -47,6 +47,7 @@ extern "C" {
 #define AICAS_ERR_SHAPE 2
 #define AICAS_ERR_ALIGN 3
 #define AICAS_ERR_CUDA 4
+#define AICAS_ERR_CAPACITY 5
 
 typedef struct CUstream_st* aicas_stream_t; /* == cudaStream_t */
 
@@ -135,6 +136,26 @@ AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const 
  * layer loop over `OptimizedDecoderLayer.forward` (optimized_layer.py:108-469). */
 AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
                                        void* scratch, aicas_stream_t stream);
+
+/* Allocation-free variant of aicas_decode_attn_splitkv_f16, for callers that
+ * cannot allocate device memory themselves (for example code running inside
+ * a framework that owns every allocation, or a plugin that is only handed the
+ * tensors of one call): same arguments and result, but no `scratch`
+ * argument.  Its scratch is a fixed array inside this library, one per
+ * device, of aicas_scratch_bytes() bytes (about 2.1 MB), held until the
+ * process exits; it fits at most 8 KV heads (q_heads == 2 * kv_heads, head
+ * dim 128) and returns AICAS_ERR_CAPACITY for anything larger.  The first
+ * call on a device looks up the array's address, so make that call before
+ * any stream capture.  Every call on a device shares the one array: calls
+ * that overlap on the GPU (different streams, no ordering) race and give
+ * wrong results.  Each call zeroes the array's counters before its launch;
+ * `status` (device int32, may be null) receives the call's device error
+ * code.  Nothing is allocated or freed.  This entry point has no counterpart
+ * in the reference. */
+AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                                   const void* cache_position, float scale, void* out,
+                                                   int64_t q_heads, int64_t kv_heads, int64_t max_len,
+                                                   int32_t* status, aicas_stream_t stream);
 
 /* Profiling variant of aicas_decode_program_f16: additionally writes, per
  * CTA and phase, trace[cta][phase][6] (int64, aicas_num_ctas() * n_phases * 6
