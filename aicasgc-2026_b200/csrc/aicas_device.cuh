@@ -126,6 +126,11 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ int ld_volatile_int(const int32_t* p) {
   return *reinterpret_cast<const volatile int32_t*>(p);
 }

@@ -165,85 +165,166 @@ struct Ring {
   __device__ __forceinline__ uint32_t round() const { return it / kStages; }
 };
 
-__device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
-  AicasScratch* s = a.scratch;
-  const int nct = gridDim.x, cta = blockIdx.x;
-  const uint64_t pol = l2_evict_first_policy();
-  Ring r;
-  bool ok = true;
-  const AicasPhase* P = a.phases ? a.phases : a.inl;
-  uint64_t slot_wait = 0;  // trace only
-  auto acquire = [&](int st) -> bool {
-    if (r.round() == 0) return true;
-    if (a.trace) {
-      const uint64_t t0 = globaltimer_ns();
-      const bool good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
-      slot_wait += globaltimer_ns() - t0;
-      return good;
-    }
-    return mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
-  };
-  for (int ph = 0; ph < a.n_phases && ok; ++ph) {
-    if (a.trace && ph > 0) {
-      a.trace[((size_t)cta * a.n_phases + ph - 1) * kTraceFields + 4] = (int64_t)slot_wait;
-      slot_wait = 0;
-    }
+// One tile of the CTA's schedule: `pieces` copies of `bytes` each, from src
+// + i * src_stride to ring stage + i * dst_stride.
+struct TileDesc {
+  const uint8_t* src;
+  int64_t src_stride;
+  uint32_t dst_stride;
+  uint32_t bytes;
+  int pieces;
+  bool weights;  // weight tile (evict-first L2 policy) vs KV-cache tile
+};
+
+// Walks this CTA's tiles of a program in the exact order the consumers
+// take them.  The producer runs one cursor for the shared-memory ring and a
+// second one ahead of it for L2 prefetches.
+struct TileCursor {
+  const AicasPhase* P;
+  int n_phases;
+  int nct, cta;
+  int ph = -1;
+  int ti = 0, n = 0;
+  // cached per-phase schedule
+  int kind, flags, C, T, rows_total;
+  Range rg;
+  bool cmajor;
+  int valid, cph;
+
+  __device__ __forceinline__ void enter(int phase, const StepIn& in) {
+    ph = phase;
+    ti = 0;
+    n = 0;
+    if (ph >= n_phases) return;
     const AicasPhase& d = P[ph];
-    if (d.kind == AICAS_PH_ATTN) {
-      const int valid = phase_valid_len(d, in);
-      const int cph = (valid + kAttnChunk - 1) / kAttnChunk;
-      const Range rg = split_range(d.kv_heads * cph, nct, cta, 0);  // empty when valid == 0
-      const __half* kc = reinterpret_cast<const __half*>(d.k_cache);
-      const __half* vc = reinterpret_cast<const __half*>(d.v_cache);
-      for (int u = rg.start; u < rg.start + rg.count; ++u) {
-        const int st = r.stage();
-        if (!(ok = acquire(st))) break;
-        const int h = u / cph, p0 = (u % cph) * kAttnChunk;
-        const int rows = min(kAttnChunk, valid - p0);
-        const uint32_t bytes = rows * kHD * 2;
-        mbar_arrive_expect_tx(&sm.full[st], 2 * bytes);
-        const size_t off = ((size_t)h * d.max_len + p0) * kHD;
-        bulk_g2s_nohint(sm.ring[st], kc + off, bytes, &sm.full[st]);
-        bulk_g2s_nohint(sm.ring[st] + kStageBytes / 2, vc + off, bytes, &sm.full[st]);
-        ++r.it;
-      }
-    } else if (d.kind == AICAS_PH_GEMV || d.kind == AICAS_PH_GATEUP || d.kind == AICAS_PH_LMHEAD) {
-      const int G = (d.n + kRows - 1) / kRows;
-      const int C = n_chunks(d);
-      const int T = tiles_per_group(d);
-      const Range rg = split_range(G, nct, cta, d.rot);
-      const __half* W = reinterpret_cast<const __half*>(d.w);
-      auto issue = [&](int g, int t) -> bool {
-        const int st = r.stage();
-        if (!acquire(st)) return false;
-        const int nrows = min(kRows, d.n - g * kRows);
-        const int c = t % C;
-        const int row0 = g * kRows + (t >= C ? d.n : 0);
-        const int col0 = c * kChunk;
-        const uint32_t bytes = min(kChunk, d.k - col0) * 2;
-        mbar_arrive_expect_tx(&sm.full[st], nrows * bytes);
-        if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
-          bulk_g2s(sm.ring[st], W + (size_t)row0 * d.k, nrows * bytes, &sm.full[st], pol);
-        } else if (d.flags & AICAS_F_KBLOCKED) {  // block c of rows row0.. is contiguous
-          const int rows_total = d.kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
-          bulk_g2s(sm.ring[st], W + ((size_t)c * rows_total + row0) * kChunk, nrows * bytes, &sm.full[st], pol);
-        } else {  // row-major with k > 2048: one copy per row piece
-          for (int i = 0; i < nrows; ++i)
-            bulk_g2s(sm.ring[st] + i * kRowBytes, W + (size_t)(row0 + i) * d.k + col0, bytes, &sm.full[st], pol);
-        }
-        ++r.it;
-        return true;
-      };
-      if (chunk_major(C, d.kind, rg.count)) {
-        for (int c = 0; c < C && ok; ++c)
-          for (int g = rg.start; g < rg.start + rg.count && ok; ++g) ok = issue(g, c);
-      } else {
-        for (int g = rg.start; g < rg.start + rg.count && ok; ++g)
-          for (int t = 0; t < T && ok; ++t) ok = issue(g, t);
-      }
+    kind = d.kind;
+    flags = d.flags;
+    if (kind == AICAS_PH_ATTN) {
+      valid = phase_valid_len(d, in);
+      cph = (valid + kAttnChunk - 1) / kAttnChunk;
+      rg = split_range(d.kv_heads * cph, nct, cta, 0);  // empty when valid == 0
+      n = rg.count;
+    } else if (kind == AICAS_PH_GEMV || kind == AICAS_PH_GATEUP || kind == AICAS_PH_LMHEAD) {
+      C = n_chunks(d);
+      T = tiles_per_group(d);
+      rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
+      cmajor = chunk_major(C, kind, rg.count);
+      rows_total = kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
+      n = rg.count * T;
     }
   }
-  if (a.trace) a.trace[((size_t)cta * a.n_phases + a.n_phases - 1) * kTraceFields + 4] = (int64_t)slot_wait;
+
+  // Next tile; false when the program is exhausted.
+  __device__ __forceinline__ bool next(const StepIn& in, TileDesc& td) {
+    while (ti >= n) {
+      if (ph >= n_phases) return false;
+      enter(ph + 1, in);
+      if (ph >= n_phases) return false;
+    }
+    const AicasPhase& d = P[ph];
+    if (kind == AICAS_PH_ATTN) {
+      const int u = rg.start + ti;
+      const int h = u / cph, p0 = (u % cph) * kAttnChunk;
+      const int rows = min(kAttnChunk, valid - p0);
+      const size_t off = ((size_t)h * d.max_len + p0) * kHD * 2;
+      td.src = reinterpret_cast<const uint8_t*>(d.k_cache) + off;
+      td.src_stride = reinterpret_cast<const uint8_t*>(d.v_cache) - reinterpret_cast<const uint8_t*>(d.k_cache);
+      td.dst_stride = kStageBytes / 2;
+      td.bytes = rows * kHD * 2;
+      td.pieces = 2;
+      td.weights = false;
+    } else {
+      int g, t;
+      if (cmajor) {
+        t = ti / rg.count;
+        g = rg.start + ti % rg.count;
+      } else {
+        g = rg.start + ti / T;
+        t = ti % T;
+      }
+      const int nrows = min(kRows, d.n - g * kRows);
+      const int c = t % C;
+      const int row0 = g * kRows + (t >= C ? d.n : 0);
+      const int col0 = c * kChunk;
+      const uint32_t bytes = min(kChunk, d.k - col0) * 2;
+      const uint8_t* W = reinterpret_cast<const uint8_t*>(d.w);
+      td.weights = true;
+      if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
+        td.src = W + (size_t)row0 * d.k * 2;
+        td.bytes = nrows * bytes;
+        td.pieces = 1;
+      } else if (flags & AICAS_F_KBLOCKED) {  // block c of rows row0.. is contiguous
+        td.src = W + ((size_t)c * rows_total + row0) * kChunk * 2;
+        td.bytes = nrows * bytes;
+        td.pieces = 1;
+      } else {  // row-major with k > 2048: one copy per row piece
+        td.src = W + ((size_t)row0 * d.k + col0) * 2;
+        td.src_stride = (int64_t)d.k * 2;
+        td.dst_stride = kRowBytes;
+        td.bytes = bytes;
+        td.pieces = nrows;
+      }
+    }
+    ++ti;
+    return true;
+  }
+};
+
+// L2 run-ahead distance of the producer, in tiles (x 32 KB x CTAs of L2).
+constexpr int kL2Ahead = 16;
+
+__device__ __forceinline__ void l2_prefetch_tile(const TileDesc& td) {
+  for (int i = 0; i < td.pieces; ++i) bulk_prefetch_l2(td.src + i * td.src_stride, td.bytes);
+}
+
+__device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+  AicasScratch* s = a.scratch;
+  const uint64_t pol = l2_evict_first_policy();
+  Ring r;
+  const AicasPhase* P = a.phases ? a.phases : a.inl;
+  TileCursor ld{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+  TileCursor pf = ld;
+  uint64_t slot_wait = 0;  // trace only
+  int traced_ph = 0;
+  // Run-ahead: while the consumers wait for a phase's inputs (and the ring
+  // is full), HBM keeps filling L2 with the tiles that follow.
+  TileDesc td;
+  for (int i = 0; i < kL2Ahead && pf.next(in, td); ++i) l2_prefetch_tile(td);
+  while (ld.next(in, td)) {
+    if (a.trace && ld.ph != traced_ph) {
+      a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
+      slot_wait = 0;
+      traced_ph = ld.ph;
+    }
+    const int st = r.stage();
+    if (r.round() > 0) {
+      bool good;
+      if (a.trace) {
+        const uint64_t t0 = globaltimer_ns();
+        good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+        slot_wait += globaltimer_ns() - t0;
+      } else {
+        good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+      }
+      if (!good) break;
+    }
+    mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
+    for (int i = 0; i < td.pieces; ++i) {
+      uint8_t* dst = sm.ring[st] + i * td.dst_stride;
+      if (td.weights) bulk_g2s(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
+      else bulk_g2s_nohint(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st]);
+    }
+    ++r.it;
+    TileDesc tp;
+    if (pf.next(in, tp)) l2_prefetch_tile(tp);
+  }
+  if (a.trace) a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
+  // A decode step runs the same program again next launch: warm L2 with its
+  // first tiles (only a hint; the next launch fetches them regardless).
+  if (a.phases && a.state) {
+    TileCursor nx{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+    for (int i = 0; i < kL2Ahead && nx.next(in, td); ++i) l2_prefetch_tile(td);
+  }
   // Drain: every issued copy must land before this CTA may exit.  In the
   // normal path the consumers already waited for all of them.
   const uint32_t issued = r.it;
