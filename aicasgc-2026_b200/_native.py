@@ -8,11 +8,12 @@ calling it without a CUDA device, raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "libaicas_decode.so"
+LIB_PATH = Path(os.environ.get("AICAS_LIB", str(HERE / "libaicas_decode.so")))
 
 # Phase kinds / flags (include/aicas_phase_program.h)
 PH_GEMV, PH_GATEUP, PH_ATTN, PH_LMHEAD = 1, 2, 3, 4

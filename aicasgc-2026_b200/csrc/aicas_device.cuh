@@ -131,6 +131,11 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// One 128-byte line into L2 (a hint; no register result).
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ int ld_volatile_int(const int32_t* p) {
   return *reinterpret_cast<const volatile int32_t*>(p);
 }

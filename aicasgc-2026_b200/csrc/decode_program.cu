@@ -270,14 +270,33 @@ struct TileCursor {
   }
 };
 
-// L2 run-ahead distance of the producer, in tiles (x 32 KB x CTAs of L2).
-constexpr int kL2Ahead = 16;
+// L2 run-ahead of the producer: distance in tiles (x 32 KB x CTAs of L2)
+// and mode (0 off, 1 bulk prefetch by the copy engine, 2 one 128-byte line
+// prefetch per producer-warp lane and instruction).  Measured on B200 at
+// distances 4-32 tiles, every prefetch mode made the decode step slower
+// (1791 us/token without, 1918-2424 with), so it is off by default.
+#ifndef AICAS_L2_AHEAD
+#define AICAS_L2_AHEAD 16
+#endif
+#ifndef AICAS_L2_MODE
+#define AICAS_L2_MODE 0
+#endif
+constexpr int kL2Ahead = AICAS_L2_AHEAD;
 
-__device__ __forceinline__ void l2_prefetch_tile(const TileDesc& td) {
-  for (int i = 0; i < td.pieces; ++i) bulk_prefetch_l2(td.src + i * td.src_stride, td.bytes);
+__device__ __forceinline__ void l2_prefetch_tile(const TileDesc& td, int lane) {
+  if (AICAS_L2_MODE == 1) {
+    if (lane == 0)
+      for (int i = 0; i < td.pieces; ++i) bulk_prefetch_l2(td.src + i * td.src_stride, td.bytes);
+  } else if (AICAS_L2_MODE == 2) {
+    for (int i = 0; i < td.pieces; ++i)
+      for (uint32_t off = lane * 128u; off < td.bytes; off += 32u * 128u) prefetch_l2_line(td.src + i * td.src_stride + off);
+  }
 }
 
+// Run by all 32 lanes of warp 0: lane 0 owns the ring (waits, expect_tx,
+// copies); every lane takes part in the L2 run-ahead prefetches.
 __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+  const int lane = threadIdx.x & 31;
   AicasScratch* s = a.scratch;
   const uint64_t pol = l2_evict_first_policy();
   Ring r;
@@ -289,42 +308,49 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   // Run-ahead: while the consumers wait for a phase's inputs (and the ring
   // is full), HBM keeps filling L2 with the tiles that follow.
   TileDesc td;
-  for (int i = 0; i < kL2Ahead && pf.next(in, td); ++i) l2_prefetch_tile(td);
+  if (AICAS_L2_MODE)
+    for (int i = 0; i < kL2Ahead && pf.next(in, td); ++i) l2_prefetch_tile(td, lane);
   while (ld.next(in, td)) {
-    if (a.trace && ld.ph != traced_ph) {
+    if (lane == 0 && a.trace && ld.ph != traced_ph) {
       a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
       slot_wait = 0;
-      traced_ph = ld.ph;
     }
+    traced_ph = ld.ph;
     const int st = r.stage();
-    if (r.round() > 0) {
-      bool good;
-      if (a.trace) {
-        const uint64_t t0 = globaltimer_ns();
-        good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
-        slot_wait += globaltimer_ns() - t0;
-      } else {
-        good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+    int good = 1;
+    if (lane == 0) {
+      if (r.round() > 0) {
+        if (a.trace) {
+          const uint64_t t0 = globaltimer_ns();
+          good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+          slot_wait += globaltimer_ns() - t0;
+        } else {
+          good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+        }
       }
-      if (!good) break;
+      if (good) {
+        mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
+        for (int i = 0; i < td.pieces; ++i) {
+          uint8_t* dst = sm.ring[st] + i * td.dst_stride;
+          if (td.weights) bulk_g2s(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
+          else bulk_g2s_nohint(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st]);
+        }
+      }
     }
-    mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
-    for (int i = 0; i < td.pieces; ++i) {
-      uint8_t* dst = sm.ring[st] + i * td.dst_stride;
-      if (td.weights) bulk_g2s(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
-      else bulk_g2s_nohint(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st]);
-    }
+    if (!__shfl_sync(0xffffffffu, good, 0)) break;
     ++r.it;
     TileDesc tp;
-    if (pf.next(in, tp)) l2_prefetch_tile(tp);
+    if (AICAS_L2_MODE && pf.next(in, tp)) l2_prefetch_tile(tp, lane);
   }
-  if (a.trace) a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
+  if (lane == 0 && a.trace)
+    a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
   // A decode step runs the same program again next launch: warm L2 with its
   // first tiles (only a hint; the next launch fetches them regardless).
-  if (a.phases && a.state) {
+  if (AICAS_L2_MODE && a.phases && a.state) {
     TileCursor nx{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
-    for (int i = 0; i < kL2Ahead && nx.next(in, td); ++i) l2_prefetch_tile(td);
+    for (int i = 0; i < kL2Ahead && nx.next(in, td); ++i) l2_prefetch_tile(td, lane);
   }
+  if (lane != 0) return;
   // Drain: every issued copy must land before this CTA may exit.  In the
   // normal path the consumers already waited for all of them.
   const uint32_t issued = r.it;
@@ -1199,7 +1225,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   const AicasPhase* P = a.phases ? a.phases : a.inl;
   const int warp = threadIdx.x / 32;
   if (warp == 0) {
-    if ((threadIdx.x & 31) == 0) run_producer(a, sm, in);
+    run_producer(a, sm, in);
     return;
   }
   Consumer c{a, sm, in, a.scratch};

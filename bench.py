@@ -322,6 +322,9 @@ def write_trace_summary(eng, start_state, path):
         e["span_us"] += float(end[:, i].max() - start[:, i].min()) / 1e3
     total = float(end.max() - start.min()) / 1e3
     summary = {"step_us": total, "by_kind_total": kinds}
+    import numpy as np
+
+    np.save(str(Path(path).with_suffix(".npy")), tr.numpy().astype(np.int64))
     Path(path).parent.mkdir(parents=True, exist_ok=True)
     Path(path).write_text(json.dumps(summary, indent=1))
 
