@@ -71,7 +71,7 @@ class AicasStepState(ctypes.Structure):
 
 
 # Offsets of the scratch words the host reads (AicasScratch).
-SCRATCH_ERROR_OFFSET = 8
+SCRATCH_ERROR_OFFSET = 16
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -123,7 +123,8 @@ def lib() -> ctypes.CDLL:
         sig = (ctypes.c_int64 * 8)()
         n = L.aicas_layout_signature(sig, 8)
         want = [ctypes.sizeof(AicasPhase), ctypes.sizeof(AicasStepState), None,
-                AicasPhase.w.offset, AicasPhase.eps.offset, AicasStepState.inv_freq.offset, None]
+                AicasPhase.w.offset, AicasPhase.eps.offset, AicasStepState.inv_freq.offset, None,
+                SCRATCH_ERROR_OFFSET]
         for i in range(min(n, len(want))):
             if want[i] is not None and sig[i] != want[i]:
                 raise AicasError(f"struct layout mismatch at {i}: lib {sig[i]} vs ctypes {want[i]}")

@@ -263,6 +263,23 @@ __device__ __forceinline__ void ll_store(uint32_t* p, float value, uint32_t epoc
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// 64-bit LL words {fp32 value (low), uint32 epoch (high)} (split-KV partials):
+// one aligned 64-bit store is single-copy atomic, so a reader that sees the
+// epoch also sees the value, with no fence on either side.
+__device__ __forceinline__ void ll64_store(uint64_t* p, float value, uint32_t epoch) {
+  const uint64_t v = ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(value);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ll64_load(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ll64_epoch(uint64_t v) { return (uint32_t)(v >> 32); }
+__device__ __forceinline__ float ll64_value(uint64_t v) { return __uint_as_float((uint32_t)v); }
+
 __device__ __forceinline__ bool ll_ok(uint4 v, uint32_t e) {
   return (v.x >> 16) == e && (v.y >> 16) == e && (v.z >> 16) == e && (v.w >> 16) == e;
 }
@@ -291,6 +308,41 @@ __device__ __forceinline__ uint4 ll_poll8(const uint32_t* words, int col, uint32
     }
   }
   return make_uint4(ll_pack(a.x, a.y), ll_pack(a.z, a.w), ll_pack(b.x, b.y), ll_pack(b.z, b.w));
+}
+
+// Bounded poll of N groups of 8 LL words at once (group i starts at value
+// index cols[i]; a negative index skips the group and yields zeros).  Every
+// round issues the loads of all groups with no branch between them and packs
+// each group into `out` as it lands, so data that has already arrived costs
+// one round trip in total rather than one per group, and a group's raw words
+// die as soon as they are packed.
+template <int N>
+__device__ __forceinline__ void ll_poll8_n(const uint32_t* words, const int (&cols)[N], uint32_t epoch16,
+                                           AicasScratch* s, uint4 (&out)[N]) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if (cols[i] >= 0) {
+        const uint4 a = ll_load4w(words + cols[i]);
+        const uint4 b = ll_load4w(words + cols[i] + 4);
+        ok = ok && ll_ok(a, epoch16) && ll_ok(b, epoch16);
+        out[i] = make_uint4(ll_pack(a.x, a.y), ll_pack(a.z, a.w), ll_pack(b.x, b.y), ll_pack(b.z, b.w));
+      } else {
+        out[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (ok) break;
+    if (it == 0) t0 = globaltimer_ns();
+    if ((it & 31u) == 31u) {
+      if (ld_volatile_int(&s->abort)) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrInputTimeout);
+        break;
+      }
+    }
+  }
 }
 
 // Same for the 4 words holding values [col, col + 4).

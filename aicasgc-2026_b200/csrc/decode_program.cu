@@ -78,9 +78,6 @@ struct AttnSmem {
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
-  float mm[AICAS_MAX_SPLITS][2];  // final merge: per-split max / sum
-  float ll[AICAS_MAX_SPLITS][2];
-  int last;
 };
 
 struct __align__(128) Smem {
@@ -152,6 +149,8 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
 // the input vector is needed in fp32 registers at a time.  Producer and
 // consumers both call this to agree on the tile order.
 constexpr int kMaxCmajorGroups = 2;
+// split-KV merge: partials polled per round by the merging CTA
+constexpr int kMergeBatch = 16;
 __device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
   return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
 }
@@ -500,38 +499,51 @@ struct Consumer {
     const bool ll = flags & AICAS_F_LL_IN;
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(d.x);
     const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
+    // this lane's vectors: (c, j) with col = c*2048 + j*256 + lane*8; for C > 1
+    // the 8 warps split them and share the result through sm.nw
+    constexpr int NV = C == 1 ? kVec : (C * kVec + kConsumerWarps - 1) / kConsumerWarps;
+    int cols[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = C == 1 ? i : i * kConsumerWarps + w;  // vector index c*kVec + j
+      const int col = (v / kVec) * kChunk + (v % kVec) * 256 + lane * 8;
+      cols[i] = (v < C * kVec && col < k) ? col : -1;
+    }
+    uint4 raw[NV];
+    if (ll) {
+      ll_poll8_n<NV>(xw, cols, x_epoch, s, raw);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) raw[i] = cols[i] >= 0 ? ldcg_u4(x + cols[i]) : make_uint4(0, 0, 0, 0);
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
+    for (int i = 0; i < NV; ++i) {
+      if (cols[i] < 0) continue;
+      if (flags & AICAS_F_X_ADD) {
+        const uint4 raw2 = ldcg_u4(x2 + cols[i]);
+        __half2* hp = reinterpret_cast<__half2*>(&raw[i]);
+        const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
 #pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        const int col = c * kChunk + j * 256 + lane * 8;
-        uint4 raw = make_uint4(0, 0, 0, 0);
-        // C > 1: the 4 warps split the columns and share them through sm.nw
-        if (col < k && (C == 1 || (c * kVec + j) % kConsumerWarps == w)) {
-          raw = ll ? ll_poll8(xw, col, x_epoch, s) : ldcg_u4(x + col);
-          if (flags & AICAS_F_X_ADD) {
-            const uint4 raw2 = ldcg_u4(x2 + col);
-            __half2* hp = reinterpret_cast<__half2*>(&raw);
-            const __half2* hq = reinterpret_cast<const __half2*>(&raw2);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 fa = __half22float2(hp[q]), fb = __half22float2(hq[q]);
-              hp[q] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
-            }
-          }
-          if (C == 1) {
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 f = __half22float2(hp[q]);
-              ss += f.x * f.x + f.y * f.y;
-            }
-          }
+        for (int q = 0; q < 4; ++q) {
+          const float2 fa = __half22float2(hp[q]), fb = __half22float2(hq[q]);
+          hp[q] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
         }
-        if (C == 1) x0[j] = raw;
-        else if (col < k && (c * kVec + j) % kConsumerWarps == w) *reinterpret_cast<uint4*>(&sm.nw[col]) = raw;
       }
+      if (C == 1) {
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hp[q]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      } else {
+        *reinterpret_cast<uint4*>(&sm.nw[cols[i]]) = raw[i];
+      }
+    }
+    if constexpr (C == 1) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) x0[j] = raw[j];
     }
     if (C > 1) consumer_sync(kConsumerThreads);
     if (C == 1 && (flags & AICAS_F_NORM)) {
@@ -1100,75 +1112,91 @@ struct Consumer {
         const int last_owner = owner_of(h * cph + cph - 1, U, nct);
         const int split = cta - first_owner;
         const int nsplit = last_owner - first_owner + 1;
-        // thread (g, t): query head 2h + g, head dim t
+        const uint32_t ep = epoch_base + (uint32_t)ph + 1;
+        // thread (g, t): query head 2h + g, head dim t.  This CTA's partial
+        // as (log-sum-exp, normalised acc): merge the 8 warps' states.
         const int g = tid / kHD, t = tid % kHD;
-        {
-          float M = -INFINITY;
+        float M = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
-          float L = 0.f, A = 0.f;
+        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
+        float L = 0.f, A = 0.f;
 #pragma unroll
-          for (int i = 0; i < kConsumerWarps; ++i) {
-            const float mi = at.wm[i][g];
-            if (mi != -INFINITY) {
-              const float f = expf(mi - M);
-              L += at.wl[i][g] * f;
-              A += at.wacc[i][g][t] * f;
+        for (int i = 0; i < kConsumerWarps; ++i) {
+          const float mi = at.wm[i][g];
+          if (mi != -INFINITY) {
+            const float f = expf(mi - M);
+            L += at.wl[i][g] * f;
+            A += at.wacc[i][g][t] * f;
+          }
+        }
+        float lse = M + logf(L), o = A / L;
+        uint64_t* pp = &s->part[h][0][g][0];
+        constexpr int kSplitStride = 2 * (kHD + 1);
+        if (cta != last_owner) {
+          // 64-bit LL stores: the merging CTA polls them, no fence or counter
+          if (t == 0) ll64_store(pp + split * kSplitStride, lse, ep);
+          ll64_store(pp + split * kSplitStride + 1 + t, o, ep);
+        } else {
+          // the head's last owner merges: its own partial, then splits
+          // 0 .. nsplit-2 in order, kMergeBatch per polling round (all loads
+          // of a round issued before any is checked).  Lane i of the warp
+          // loads the log-sum-exp of split b0 + i and shares it by shuffle;
+          // each thread loads its own dim's normalised acc.  The warp polls
+          // as one (uniform exit), so the shuffles stay converged.
+          float mx = lse, S = 1.f, acc = o;
+          for (int b0 = 0; b0 < nsplit - 1; b0 += kMergeBatch) {
+            const int cnt = min(kMergeBatch, nsplit - 1 - b0);
+            uint64_t lw = 0, ow[kMergeBatch];
+            uint64_t t0 = 0;
+            for (uint32_t it = 0;; ++it) {
+              bool ok = true;
+              if (lane < cnt) {
+                lw = ll64_load(pp + (b0 + lane) * kSplitStride);
+                ok = ll64_epoch(lw) == ep;
+              }
+#pragma unroll
+              for (int i = 0; i < kMergeBatch; ++i) {
+                if (i < cnt) {
+                  ow[i] = ll64_load(pp + (b0 + i) * kSplitStride + 1 + t);
+                  ok = ok && ll64_epoch(ow[i]) == ep;
+                }
+              }
+              if (__all_sync(0xffffffffu, ok)) break;
+              if (it == 0) t0 = globaltimer_ns();
+              if ((it & 31u) == 31u) {
+                bool give_up = ld_volatile_int(&s->abort) != 0;
+                if (!give_up && globaltimer_ns() - t0 > kWaitLimitNs) {
+                  raise_error(s, kErrInputTimeout);
+                  give_up = true;
+                }
+                if (__any_sync(0xffffffffu, give_up)) break;
+              }
             }
-          }
-          float* pp = &s->part[h][split][g][0];
-          if (t == 0) {
-            pp[0] = M;
-            pp[1] = L;
-          }
-          pp[2 + t] = A;
-        }
-        __threadfence();
-        consumer_sync(kConsumerThreads);
-        if (tid == 0) {
-          const uint32_t prev = atomicAdd(&s->head_done[h], 1u);
-          at.last = (prev == (uint32_t)nsplit - 1) ? 1 : 0;
-          if (at.last) {
-            s->head_done[h] = 0;
-            __threadfence();
-          }
-        }
-        consumer_sync(kConsumerThreads);
-        if (at.last) {
-          // (M, L) of every split into shared memory with one parallel round
-          // of loads, then per dim all splits' acc values (loads issued in
-          // batches of 8 before they are combined), combined in split order.
-          for (int i = tid; i < 2 * nsplit; i += kConsumerThreads) {
-            const int sp = i >> 1, g = i & 1;
-            at.mm[sp][g] = __ldcg(&s->part[h][sp][g][0]);
-            at.ll[sp][g] = __ldcg(&s->part[h][sp][g][1]);
-          }
-          consumer_sync(kConsumerThreads);
-          {
-            float Mg = -INFINITY;
-            for (int sp = 0; sp < nsplit; ++sp) Mg = fmaxf(Mg, at.mm[sp][g]);
-            float Lg = 0.f, Ag = 0.f;
-            for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
-              float av[8];
+            const float lmine = ll64_value(lw);
 #pragma unroll
-              for (int q = 0; q < 8; ++q) av[q] = sp0 + q < nsplit ? __ldcg(&s->part[h][sp0 + q][g][2 + t]) : 0.f;
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                if (sp0 + q < nsplit) {
-                  const float f = expf(at.mm[sp0 + q][g] - Mg);
-                  Lg += at.ll[sp0 + q][g] * f;
-                  Ag += av[q] * f;
+            for (int i = 0; i < kMergeBatch; ++i) {
+              const float li = __shfl_sync(0xffffffffu, lmine, i);
+              if (i < cnt) {
+                const float oi = ll64_value(ow[i]);
+                if (li > mx) {
+                  const float c = expf(mx - li);
+                  S = S * c + 1.f;
+                  acc = acc * c + oi;
+                  mx = li;
+                } else {
+                  const float c = expf(li - mx);
+                  S += c;
+                  acc += c * oi;
                 }
               }
             }
-            const int o = (h * 2 + g) * kHD + t;
-            if (d.flags & AICAS_F_LL_OUT)
-              ll_store(reinterpret_cast<uint32_t*>(d.out) + o, Ag / Lg, (epoch_base + (uint32_t)ph + 1) & 0xffffu);
-            else
-              reinterpret_cast<__half*>(d.out)[o] = __float2half_rn(Ag / Lg);
           }
+          const int oidx = (h * 2 + g) * kHD + t;
+          if (d.flags & AICAS_F_LL_OUT)
+            ll_store(reinterpret_cast<uint32_t*>(d.out) + oidx, acc / S, ep & 0xffffu);
+          else
+            reinterpret_cast<__half*>(d.out)[oidx] = __float2half_rn(acc / S);
         }
-        consumer_sync(kConsumerThreads);
       }
     }
   }
@@ -1366,7 +1394,8 @@ AICAS_API size_t aicas_scratch_bytes(void) { return sizeof(AicasScratch); }
 AICAS_API int aicas_layout_signature(int64_t* out, int n) {
   const int64_t v[] = {(int64_t)sizeof(AicasPhase), (int64_t)sizeof(AicasStepState), (int64_t)sizeof(AicasScratch),
                        (int64_t)offsetof(AicasPhase, w), (int64_t)offsetof(AicasPhase, eps),
-                       (int64_t)offsetof(AicasStepState, inv_freq), (int64_t)offsetof(AicasScratch, part)};
+                       (int64_t)offsetof(AicasStepState, inv_freq), (int64_t)offsetof(AicasScratch, part),
+                       (int64_t)offsetof(AicasScratch, error)};
   const int m = (int)(sizeof(v) / sizeof(v[0]));
   for (int i = 0; i < n && i < m; ++i) out[i] = v[i];
   return m;
@@ -1601,9 +1630,9 @@ extern "C" AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, co
     g_noalloc_scratch_ptr[dev] = scr;
   }
   // The array keeps the previous call's contents: zero the words a launch
-  // expects to start at zero (counters, error and abort words).  The split
-  // partials are always written before they are read.
-  e = cudaMemsetAsync(scr, 0, offsetof(AicasScratch, am_val), stream);
+  // expects to start at zero (error, abort and counters).  The epoch base
+  // keeps counting, so partials left by the previous call never match.
+  e = cudaMemsetAsync(&scr->error, 0, offsetof(AicasScratch, am_val) - offsetof(AicasScratch, error), stream);
   if (e != cudaSuccess) return cuda_fail(e);
   ProgramArgs a;
   memset(&a, 0, sizeof(a));

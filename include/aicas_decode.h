@@ -142,7 +142,7 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
  * a framework that owns every allocation, or a plugin that is only handed the
  * tensors of one call): same arguments and result, but no `scratch`
  * argument.  Its scratch is a fixed array inside this library, one per
- * device, of aicas_scratch_bytes() bytes (about 2.1 MB), held until the
+ * device, of aicas_scratch_bytes() bytes (about 4.2 MB), held until the
  * process exits; it fits at most 8 KV heads (q_heads == 2 * kv_heads, head
  * dim 128) and returns AICAS_ERR_CAPACITY for anything larger.  The first
  * call on a device looks up the array's address, so make that call before

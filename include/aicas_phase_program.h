@@ -110,17 +110,19 @@ typedef struct AicasStepState {
 // every launch leaves it ready for the next one).
 typedef struct AicasScratch {
   uint64_t bar_count;   // grid barrier arrivals (monotonic across launches)
+  uint32_t epoch;       // LL epoch base of the next launch (never reset: see part)
+  uint32_t pad0;
   int32_t error;        // first error code raised on the device (0 = none)
   int32_t abort;        // set with `error`; every wait gives up when it is set
-  uint32_t head_done[AICAS_MAX_KV_HEADS];  // split-KV merge arrivals per KV head
   uint32_t argmax_done;
-  uint32_t epoch;       // LL epoch base of the next launch
   uint32_t exit_count;  // CTAs finished in the running launch
-  uint32_t pad;
   float am_val[AICAS_MAX_CTAS];
   int32_t am_idx[AICAS_MAX_CTAS];
-  // split-KV partials: [kv head][split][group 2][M, L, acc[128]]
-  float part[AICAS_MAX_KV_HEADS][AICAS_MAX_SPLITS][2][AICAS_HEAD_DIM + 2];
+  // split-KV partials as 64-bit LL words {fp32 value (low), uint32 epoch
+  // (high)}: [kv head][split][group 2][log-sum-exp, normalised acc[128]].
+  // A word is accepted when its epoch equals the writing phase's full 32-bit
+  // epoch, so `epoch` must keep counting across launches.
+  uint64_t part[AICAS_MAX_KV_HEADS][AICAS_MAX_SPLITS][2][AICAS_HEAD_DIM + 1];
 } AicasScratch;
 
 #ifdef __cplusplus
