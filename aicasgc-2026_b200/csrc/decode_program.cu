@@ -78,12 +78,15 @@ struct AttnSmem {
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
+  float rope_c[kHD / 2], rope_s[kHD / 2];  // this launch's MRoPE cos/sin (fp16-rounded)
 };
 
 struct __align__(128) Smem {
   uint8_t ring[kStages][kStageBytes];
   __half nw[AICAS_MAX_K];  // norm weights of the running phase (prefetched before its barrier)
   AttnSmem at;
+  __half xs[kChunk];            // C == 1 phases: the input vector, shared by the 8 warps
+  float ssq[kConsumerWarps];    // per-warp sums of squares for the RMSNorm prologue
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
   uint64_t full[kStages];
@@ -294,6 +297,7 @@ __device__ __forceinline__ void l2_prefetch_tile(const TileDesc& td, int lane) {
 
 // Run by all 32 lanes of warp 0: lane 0 owns the ring (waits, expect_tx,
 // copies); every lane takes part in the L2 run-ahead prefetches.
+template <bool kTrace>
 __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
   const int lane = threadIdx.x & 31;
   AicasScratch* s = a.scratch;
@@ -310,7 +314,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   if (AICAS_L2_MODE)
     for (int i = 0; i < kL2Ahead && pf.next(in, td); ++i) l2_prefetch_tile(td, lane);
   while (ld.next(in, td)) {
-    if (lane == 0 && a.trace && ld.ph != traced_ph) {
+    if (kTrace && lane == 0 && ld.ph != traced_ph) {
       a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
       slot_wait = 0;
     }
@@ -319,7 +323,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
     int good = 1;
     if (lane == 0) {
       if (r.round() > 0) {
-        if (a.trace) {
+        if (kTrace) {
           const uint64_t t0 = globaltimer_ns();
           good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
           slot_wait += globaltimer_ns() - t0;
@@ -341,7 +345,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
     TileDesc tp;
     if (AICAS_L2_MODE && pf.next(in, tp)) l2_prefetch_tile(tp, lane);
   }
-  if (lane == 0 && a.trace)
+  if (kTrace && lane == 0)
     a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
   // A decode step runs the same program again next launch: warm L2 with its
   // first tiles (only a hint; the next launch fetches them regardless).
@@ -369,6 +373,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
 // ---------------------------------------------------------------------------
 // Consumers (warps 1..8)
 // ---------------------------------------------------------------------------
+template <bool kTrace>
 struct Consumer {
   const ProgramArgs& a;
   Smem& sm;
@@ -392,7 +397,7 @@ struct Consumer {
   // launch ends promptly with the error recorded in the scratch block.
   uint64_t wait_ns = 0;  // trace only: time consumer warp 0 spent waiting for tiles in this phase
   __device__ __forceinline__ void wait_full_at(int st, uint32_t round) {
-    if (a.trace && tid == 0) {
+    if (kTrace && tid == 0) {
       const uint64_t t0 = globaltimer_ns();
       mbar_wait_bounded(&sm.full[st], round & 1u, s, kErrFullTimeout);
       wait_ns += globaltimer_ns() - t0;
@@ -401,7 +406,7 @@ struct Consumer {
     mbar_wait_bounded(&sm.full[st], round & 1u, s, kErrFullTimeout);
   }
   __device__ __forceinline__ void wait_full(int st) {
-    if (a.trace && tid == 0) {
+    if (kTrace && tid == 0) {
       const uint64_t t0 = globaltimer_ns();
       mbar_wait_bounded(&sm.full[st], r.round() & 1u, s, kErrFullTimeout);
       wait_ns += globaltimer_ns() - t0;
@@ -419,7 +424,7 @@ struct Consumer {
   // which: 0 = phase start, 1 = inputs ready, 2 = phase end (also records
   // the tile-wait time and the number of tiles consumed)
   __device__ __forceinline__ void stamp(int phase, int which) {
-    if (a.trace && tid == 0) {
+    if (kTrace && tid == 0) {
       int64_t* t = a.trace + ((size_t)cta * a.n_phases + phase) * kTraceFields;
       t[which] = (int64_t)globaltimer_ns();
       if (which == 0) it_at_start = r.it;
@@ -481,15 +486,14 @@ struct Consumer {
     }
   }
 
-  // This warp's slice of the phase input vector:
+  // The phase input vector:
   //   v = x (or the token's embedding row) [+ x2, rounded]; optionally
   //   RMSNorm with HF's rounding points (modeling_qwen3_vl.py:398-403).
-  // Every warp covers the whole vector across its lanes, so the sum of
-  // squares is a warp reduction and no block synchronisation is needed.
-  // C == 1: the lane's 64 values stay in registers (x0).  C > 1: they go to
-  // sm.nw (each lane later reads back only what it wrote; all warps write
-  // the same values) -- the norm prologue is limited to k <= 2048.
-  // Columns at or beyond k read as zero.
+  // The warps load (or poll) disjoint slices and meet at one consumer
+  // barrier; the sum of squares is reduced per warp and then over the 8
+  // warps.  C == 1: each lane ends with its 64 values in registers (x0).
+  // C > 1: the vector stays in sm.nw -- the norm prologue is limited to
+  // k <= 2048.  Columns at or beyond k read as zero.
   template <int C>
   __device__ __forceinline__ void build_x(const AicasPhase& d, uint4 (&x0)[kVec]) {
     const int k = d.k, flags = d.flags;
@@ -499,13 +503,16 @@ struct Consumer {
     const bool ll = flags & AICAS_F_LL_IN;
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(d.x);
     const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
-    // this lane's vectors: (c, j) with col = c*2048 + j*256 + lane*8; for C > 1
-    // the 8 warps split them and share the result through sm.nw
-    constexpr int NV = C == 1 ? kVec : (C * kVec + kConsumerWarps - 1) / kConsumerWarps;
+    // The 8 warps split the input: vector index v = c*kVec + j covers
+    // columns c*2048 + j*256 + [lane*8, lane*8 + 8), and warp w takes
+    // v = w, w + 8, ...  Each CTA so reads (polls) the vector once, not once
+    // per warp.  C == 1: the vector goes to sm.xs and every warp reads its
+    // lanes' 64 values back into registers (x0); C > 1: to sm.nw.
+    constexpr int NV = (C * kVec + kConsumerWarps - 1) / kConsumerWarps;
     int cols[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int v = C == 1 ? i : i * kConsumerWarps + w;  // vector index c*kVec + j
+      const int v = i * kConsumerWarps + w;
       const int col = (v / kVec) * kChunk + (v % kVec) * 256 + lane * 8;
       cols[i] = (v < C * kVec && col < k) ? col : -1;
     }
@@ -517,6 +524,7 @@ struct Consumer {
       for (int i = 0; i < NV; ++i) raw[i] = cols[i] >= 0 ? ldcg_u4(x + cols[i]) : make_uint4(0, 0, 0, 0);
     }
     float ss = 0.f;
+    __half* xbuf = C == 1 ? sm.xs : sm.nw;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       if (cols[i] < 0) continue;
@@ -537,17 +545,28 @@ struct Consumer {
           const float2 f = __half22float2(hp[q]);
           ss += f.x * f.x + f.y * f.y;
         }
-      } else {
-        *reinterpret_cast<uint4*>(&sm.nw[cols[i]]) = raw[i];
       }
+      *reinterpret_cast<uint4*>(&xbuf[cols[i]]) = raw[i];
     }
+    if (C == 1 && (flags & AICAS_F_NORM)) {
+      ss = warp_sum(ss);
+      if (lane == 0) sm.ssq[w] = ss;
+    }
+    consumer_sync(kConsumerThreads);
     if constexpr (C == 1) {
 #pragma unroll
-      for (int j = 0; j < kVec; ++j) x0[j] = raw[j];
+      for (int j = 0; j < kVec; ++j) {
+        const int col = j * 256 + lane * 8;
+        x0[j] = col < k ? *reinterpret_cast<const uint4*>(&sm.xs[col]) : make_uint4(0, 0, 0, 0);
+      }
+      if (flags & AICAS_F_NORM) {
+        ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kConsumerWarps; ++i) ss += sm.ssq[i];
+      }
     }
-    if (C > 1) consumer_sync(kConsumerThreads);
     if (C == 1 && (flags & AICAS_F_NORM)) {
-      const float inv = rsqrtf(warp_sum(ss) / (float)k + d.eps);
+      const float inv = rsqrtf(ss / (float)k + d.eps);
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
         const int col = j * 256 + lane * 8;
@@ -726,7 +745,7 @@ struct Consumer {
     const uint32_t empty_s = smem_addr(&sm.empty[0]);
     AicasScratch* const scr = s;
     const int ln = lane, wp = w;
-    const bool timing = a.trace != nullptr && tid == 0;
+    const bool timing = kTrace && tid == 0;
     uint64_t waited = 0;
     uint32_t it = r.it;
 #define AICAS_TAKE(st)                                                                          \
@@ -755,8 +774,8 @@ struct Consumer {
         for (int rr = 0; rr < kRowsPerWarp; ++rr)
 #pragma unroll
           for (int q = 0; q < 4; ++q) acc[g][rr][q] = 0.f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
+#pragma unroll 1
+      for (int c = 0; c < C; ++c) {  // not unrolled: one copy of the tile code per group
         x_chunk<C>(c, k, x0, xh);
         const unsigned jmask = c < C - 1 ? 0xffu : jlast;
 #pragma unroll
@@ -806,7 +825,7 @@ struct Consumer {
 #pragma unroll
         for (int part = 0; part < (C == 1 ? 2 : 1); ++part) {  // gate_up: k <= 2048 (host-checked)
           if (part == 1 && !gateup) break;
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < C; ++c) {
             if (C > 1) x_chunk<C>(c, k, x0, xh);
             const unsigned jmask = c < C - 1 ? 0xffu : jlast;
@@ -950,19 +969,13 @@ struct Consumer {
     __half* kc = reinterpret_cast<__half*>(d.k_cache);
     __half* vc = reinterpret_cast<__half*>(d.v_cache);
     const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
-    // interleaved MRoPE cos/sin of this lane's 4 dims (modeling_qwen3_vl.py:352-386)
+    // interleaved MRoPE cos/sin of this lane's 4 dims (table built by init_rope)
     float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
     if (!q_ready) {
-      const AicasStepState* stt = a.state;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = (lane * 4 + e) % (kHD / 2);
-        int axis = 0;
-        if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
-        else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
-        const float ang = stt->inv_freq[i] * (float)in.rope[axis];
-        cs[e] = r16(cosf(ang));
-        sn[e] = r16(sinf(ang));
+        cs[e] = at.rope_c[(lane * 4 + e) % (kHD / 2)];
+        sn[e] = at.rope_s[(lane * 4 + e) % (kHD / 2)];
       }
     }
     const float scale = d.scale;
@@ -1201,7 +1214,26 @@ struct Consumer {
     }
   }
 
+  // Interleaved-MRoPE cos/sin of the step's position, once per launch
+  // (every attention phase of the step uses the same table):
+  // frequency i takes axis 1 (h) when i % 3 == 1 and i < 3 * section[1],
+  // axis 2 (w) when i % 3 == 2 and i < 3 * section[2], else axis 0 (t);
+  // cos/sin in fp32, rounded to fp16 (modeling_qwen3_vl.py:352-386).
+  __device__ __noinline__ void init_rope() {
+    const AicasStepState* stt = a.state;
+    if (stt && tid < kHD / 2) {
+      const int i = tid;
+      int axis = 0;
+      if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
+      else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
+      const float ang = stt->inv_freq[i] * (float)in.rope[axis];
+      sm.at.rope_c[i] = r16(cosf(ang));
+      sm.at.rope_s[i] = r16(sinf(ang));
+    }
+  }
+
   __device__ __forceinline__ void run(const AicasPhase* P, int n_phases) {
+    init_rope();  // visible after the first phase's consumer barrier
     for (ph = 0; ph < n_phases; ++ph) {
       const AicasPhase& d = P[ph];
       // every warp is done with the previous phase's shared buffers
@@ -1229,6 +1261,9 @@ struct Consumer {
   }
 };
 
+// kTrace: the traced variant records per-phase timestamps (a.trace); the
+// plain one carries none of that code.
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1253,10 +1288,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   const AicasPhase* P = a.phases ? a.phases : a.inl;
   const int warp = threadIdx.x / 32;
   if (warp == 0) {
-    run_producer(a, sm, in);
+    run_producer<kTrace>(a, sm, in);
     return;
   }
-  Consumer c{a, sm, in, a.scratch};
+  Consumer<kTrace> c{a, sm, in, a.scratch};
   c.tid = threadIdx.x - 32;
   c.w = warp - 1;
   c.lane = threadIdx.x & 31;
@@ -1293,13 +1328,16 @@ static int device_setup(int* dev_out) {
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
   if (!g_attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sizeof(Smem));
-    if (e != cudaSuccess) return cuda_fail(e);
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_program_kernel, kThreads, sizeof(Smem));
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (per_sm < 1) return cuda_fail(cudaErrorLaunchOutOfResources);
+    for (int v = 0; v < 2; ++v) {
+      const void* fn = v ? reinterpret_cast<const void*>(decode_program_kernel<true>)
+                         : reinterpret_cast<const void*>(decode_program_kernel<false>);
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+      if (e != cudaSuccess) return cuda_fail(e);
+      int per_sm = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, sizeof(Smem));
+      if (e != cudaSuccess) return cuda_fail(e);
+      if (per_sm < 1) return cuda_fail(cudaErrorLaunchOutOfResources);
+    }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
     g_num_sms[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
@@ -1372,7 +1410,8 @@ static int launch_program(ProgramArgs& a, cudaStream_t stream) {
   attr[0].val.cooperative = g_cooperative;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_program_kernel, a);
+  cudaError_t e = a.trace ? cudaLaunchKernelEx(&cfg, decode_program_kernel<true>, a)
+                          : cudaLaunchKernelEx(&cfg, decode_program_kernel<false>, a);
   return e == cudaSuccess ? AICAS_OK : cuda_fail(e);
 }
 
