@@ -103,7 +103,9 @@ struct ProgramArgs {
   AicasPhase inl[4];
 };
 
-constexpr int kTraceFields = 6;  // start, inputs ready, end, consumer tile-wait ns, producer slot-wait ns, tiles
+// start, inputs ready, end, consumer tile-wait ns, producer slot-wait ns,
+// tiles, compute done, results issued
+constexpr int kTraceFields = 8;
 
 struct StepIn {
   int64_t token;
@@ -434,6 +436,13 @@ struct Consumer {
         wait_ns = 0;
       }
     }
+  }
+
+  // Extra timestamps of the traced variant: field 6 = this CTA's own compute
+  // done (last tile or attention unit), field 7 = results issued (attention:
+  // partial stored, or all splits merged by the merging CTA).
+  __device__ __forceinline__ void stamp_field(int field) {
+    if (kTrace && tid == 0) a.trace[((size_t)cta * a.n_phases + ph) * kTraceFields + field] = (int64_t)globaltimer_ns();
   }
 
   // Token id of the step, checked against the embedding table (an
@@ -859,6 +868,7 @@ struct Consumer {
     }
 #undef AICAS_TAKE
 #undef AICAS_GIVE
+    stamp_field(7);
     wait_ns += waited;
     r.it = it;
     if (kind == AICAS_PH_LMHEAD) finish_argmax(d, best_v, best_i);
@@ -1109,6 +1119,7 @@ struct Consumer {
       }
       release(st);
       if (seg_end) {
+        stamp_field(6);
         // merge the 8 warps' states of this segment into one partial
         if (lane == 0) {
           at.wm[w][0] = m[0];
@@ -1149,6 +1160,7 @@ struct Consumer {
           // 64-bit LL stores: the merging CTA polls them, no fence or counter
           if (t == 0) ll64_store(pp + split * kSplitStride, lse, ep);
           ll64_store(pp + split * kSplitStride + 1 + t, o, ep);
+          stamp_field(7);
         } else {
           // the head's last owner merges: its own partial, then splits
           // 0 .. nsplit-2 in order, kMergeBatch per polling round (all loads
@@ -1160,21 +1172,23 @@ struct Consumer {
           for (int b0 = 0; b0 < nsplit - 1; b0 += kMergeBatch) {
             const int cnt = min(kMergeBatch, nsplit - 1 - b0);
             uint64_t lw = 0, ow[kMergeBatch];
+            // only words not yet seen with this phase's epoch are reloaded
+            bool lpend = lane < cnt;
+            uint32_t pend = (1u << cnt) - 1u;
             uint64_t t0 = 0;
             for (uint32_t it = 0;; ++it) {
-              bool ok = true;
-              if (lane < cnt) {
+              if (lpend) {
                 lw = ll64_load(pp + (b0 + lane) * kSplitStride);
-                ok = ll64_epoch(lw) == ep;
+                lpend = ll64_epoch(lw) != ep;
               }
 #pragma unroll
               for (int i = 0; i < kMergeBatch; ++i) {
-                if (i < cnt) {
+                if (pend & (1u << i)) {
                   ow[i] = ll64_load(pp + (b0 + i) * kSplitStride + 1 + t);
-                  ok = ok && ll64_epoch(ow[i]) == ep;
+                  if (ll64_epoch(ow[i]) == ep) pend &= ~(1u << i);
                 }
               }
-              if (__all_sync(0xffffffffu, ok)) break;
+              if (__all_sync(0xffffffffu, !lpend && pend == 0u)) break;
               if (it == 0) t0 = globaltimer_ns();
               if ((it & 31u) == 31u) {
                 bool give_up = ld_volatile_int(&s->abort) != 0;
@@ -1204,6 +1218,7 @@ struct Consumer {
               }
             }
           }
+          stamp_field(7);
           const int oidx = (h * 2 + g) * kHD + t;
           if (d.flags & AICAS_F_LL_OUT)
             ll_store(reinterpret_cast<uint32_t*>(d.out) + oidx, acc / S, ep & 0xffffu);

@@ -232,9 +232,10 @@ class Qwen3VLDecodeEngine:
 
     def launch_traced(self) -> torch.Tensor:
         """One step with per-CTA per-phase %globaltimer stamps; returns the
-        trace [num_ctas, n_phases, 6] (start, inputs ready, end, consumer
-        tile-wait ns, producer slot-wait ns, tiles) after synchronising."""
-        trace = torch.zeros((self.num_ctas, self.n_phases, 6), dtype=torch.int64, device=self.device)
+        trace [num_ctas, n_phases, 8] (start, inputs ready, end, consumer
+        tile-wait ns, producer slot-wait ns, tiles, compute done, results
+        issued) after synchronising."""
+        trace = torch.zeros((self.num_ctas, self.n_phases, 8), dtype=torch.int64, device=self.device)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         rc = self._lib.aicas_decode_program_trace_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
                                                       ctypes.c_void_p(self.state_dev.data_ptr()),

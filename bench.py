@@ -304,7 +304,7 @@ def write_trace_summary(eng, start_state, path):
     import torch
 
     eng.restore(start_state)
-    tr = eng.launch_traced().double()  # [cta, phase, 6]
+    tr = eng.launch_traced().double()  # [cta, phase, 8]
     names = eng.phase_names()
     t0 = tr[:, 0, 0].min()
     start, ready, end = tr[:, :, 0] - t0, tr[:, :, 1] - t0, tr[:, :, 2] - t0

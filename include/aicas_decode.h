@@ -158,12 +158,15 @@ AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, const void* k
                                                    int32_t* status, aicas_stream_t stream);
 
 /* Profiling variant of aicas_decode_program_f16: additionally writes, per
- * CTA and phase, trace[cta][phase][6] (int64, aicas_num_ctas() * n_phases * 6
+ * CTA and phase, trace[cta][phase][8] (int64, aicas_num_ctas() * n_phases * 8
  * entries): the %globaltimer (ns) when the phase started, when its inputs
  * were ready, when it finished; the ns one consumer warp spent waiting for
  * weight/KV tiles to land; the ns the producer spent waiting for free ring
- * slots while issuing the phase's tiles; and the number of tiles consumed.  The reference records the same
- * kind of per-block timelines in its `*_profile_*` kernel variants
+ * slots while issuing the phase's tiles; the number of tiles consumed; and
+ * (ns) when the CTA's own attention units were computed, and when its
+ * results were issued (attention partial stored / splits merged; GEMV: tile
+ * loops done).  The reference records the same kind of per-block timelines
+ * in its `*_profile_*` kernel variants
  * (cuda_extensions/decode_gemv_kernel_common.cuh:174-188). */
 AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, int n_phases,
                                              AicasStepState* state, void* scratch, int64_t* trace,
