@@ -79,6 +79,7 @@ struct AttnSmem {
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
   float rope_c[kHD / 2], rope_s[kHD / 2];  // this launch's MRoPE cos/sin (fp16-rounded)
+  float sc[kConsumerWarps][2 * kPosPerWarp];  // raw q.k scores of each warp's positions
 };
 
 struct __align__(128) Smem {
@@ -134,6 +135,23 @@ __device__ __forceinline__ int owner_of(int u, int total, int nct) {
   return extra + (u - big) / base;
 }
 
+// CTAs taking part in an attention phase of U units (KV head x 64-slot
+// chunk): each gets at least kAttnMinUnits units (fewer partials to merge,
+// but more serial unit work per CTA).  CTAs [0, attn_ctas) take part.
+// Measured on B200 (1024-slot prefix): 1 unit 1258 us/token, 2: 1281,
+// 3: 1500, 4: 1641, so the default keeps one unit per CTA.
+#ifndef AICAS_ATTN_MIN_UNITS
+#define AICAS_ATTN_MIN_UNITS 1
+#endif
+constexpr int kAttnMinUnits = AICAS_ATTN_MIN_UNITS;
+__device__ __forceinline__ int attn_ctas(int U, int nct) {
+  return max(1, min(nct, (U + kAttnMinUnits - 1) / kAttnMinUnits));
+}
+__device__ __forceinline__ Range attn_range(int U, int nct, int cta) {
+  const int na = attn_ctas(U, nct);
+  return cta < na ? split_range(U, na, cta, 0) : Range{0, 0};
+}
+
 // Attention covers cache slots [0, valid); 0 when the position is outside
 // the cache (the phase is then skipped by producer and consumers alike and
 // kErrBadInput is raised).
@@ -154,8 +172,8 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
 // the input vector is needed in fp32 registers at a time.  Producer and
 // consumers both call this to agree on the tile order.
 constexpr int kMaxCmajorGroups = 2;
-// split-KV merge: partials polled per round by the merging CTA
-constexpr int kMergeBatch = 16;
+// split-KV merge: splits whose partial words one merging thread polls per round
+constexpr int kMergeBatch = 8;
 __device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
   return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
 }
@@ -206,7 +224,7 @@ struct TileCursor {
     if (kind == AICAS_PH_ATTN) {
       valid = phase_valid_len(d, in);
       cph = (valid + kAttnChunk - 1) / kAttnChunk;
-      rg = split_range(d.kv_heads * cph, nct, cta, 0);  // empty when valid == 0
+      rg = attn_range(d.kv_heads * cph, nct, cta);  // empty when valid == 0
       n = rg.count;
     } else if (kind == AICAS_PH_GEMV || kind == AICAS_PH_GATEUP || kind == AICAS_PH_LMHEAD) {
       C = n_chunks(d);
@@ -971,7 +989,7 @@ struct Consumer {
     const int pos = valid - 1;
     const int cph = (valid + kAttnChunk - 1) / kAttnChunk;
     const int U = d.kv_heads * cph;
-    const Range rg = split_range(U, nct, cta, 0);
+    const Range rg = attn_range(U, nct, cta);
     const __half* qkv = reinterpret_cast<const __half*>(d.x);
     const bool ll_in = d.flags & AICAS_F_LL_IN;
     const uint32_t* qkv_w = reinterpret_cast<const uint32_t*>(d.x);
@@ -1071,22 +1089,18 @@ struct Consumer {
               qreg[g][0] * kv[i][0] + qreg[g][1] * kv[i][1] + qreg[g][2] * kv[i][2] + qreg[g][3] * kv[i][3];
       int vidx;
       const float tot = reduce_scatter<2 * kPosPerWarp>(part, vidx);
-      (void)vidx;
-      float sc[2][kPosPerWarp];
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-#pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i)
-          sc[g][i] = __shfl_sync(0xffffffffu, tot, scatter_lane<2 * kPosPerWarp>(g * kPosPerWarp + i));
+      // the 16 scores (value index g * kPosPerWarp + i) go to shared memory,
+      // so the softmax below is a compact loop rather than unrolled code:
+      // this runs once per layer, on cold instruction cache lines
+      if ((lane & 1) == 0) at.sc[w][vidx] = tot;
+      __syncwarp();
+      const int pw = p0 + w * kPosPerWarp;  // this warp's first position
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
         float cmax = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i) {
-          const int p = p0 + w * kPosPerWarp + i;
-          sc[g][i] = (p < valid) ? sc[g][i] * scale : -INFINITY;
-          cmax = fmaxf(cmax, sc[g][i]);
-        }
+        for (int i = 0; i < kPosPerWarp; ++i)
+          if (pw + i < valid) cmax = fmaxf(cmax, at.sc[w][g * kPosPerWarp + i] * scale);
         const float mn = fmaxf(m[g], cmax);
         if (mn == -INFINITY) continue;
         const float corr = expf(m[g] - mn);
@@ -1094,27 +1108,31 @@ struct Consumer {
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
         m[g] = mn;
+      }
+      // one V row per position serves both query heads
+#pragma unroll 1
+      for (int i = 0; i < kPosPerWarp && pw + i < valid; ++i) {
+        const int p = pw + i;
+        float vv[4];
+        if (!q_ready && p == pos) {
 #pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i) {
-          const int p = p0 + w * kPosPerWarp + i;
-          if (p < valid) {
-            const float pr = expf(sc[g][i] - mn);
-            l[g] += pr;
-            float vv[4];
-            if (!q_ready && p == pos) {
+          for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
+        } else {
+          const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
+          const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+          vv[0] = __low2float(vh[0]);
+          vv[1] = __high2float(vh[0]);
+          vv[2] = __low2float(vh[1]);
+          vv[3] = __high2float(vh[1]);
+        }
+        const float pr0 = expf(at.sc[w][i] * scale - m[0]);
+        const float pr1 = expf(at.sc[w][kPosPerWarp + i] * scale - m[1]);
+        l[0] += pr0;
+        l[1] += pr1;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
-            } else {
-              const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
-              const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-              vv[0] = __low2float(vh[0]);
-              vv[1] = __high2float(vh[0]);
-              vv[2] = __low2float(vh[1]);
-              vv[3] = __high2float(vh[1]);
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[g][e] += pr * vv[e];
-          }
+        for (int e = 0; e < 4; ++e) {
+          acc[0][e] += pr0 * vv[e];
+          acc[1][e] += pr1 * vv[e];
         }
       }
       release(st);
@@ -1132,8 +1150,9 @@ struct Consumer {
 #pragma unroll
           for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
         consumer_sync(kConsumerThreads);
-        const int first_owner = owner_of(h * cph, U, nct);
-        const int last_owner = owner_of(h * cph + cph - 1, U, nct);
+        const int na = attn_ctas(U, nct);
+        const int first_owner = owner_of(h * cph, U, na);
+        const int last_owner = owner_of(h * cph + cph - 1, U, na);
         const int split = cta - first_owner;
         const int nsplit = last_owner - first_owner + 1;
         const uint32_t ep = epoch_base + (uint32_t)ph + 1;
@@ -1144,7 +1163,7 @@ struct Consumer {
 #pragma unroll
         for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
         float L = 0.f, A = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < kConsumerWarps; ++i) {
           const float mi = at.wm[i][g];
           if (mi != -INFINITY) {
@@ -1153,77 +1172,82 @@ struct Consumer {
             A += at.wacc[i][g][t] * f;
           }
         }
-        float lse = M + logf(L), o = A / L;
-        uint64_t* pp = &s->part[h][0][g][0];
-        constexpr int kSplitStride = 2 * (kHD + 1);
-        if (cta != last_owner) {
-          // 64-bit LL stores: the merging CTA polls them, no fence or counter
-          if (t == 0) ll64_store(pp + split * kSplitStride, lse, ep);
-          ll64_store(pp + split * kSplitStride + 1 + t, o, ep);
+        const float lse = M + logf(L), o = A / L;
+        uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out);
+        __half* const out_h = reinterpret_cast<__half*>(d.out);
+        const bool ll_out = d.flags & AICAS_F_LL_OUT;
+        if (nsplit == 1) {  // the whole head is this CTA's: thread (g, t) has its output
+          const int oidx = (h * 2 + g) * kHD + t;
+          if (ll_out) ll_store(out_w + oidx, o, ep & 0xffffu);
+          else out_h[oidx] = __float2half_rn(o);
           stamp_field(7);
         } else {
-          // the head's last owner merges: its own partial, then splits
-          // 0 .. nsplit-2 in order, kMergeBatch per polling round (all loads
-          // of a round issued before any is checked).  Lane i of the warp
-          // loads the log-sum-exp of split b0 + i and shares it by shuffle;
-          // each thread loads its own dim's normalised acc.  The warp polls
-          // as one (uniform exit), so the shuffles stay converged.
-          float mx = lse, S = 1.f, acc = o;
-          for (int b0 = 0; b0 < nsplit - 1; b0 += kMergeBatch) {
-            const int cnt = min(kMergeBatch, nsplit - 1 - b0);
-            uint64_t lw = 0, ow[kMergeBatch];
-            // only words not yet seen with this phase's epoch are reloaded
-            bool lpend = lane < cnt;
-            uint32_t pend = (1u << cnt) - 1u;
-            uint64_t t0 = 0;
-            for (uint32_t it = 0;; ++it) {
-              if (lpend) {
-                lw = ll64_load(pp + (b0 + lane) * kSplitStride);
-                lpend = ll64_epoch(lw) != ep;
+          // 1) this CTA's partial as 64-bit LL words (no fence, no counter)
+          uint64_t* const hp = &s->part[h][0][0][0];  // [split][g][log-sum-exp, acc[128]]
+          constexpr int kSplitStride = 2 * (kHD + 1);
+          if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
+          ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
+          // 2) every CTA of the head merges a 1/nsplit slice of its 256
+          // outputs, one thread per output, over splits 0..nsplit-1 in order
+          // (the same order whichever CTA merges).  A CTA only waits for
+          // partials of its current head, which every owner stores before it
+          // waits on anything later, so the waits cannot form a cycle.
+          const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
+          if (tid < q1 - q0) {
+            const int q = q0 + tid, gq = q / kHD, tq = q % kHD;
+            const uint64_t* const base = hp + gq * (kHD + 1);
+            float mx = -INFINITY, S = 0.f, acc = 0.f;
+            for (int b0 = 0; b0 < nsplit; b0 += kMergeBatch) {
+              const int cnt = min(kMergeBatch, nsplit - b0);
+              uint64_t lw[kMergeBatch], ow[kMergeBatch];
+              // words not yet seen with this phase's epoch are reloaded
+              uint32_t lpend = (1u << cnt) - 1u, opend = lpend;
+              uint64_t t0 = 0;
+              for (uint32_t it = 0;; ++it) {
+#pragma unroll
+                for (int i = 0; i < kMergeBatch; ++i) {
+                  const uint64_t* sp = base + (b0 + i) * kSplitStride;
+                  if (lpend & (1u << i)) {
+                    lw[i] = ll64_load(sp);
+                    if (ll64_epoch(lw[i]) == ep) lpend &= ~(1u << i);
+                  }
+                  if (opend & (1u << i)) {
+                    ow[i] = ll64_load(sp + 1 + tq);
+                    if (ll64_epoch(ow[i]) == ep) opend &= ~(1u << i);
+                  }
+                }
+                if ((lpend | opend) == 0u) break;
+                if (it == 0) t0 = globaltimer_ns();
+                if ((it & 31u) == 31u) {
+                  if (ld_volatile_int(&s->abort)) break;
+                  if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    raise_error(s, kErrInputTimeout);
+                    break;
+                  }
+                }
               }
 #pragma unroll
               for (int i = 0; i < kMergeBatch; ++i) {
-                if (pend & (1u << i)) {
-                  ow[i] = ll64_load(pp + (b0 + i) * kSplitStride + 1 + t);
-                  if (ll64_epoch(ow[i]) == ep) pend &= ~(1u << i);
-                }
-              }
-              if (__all_sync(0xffffffffu, !lpend && pend == 0u)) break;
-              if (it == 0) t0 = globaltimer_ns();
-              if ((it & 31u) == 31u) {
-                bool give_up = ld_volatile_int(&s->abort) != 0;
-                if (!give_up && globaltimer_ns() - t0 > kWaitLimitNs) {
-                  raise_error(s, kErrInputTimeout);
-                  give_up = true;
-                }
-                if (__any_sync(0xffffffffu, give_up)) break;
-              }
-            }
-            const float lmine = ll64_value(lw);
-#pragma unroll
-            for (int i = 0; i < kMergeBatch; ++i) {
-              const float li = __shfl_sync(0xffffffffu, lmine, i);
-              if (i < cnt) {
-                const float oi = ll64_value(ow[i]);
-                if (li > mx) {
-                  const float c = expf(mx - li);
-                  S = S * c + 1.f;
-                  acc = acc * c + oi;
-                  mx = li;
-                } else {
-                  const float c = expf(li - mx);
-                  S += c;
-                  acc += c * oi;
+                if (i < cnt) {
+                  const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
+                  if (li > mx) {
+                    const float c = expf(mx - li);
+                    S = S * c + 1.f;
+                    acc = acc * c + oi;
+                    mx = li;
+                  } else {
+                    const float c = expf(li - mx);
+                    S += c;
+                    acc += c * oi;
+                  }
                 }
               }
             }
+            const int oidx = (h * 2 + gq) * kHD + tq;
+            if (ll_out) ll_store(out_w + oidx, acc / S, ep & 0xffffu);
+            else out_h[oidx] = __float2half_rn(acc / S);
           }
           stamp_field(7);
-          const int oidx = (h * 2 + g) * kHD + t;
-          if (d.flags & AICAS_F_LL_OUT)
-            ll_store(reinterpret_cast<uint32_t*>(d.out) + oidx, acc / S, ep & 0xffffu);
-          else
-            reinterpret_cast<__half*>(d.out)[oidx] = __float2half_rn(acc / S);
         }
       }
     }
