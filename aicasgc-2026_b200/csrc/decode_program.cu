@@ -172,8 +172,8 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
 // the input vector is needed in fp32 registers at a time.  Producer and
 // consumers both call this to agree on the tile order.
 constexpr int kMaxCmajorGroups = 2;
-// split-KV merge: splits whose partial words one merging thread polls per round
-constexpr int kMergeBatch = 8;
+// split-KV merge: splits whose partial words one merging lane polls per round
+constexpr int kMergePer = 4;
 __device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
   return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
 }
@@ -1192,29 +1192,48 @@ struct Consumer {
           // (the same order whichever CTA merges).  A CTA only waits for
           // partials of its current head, which every owner stores before it
           // waits on anything later, so the waits cannot form a cycle.
+          // Each output is merged by a group of tpo lanes (a power of two
+          // <= 16, as many as the CTA's threads allow): lane `sub` of the
+          // group takes splits sub, sub + tpo, ... in order, polling up to
+          // kMergePer of them per round, then the group combines its
+          // (max, sum, acc) triples with a fixed xor-shuffle tree.
           const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
-          if (tid < q1 - q0) {
-            const int q = q0 + tid, gq = q / kHD, tq = q % kHD;
+          const int npairs = q1 - q0;
+          int tpo = 16;
+          while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
+          const int nact = npairs * tpo;
+          if ((tid & ~31) < nact) {  // warps holding at least one active lane
+            const bool act = tid < nact;
+            const int pl = tid / tpo, sub = tid % tpo;
+            const int q = q0 + (act ? pl : 0), gq = q / kHD, tq = q % kHD;
             const uint64_t* const base = hp + gq * (kHD + 1);
             float mx = -INFINITY, S = 0.f, acc = 0.f;
-            for (int b0 = 0; b0 < nsplit; b0 += kMergeBatch) {
-              const int cnt = min(kMergeBatch, nsplit - b0);
-              uint64_t lw[kMergeBatch], ow[kMergeBatch];
-              // words not yet seen with this phase's epoch are reloaded
-              uint32_t lpend = (1u << cnt) - 1u, opend = lpend;
-              uint64_t t0 = 0;
-              for (uint32_t it = 0;; ++it) {
+#pragma unroll 1
+            for (int b0 = act ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
+              uint64_t lw[kMergePer], ow[kMergePer];
+              uint32_t lpend = 0u;
 #pragma unroll
-                for (int i = 0; i < kMergeBatch; ++i) {
-                  const uint64_t* sp = base + (b0 + i) * kSplitStride;
-                  if (lpend & (1u << i)) {
-                    lw[i] = ll64_load(sp);
-                    if (ll64_epoch(lw[i]) == ep) lpend &= ~(1u << i);
-                  }
-                  if (opend & (1u << i)) {
-                    ow[i] = ll64_load(sp + 1 + tq);
-                    if (ll64_epoch(ow[i]) == ep) opend &= ~(1u << i);
-                  }
+              for (int i = 0; i < kMergePer; ++i)
+                if (b0 + i * tpo < nsplit) lpend |= 1u << i;
+              uint32_t opend = lpend;
+              const uint32_t have = lpend;
+              uint64_t t0 = 0;
+#pragma unroll 1
+              for (uint32_t it = 0;; ++it) {
+                // predicates from the round's starting masks: no load waits
+                // for another load's result, so a round is one round trip
+                const uint32_t lp = lpend, op = opend;
+#pragma unroll
+                for (int i = 0; i < kMergePer; ++i) {
+                  const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
+                  if (lp & (1u << i)) lw[i] = ll64_load(sp);
+                  if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
+                }
+                lpend = opend = 0u;
+#pragma unroll
+                for (int i = 0; i < kMergePer; ++i) {
+                  if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
+                  if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
                 }
                 if ((lpend | opend) == 0u) break;
                 if (it == 0) t0 = globaltimer_ns();
@@ -1227,8 +1246,8 @@ struct Consumer {
                 }
               }
 #pragma unroll
-              for (int i = 0; i < kMergeBatch; ++i) {
-                if (i < cnt) {
+              for (int i = 0; i < kMergePer; ++i) {
+                if (have & (1u << i)) {
                   const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
                   if (li > mx) {
                     const float c = expf(mx - li);
@@ -1243,9 +1262,24 @@ struct Consumer {
                 }
               }
             }
-            const int oidx = (h * 2 + gq) * kHD + tq;
-            if (ll_out) ll_store(out_w + oidx, acc / S, ep & 0xffffu);
-            else out_h[oidx] = __float2half_rn(acc / S);
+            for (int o = 1; o < tpo; o <<= 1) {  // tpo is the same in every lane
+              const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
+              const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
+              const float a2 = __shfl_xor_sync(0xffffffffu, acc, o);
+              const float mm = fmaxf(mx, m2);
+              if (mm != -INFINITY) {
+                const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
+                const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
+                S = S * f1 + s2 * f2;
+                acc = acc * f1 + a2 * f2;
+                mx = mm;
+              }
+            }
+            if (act && sub == 0) {
+              const int oidx = (h * 2 + gq) * kHD + tq;
+              if (ll_out) ll_store(out_w + oidx, acc / S, ep & 0xffffu);
+              else out_h[oidx] = __float2half_rn(acc / S);
+            }
           }
           stamp_field(7);
         }
