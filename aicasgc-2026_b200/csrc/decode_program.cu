@@ -1451,6 +1451,7 @@ static int validate_phase(const AicasPhase& d) {
       if (!d.k_cache || !d.v_cache || !aligned16(d.k_cache) || !aligned16(d.v_cache)) return AICAS_ERR_ALIGN;
       if (!d.x || !d.out) return AICAS_ERR_ARG;
       if (!(d.flags & AICAS_F_Q_READY) && (!d.norm_w || !d.norm_w2)) return AICAS_ERR_ARG;
+      if (!(d.flags & AICAS_F_Q_READY) && (!aligned16(d.norm_w) || !aligned16(d.norm_w2))) return AICAS_ERR_ALIGN;
       if ((d.flags & AICAS_F_LL_IN) && ((d.flags & AICAS_F_Q_READY) || d.x_src < 0)) return AICAS_ERR_ARG;
       return AICAS_OK;
     default:
