@@ -169,6 +169,12 @@ def run_reference(args, rank: int, world: int):
 
 
 # --------------------------------------------------------------------------- GPU
+# DRAM bytes per algorithmic byte of decode_program_kernel, from one
+# `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
+# summarised under profiles/): (1.043270e9 + 6.391296e6) / 1043908608.  The
+# per-layer shapes equal the headline model's, so the ratio carries over.
+DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0055107
+
 def run_ours(args, rank: int, world: int):
     import torch
     import torch.distributed as dist
@@ -275,7 +281,11 @@ def run_ours(args, rank: int, world: int):
         "config": workload_config(world),
         "step_us_per_token": 1000.0 * ms / (args.steps * NEW),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_req / NEW,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 4-layer "
+                                       "launch (1.0433 GB + 6.4 MB vs 1.0439 GB algorithmic), scaled to this "
+                                       "launch by algorithmic bytes",
                      "kernel": "decode_program_kernel (one launch per token)",
                      "algorithmic_bytes_per_launch": bytes_req / NEW},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 8 * NEW,
