@@ -168,6 +168,25 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def max_over_ranks(vals, world: int):
+    """Per-rank timings -> their maximum over all ranks (every rank gets it).
+    Under torchrun each rank decodes its own request on its own GPU; the job
+    takes as long as its slowest rank."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def job_throughput(steps: int, world: int, ms: float) -> float:
+    """Whole-job tok/s: every rank decodes `steps` requests of NEW tokens in
+    `ms` (the max over ranks)."""
+    return steps * NEW * world / (ms / 1000.0)
+
+
 # --------------------------------------------------------------------------- GPU
 # DRAM bytes per algorithmic byte of decode_program_kernel, from one
 # `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
@@ -261,14 +280,9 @@ def run_ours(args, rank: int, world: int):
         write_trace_summary(eng, start_state, args.trace)
 
     # ---- max over ranks
-    vals = torch.tensor([ms, e2e_ms], dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = float(vals[0]), float(vals[1])
-
-    tokens = args.steps * NEW * world
-    value = tokens / (ms / 1000.0)
-    e2e_value = args.steps * NEW * world / (e2e_ms / 1000.0)
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world)
+    value = job_throughput(args.steps, world, ms)
+    e2e_value = job_throughput(args.steps, world, e2e_ms)
     # roofline: algorithmic bytes of the 256 launches of one request (ctx 1024..1279)
     bytes_req = sum(eng.algorithmic_bytes(PREFIX + i) for i in range(NEW))
     per_launch_s = ms / 1000.0 / (args.steps * NEW)
