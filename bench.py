@@ -116,6 +116,15 @@ class ClockSampler:
 def cpu_oracle_decode(state16, seconds: float = 12.0, min_steps: int = 2, max_steps: int | None = None):
     """Time the CPU oracle port (numpy fp32, all host threads) decoding at
     cache slot 1024 over a synthetic KV prefix.  Returns (tok/s, steps, s)."""
+    from threadpoolctl import threadpool_limits
+
+    # all host threads, also under torchrun (which sets OMP_NUM_THREADS=1)
+    threads = os.cpu_count() or 1
+    with threadpool_limits(limits=threads):
+        return _cpu_oracle_decode(state16, seconds, min_steps, max_steps)
+
+
+def _cpu_oracle_decode(state16, seconds, min_steps, max_steps):
     import numpy as np
 
     from engine import hf_inv_freq
