@@ -3,37 +3,39 @@
 // One launch runs a list of phases (aicas_phase_program.h) with one CTA per SM:
 //   warp 0      producer: streams every tile this CTA will consume, phase after
 //               phase, from HBM into a 6-stage shared-memory ring with bulk
-//               async copies (cp.async.bulk + mbarrier complete_tx).  It never
-//               waits on a grid barrier, so HBM keeps streaming the next
-//               phase's weights while the consumers wait for activations.
-//   warps 1..4  consumers: per phase, wait on the grid barrier, build the input
-//               vector slice they need (RMSNorm prologue with HF's fp16 rounding
-//               points, computed by every warp on its own: no block sync), then
-//               reduce each tile row against it with exact fp16 products and
-//               fp32 accumulation (two rows per warp, four independent
-//               accumulation chains per row).
+//               async copies (cp.async.bulk + mbarrier complete_tx, L2
+//               evict_first).  It never waits for activations, so HBM keeps
+//               streaming the next phases' weights while the consumers wait.
+//   warps 1..8  consumers: per phase, wait for the phase's input vector (LL
+//               flag-in-data words written by the previous phase; the warps
+//               poll disjoint slices and meet at one barrier), apply the
+//               RMSNorm prologue with HF's fp16 rounding points, then reduce
+//               each tile row against it with exact fp16 products and fp32
+//               accumulation (one row per warp, four accumulation chains).
+//   warp 9      L2 prefetch (AICAS_L2_WARP): walks the same tile schedule up
+//               to kL2Ahead tiles ahead of the producer and prefetches them
+//               into L2, so HBM keeps working while the ring is full.
 //
 // GEMV tile: 8 weight rows x 2048 columns (32 KB), fetched with ONE bulk copy
 // (rows are contiguous when k <= 2048; the engine stores down_proj K-blocked,
 // [k/2048][n][2048], so its tiles are contiguous too: bulk copies of 8 KB and
 // more are what reach full HBM bandwidth on B200, 2 KB copies top out near
-// 4 TB/s).  Consumer warp w owns rows w and w+4 of every tile; lane l the columns
+// 4 TB/s).  Consumer warp w owns row w of every tile; lane l the columns
 // j*256 + 8l (j = 0..7) of each 2048-column chunk, so a lane keeps its slice
 // of the input vector in registers for the whole phase, every weight byte is
 // read from shared memory exactly once (conflict-free 512-byte warp accesses)
 // and a row needs one warp reduction.
 //
 // Attention tile: K and V rows of 64 cache positions of one KV head (32 KB),
-// 16 positions per consumer warp.
-// Work units (KV head, 32-position chunk) are split into contiguous ranges per
-// CTA; each CTA's segment of a head yields one (max, sum, acc) partial, and the
-// last CTA to finish a head (atomic arrival count) merges its partials in a
-// fixed order, so the result does not depend on arrival order.
+// 8 positions per consumer warp.  Work units (KV head, 64-position chunk) are
+// split into contiguous ranges over the CTAs; each CTA's segment of a head
+// yields one (log-sum-exp, normalised acc) partial, stored as 64-bit LL words;
+// every CTA of the head then merges a slice of the head's outputs over all
+// partials in a fixed split order, so the result does not depend on timing.
 //
-// Grid barrier: split arrive / wait on a monotonic 64-bit counter.  Between
-// the two, every consumer prefetches what the next phase needs and no phase
-// of the program depends on: its norm weights (to shared memory) and its
-// residual rows (to registers).
+// Phases are ordered only through their LL inputs; the op-level programs
+// that need it use a grid barrier (split arrive / wait on a monotonic 64-bit
+// counter) instead.  Every wait is bounded (see aicas_device.cuh).
 //
 // Reference behaviour this replaces (file:line in the reference checkout):
 //   fused RMSNorm+QKV      cuda_extensions/decode_gemv_kernel_fused.cuh:99-185
@@ -56,7 +58,14 @@ namespace aicas {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // 288: two consumer warps per scheduler
+// AICAS_L2_WARP: 1 (default) an extra warp runs an L2 prefetch cursor ahead
+// of the ring (one bulk prefetch per tile, lines marked evict_last; the ring
+// loads mark weights and KV tiles evict_first); 2 the same with per-line
+// prefetches; 0 no prefetch warp.
+#ifndef AICAS_L2_WARP
+#define AICAS_L2_WARP 1
+#endif
+constexpr int kThreads = kConsumerThreads + 32 + (AICAS_L2_WARP ? 32 : 0);  // producer + 8 consumer warps (+ prefetch warp)
 constexpr int kRowsPerWarp = 1;
 constexpr int kRows = kConsumerWarps * kRowsPerWarp;  // weight rows per GEMV tile
 constexpr int kChunk = 2048;           // columns per GEMV tile
@@ -92,6 +101,7 @@ struct __align__(128) Smem {
   int best_i[kConsumerWarps];
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  uint32_t ring_it;  // tiles the producer has issued (read by the L2 prefetch warp)
 };
 
 struct ProgramArgs {
@@ -195,7 +205,6 @@ struct TileDesc {
   uint32_t dst_stride;
   uint32_t bytes;
   int pieces;
-  bool weights;  // weight tile (evict-first L2 policy) vs KV-cache tile
 };
 
 // Walks this CTA's tiles of a program in the exact order the consumers
@@ -254,7 +263,6 @@ struct TileCursor {
       td.dst_stride = kStageBytes / 2;
       td.bytes = rows * kHD * 2;
       td.pieces = 2;
-      td.weights = false;
     } else {
       int g, t;
       if (cmajor) {
@@ -270,7 +278,6 @@ struct TileCursor {
       const int col0 = c * kChunk;
       const uint32_t bytes = min(kChunk, d.k - col0) * 2;
       const uint8_t* W = reinterpret_cast<const uint8_t*>(d.w);
-      td.weights = true;
       if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
         td.src = W + (size_t)row0 * d.k * 2;
         td.bytes = nrows * bytes;
@@ -292,26 +299,48 @@ struct TileCursor {
   }
 };
 
-// L2 run-ahead of the producer: distance in tiles (x 32 KB x CTAs of L2)
-// and mode (0 off, 1 bulk prefetch by the copy engine, 2 one 128-byte line
-// prefetch per producer-warp lane and instruction).  Measured on B200 at
-// distances 4-32 tiles, every prefetch mode made the decode step slower
-// (1791 us/token without, 1918-2424 with), so it is off by default.
+// L2 prefetch warp: distance in tiles ahead of the producer's ring cursor.
+// Measured on B200 (1024-slot prefix, 28 layers): no prefetch 1173-1189
+// us/token; distance 6 1161-1164, 8 1154-1159, 12 1188-1205, 24 1526 (the
+// run-ahead then evicts itself from L2).  A prefetch cursor walked by the
+// producer warp itself was slower at every distance (its descriptor reads
+// delay the ring loads).
 #ifndef AICAS_L2_AHEAD
-#define AICAS_L2_AHEAD 16
-#endif
-#ifndef AICAS_L2_MODE
-#define AICAS_L2_MODE 0
+#define AICAS_L2_AHEAD 8
 #endif
 constexpr int kL2Ahead = AICAS_L2_AHEAD;
 
-__device__ __forceinline__ void l2_prefetch_tile(const TileDesc& td, int lane) {
-  if (AICAS_L2_MODE == 1) {
-    if (lane == 0)
-      for (int i = 0; i < td.pieces; ++i) bulk_prefetch_l2(td.src + i * td.src_stride, td.bytes);
-  } else if (AICAS_L2_MODE == 2) {
-    for (int i = 0; i < td.pieces; ++i)
-      for (uint32_t off = lane * 128u; off < td.bytes; off += 32u * 128u) prefetch_l2_line(td.src + i * td.src_stride + off);
+// L2 prefetch warp (AICAS_L2_WARP): walks the CTA's tile schedule at most
+// kL2Ahead tiles ahead of the producer's ring cursor and prefetches each tile
+// into L2, so HBM keeps streaming while the ring is full and the consumers
+// wait for a phase's inputs.  Only a hint: on abort or after a bounded wait it
+// stops without raising an error.
+__device__ __forceinline__ void run_l2_prefetcher(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+  const int lane = threadIdx.x & 31;
+  const AicasPhase* P = a.phases ? a.phases : a.inl;
+  TileCursor pf{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+  TileDesc td;
+  const uint64_t pol_last = l2_evict_last_policy();
+  for (uint32_t k = 0; pf.next(in, td); ++k) {
+    uint64_t t0 = 0;
+    uint32_t ri = 0;
+    for (uint32_t it = 0;; ++it) {
+      ri = *reinterpret_cast<volatile uint32_t*>(&sm.ring_it);
+      if (k < ri + (uint32_t)kL2Ahead) break;
+      if (it == 0) t0 = globaltimer_ns();
+      if ((it & 15u) == 15u && (ld_volatile_int(&a.scratch->abort) || globaltimer_ns() - t0 > kWaitLimitNs)) return;
+      __nanosleep(128);
+    }
+    if (k < ri) continue;  // the ring has already requested it
+    if (AICAS_L2_WARP == 1) {
+      if (lane == 0)
+        for (int i = 0; i < td.pieces; ++i) {
+          bulk_prefetch_l2_hint(td.src + i * td.src_stride, td.bytes, pol_last);
+        }
+    } else {
+      for (int i = 0; i < td.pieces; ++i)
+        for (uint32_t off = lane * 128u; off < td.bytes; off += 32u * 128u) prefetch_l2_line(td.src + i * td.src_stride + off);
+    }
   }
 }
 
@@ -325,14 +354,9 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   Ring r;
   const AicasPhase* P = a.phases ? a.phases : a.inl;
   TileCursor ld{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
-  TileCursor pf = ld;
   uint64_t slot_wait = 0;  // trace only
   int traced_ph = 0;
-  // Run-ahead: while the consumers wait for a phase's inputs (and the ring
-  // is full), HBM keeps filling L2 with the tiles that follow.
   TileDesc td;
-  if (AICAS_L2_MODE)
-    for (int i = 0; i < kL2Ahead && pf.next(in, td); ++i) l2_prefetch_tile(td, lane);
   while (ld.next(in, td)) {
     if (kTrace && lane == 0 && ld.ph != traced_ph) {
       a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
@@ -355,24 +379,16 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
         mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
         for (int i = 0; i < td.pieces; ++i) {
           uint8_t* dst = sm.ring[st] + i * td.dst_stride;
-          if (td.weights) bulk_g2s(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
-          else bulk_g2s_nohint(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st]);
+          bulk_g2s(dst, td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);  // weights and KV: evict_first
         }
       }
     }
     if (!__shfl_sync(0xffffffffu, good, 0)) break;
     ++r.it;
-    TileDesc tp;
-    if (AICAS_L2_MODE && pf.next(in, tp)) l2_prefetch_tile(tp, lane);
+    if (AICAS_L2_WARP && lane == 0) *reinterpret_cast<volatile uint32_t*>(&sm.ring_it) = r.it;
   }
   if (kTrace && lane == 0)
     a.trace[((size_t)blockIdx.x * a.n_phases + traced_ph) * kTraceFields + 4] = (int64_t)slot_wait;
-  // A decode step runs the same program again next launch: warm L2 with its
-  // first tiles (only a hint; the next launch fetches them regardless).
-  if (AICAS_L2_MODE && a.phases && a.state) {
-    TileCursor nx{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
-    for (int i = 0; i < kL2Ahead && nx.next(in, td); ++i) l2_prefetch_tile(td, lane);
-  }
   if (lane != 0) return;
   // Drain: every issued copy must land before this CTA may exit.  In the
   // normal path the consumers already waited for all of them.
@@ -1345,6 +1361,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kConsumerWarps);
     }
+    sm.ring_it = 0;
     mbar_fence_init();
   }
   __syncthreads();
@@ -1360,6 +1377,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   }
   const AicasPhase* P = a.phases ? a.phases : a.inl;
   const int warp = threadIdx.x / 32;
+  if (AICAS_L2_WARP && warp == 1 + kConsumerWarps) {
+    run_l2_prefetcher(a, sm, in);
+    return;
+  }
   if (warp == 0) {
     run_producer<kTrace>(a, sm, in);
     return;
