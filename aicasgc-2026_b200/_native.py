@@ -39,6 +39,8 @@ DEVICE_ERRORS = {
     13: "in-flight copies did not drain in time",
     14: "bad phase descriptor",
     15: "token id or cache position out of range",
+    16: "an input vector did not arrive in time",
+    17: "a tensor-memory slot hand-off did not complete in time",
 }
 
 

@@ -20,6 +20,7 @@ enum : int {
   kErrBadPhase = 14,         // unknown phase kind / bad descriptor
   kErrBadInput = 15,         // token id or cache position out of range
   kErrInputTimeout = 16,     // an LL input vector did not arrive in time
+  kErrTmemTimeout = 17,      // a tensor-memory slot hand-off did not complete in time
 };
 
 // Wait limit: two seconds of %globaltimer.  Far above any legal phase time
@@ -187,6 +188,67 @@ __device__ __forceinline__ bool mbar_wait_bounded_s(uint32_t bar, uint32_t parit
     }
   }
 }
+
+// ---- tensor memory (tcgen05) ----------------------------------------------
+// TMEM address: lane in bits 31..16, column in bits 15..0.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (K-major, no swizzle: core matrices of 8
+// rows x 16 bytes, rows 16 bytes apart; 8-row groups `sbo` bytes apart, the
+// two 16-byte halves of a 256-bit row `lbo` bytes apart; version 1).
+__device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+}
+
+// 128 TMEM lanes x 256 bits from shared memory (asynchronous; completion via
+// tcgen05_commit).
+__device__ __forceinline__ void tcgen05_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Arrive once on the mbarrier when every tcgen05 operation this thread issued
+// before has completed.
+__device__ __forceinline__ void tcgen05_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 columns (the warp's lane quarter): r[i] = column col + i of
+// this thread's lane.  Completed by tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+// The same straight into 8 uint4 (w[i] = columns 4i..4i+3).
+__device__ __forceinline__ void tmem_ld_32x32b_x32_u4(uint32_t taddr, uint4 (&w)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(w[0].x), "=r"(w[0].y), "=r"(w[0].z), "=r"(w[0].w), "=r"(w[1].x), "=r"(w[1].y), "=r"(w[1].z),
+        "=r"(w[1].w), "=r"(w[2].x), "=r"(w[2].y), "=r"(w[2].z), "=r"(w[2].w), "=r"(w[3].x), "=r"(w[3].y),
+        "=r"(w[3].z), "=r"(w[3].w), "=r"(w[4].x), "=r"(w[4].y), "=r"(w[4].z), "=r"(w[4].w), "=r"(w[5].x),
+        "=r"(w[5].y), "=r"(w[5].z), "=r"(w[5].w), "=r"(w[6].x), "=r"(w[6].y), "=r"(w[6].z), "=r"(w[6].w),
+        "=r"(w[7].x), "=r"(w[7].y), "=r"(w[7].z), "=r"(w[7].w)
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Software grid barrier over `nct` co-resident CTAs, split into arrive and
 // wait so a CTA can do independent work in between.  One thread per CTA

@@ -2,8 +2,8 @@
 //
 // One launch runs a list of phases (aicas_phase_program.h) with one CTA per SM:
 //   warp 0      producer: streams every tile this CTA will consume, phase after
-//               phase, from HBM into a 6-stage shared-memory ring with bulk
-//               async copies (cp.async.bulk + mbarrier complete_tx, L2
+//               phase, from HBM into a small shared-memory ring (kStages) with
+//               bulk async copies (cp.async.bulk + mbarrier complete_tx, L2
 //               evict_first).  It never waits for activations, so HBM keeps
 //               streaming the next phases' weights while the consumers wait.
 //   warps 1..8  consumers: per phase, wait for the phase's input vector (LL
@@ -15,6 +15,10 @@
 //   warp 9      L2 prefetch (AICAS_L2_WARP): walks the same tile schedule up
 //               to kL2Ahead tiles ahead of the producer and prefetches them
 //               into L2, so HBM keeps working while the ring is full.
+//   warp 10     TMEM mover: copies every landed GEMV tile from its ring stage
+//               into an 8-slot ring in tensor memory (tcgen05.cp) and frees
+//               the stage; consumers read their tile row from TMEM
+//               (tcgen05.ld), so up to kStages + 8 tiles wait ahead of them.
 //
 // GEMV tile: 8 weight rows x 2048 columns (32 KB), fetched with ONE bulk copy
 // (rows are contiguous when k <= 2048; the engine stores down_proj K-blocked,
@@ -65,13 +69,28 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 #ifndef AICAS_L2_WARP
 #define AICAS_L2_WARP 1
 #endif
-constexpr int kThreads = kConsumerThreads + 32 + (AICAS_L2_WARP ? 32 : 0);  // producer + 8 consumer warps (+ prefetch warp)
+// Warp roles: 0 producer, 1..8 consumers, then the L2 prefetch warp (if
+// enabled), then the TMEM mover (last warp).
+constexpr int kL2Warp = 1 + kConsumerWarps;
+constexpr int kMoverWarp = 1 + kConsumerWarps + (AICAS_L2_WARP ? 1 : 0);
+constexpr int kThreads = 32 * (kMoverWarp + 1);
+// Tensor memory: an 8-slot ring of GEMV tiles (64 columns x 128 lanes each).
+constexpr int kTmemSlots = 8;
+constexpr int kTmemCols = 512;
+constexpr int kTmemTileCols = 64;
 constexpr int kRowsPerWarp = 1;
 constexpr int kRows = kConsumerWarps * kRowsPerWarp;  // weight rows per GEMV tile
 constexpr int kChunk = 2048;           // columns per GEMV tile
 constexpr int kRowBytes = kChunk * 2;
 constexpr int kStageBytes = kRows * kRowBytes;  // 32 KB: one bulk copy per tile
-constexpr int kStages = 6;
+// Ring stages in shared memory.  With the TMEM slot ring behind them a stage
+// only holds a tile until the mover has copied it out; measured on B200
+// (28 layers, 1024-slot prefix): 6 stages 1219 us/token, 5: 1238, 4: 1140,
+// 3: 1114-1120, 2: 1095-1098 (no TMEM ring, 6 stages: 1156-1174).
+#ifndef AICAS_STAGES
+#define AICAS_STAGES 2
+#endif
+constexpr int kStages = AICAS_STAGES;
 constexpr int kAttnChunk = 64;  // cache positions per attention tile
 constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
@@ -99,9 +118,14 @@ struct __align__(128) Smem {
   float ssq[kConsumerWarps];    // per-warp sums of squares for the RMSNorm prologue
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kStages];    // stage landed (bulk copy complete_tx)
+  uint64_t empty[kStages];   // stage free again (arrived by the mover)
+  uint64_t cempty[kStages];  // consumers done with a stage they read directly (attention, partial chunks)
+  uint64_t tfull[kTmemSlots];   // TMEM slot filled (tcgen05.commit of the mover)
+  uint64_t tempty[kTmemSlots];  // TMEM slot read by all 8 consumer warps
+  uint64_t cdone;               // all consumer warps finished the program (TMEM may be freed)
   uint32_t ring_it;  // tiles the producer has issued (read by the L2 prefetch warp)
+  uint32_t tmem_base;  // TMEM address of the slot ring (written by tcgen05.alloc)
 };
 
 struct ProgramArgs {
@@ -199,17 +223,25 @@ struct Ring {
 
 // One tile of the CTA's schedule: `pieces` copies of `bytes` each, from src
 // + i * src_stride to ring stage + i * dst_stride.
+// GEMV-type phases whose reduction length is a multiple of 2048 stream their
+// tiles through the TMEM slot ring (every tile row is a full 4096-byte chunk
+// row); other tiles are read by the consumers straight from the ring stage.
+__device__ __forceinline__ bool tmem_phase(int kind, int k) {
+  return kind != AICAS_PH_ATTN && k % kChunk == 0;
+}
+
 struct TileDesc {
   const uint8_t* src;
   int64_t src_stride;
   uint32_t dst_stride;
   uint32_t bytes;
   int pieces;
+  bool tmem;  // GEMV tile that goes through the TMEM slot ring (else consumers read the stage)
 };
 
 // Walks this CTA's tiles of a program in the exact order the consumers
-// take them.  The producer runs one cursor for the shared-memory ring and a
-// second one ahead of it for L2 prefetches.
+// take them.  The producer, the TMEM mover and the L2 prefetch warp each run
+// one cursor.
 struct TileCursor {
   const AicasPhase* P;
   int n_phases;
@@ -219,7 +251,7 @@ struct TileCursor {
   // cached per-phase schedule
   int kind, flags, C, T, rows_total;
   Range rg;
-  bool cmajor;
+  bool cmajor, tm;
   int valid, cph;
 
   __device__ __forceinline__ void enter(int phase, const StepIn& in) {
@@ -240,6 +272,7 @@ struct TileCursor {
       T = tiles_per_group(d);
       rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
       cmajor = chunk_major(C, kind, rg.count);
+      tm = tmem_phase(kind, d.k);
       rows_total = kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
       n = rg.count * T;
     }
@@ -263,6 +296,7 @@ struct TileCursor {
       td.dst_stride = kStageBytes / 2;
       td.bytes = rows * kHD * 2;
       td.pieces = 2;
+      td.tmem = false;
     } else {
       int g, t;
       if (cmajor) {
@@ -278,6 +312,7 @@ struct TileCursor {
       const int col0 = c * kChunk;
       const uint32_t bytes = min(kChunk, d.k - col0) * 2;
       const uint8_t* W = reinterpret_cast<const uint8_t*>(d.w);
+      td.tmem = tm;
       if (C == 1) {  // whole rows: one contiguous block, rows packed at stride k
         td.src = W + (size_t)row0 * d.k * 2;
         td.bytes = nrows * bytes;
@@ -342,6 +377,70 @@ __device__ __forceinline__ void run_l2_prefetcher(const ProgramArgs& a, Smem& sm
         for (uint32_t off = lane * 128u; off < td.bytes; off += 32u * 128u) prefetch_l2_line(td.src + i * td.src_stride + off);
     }
   }
+}
+
+// TMEM mover (last warp; lane 0 walks the tile schedule in order): every
+// GEMV tile that has landed in a ring stage is copied into the next TMEM slot
+// with 8 tcgen05.cp (128 lanes x 256 bits each) -- slot lanes 32q..32q+31
+// then hold tile row q in columns 0..31 and row 4 + q in columns 32..63, each
+// lane 64 fp16 values of the row -- and one tcgen05.commit each marks the
+// slot full and the stage free once the copies are done.  For tiles the
+// consumers read in place it passes their release on to the producer (the
+// producer waits on one arrival per stage).  So the ring stages turn over as
+// fast as tiles can be parked in TMEM, and up to kStages + 8 tiles are in flight
+// ahead of the consumers.  The whole warp allocates the TMEM at launch and
+// frees it after every consumer warp has signalled that it is done.
+__device__ __forceinline__ void run_mover(const ProgramArgs& a, Smem& sm, const StepIn& in, uint32_t tmem) {
+  const int lane = threadIdx.x & 31;
+  AicasScratch* s = a.scratch;
+  if (lane == 0) {
+    const AicasPhase* P = a.phases ? a.phases : a.inl;
+    TileCursor cur{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+    TileDesc td;
+    uint32_t it = 0, g = 0;
+    // cempty[st] completes once per in-place use of stage st (not per use):
+    // its expected parity is tracked per stage
+    uint32_t cpar = 0;
+    while (cur.next(in, td)) {
+      const int st = it % kStages;
+      const uint32_t par = (it / kStages) & 1u;
+      if (td.tmem) {
+        const uint32_t t = g % kTmemSlots;
+        if (!mbar_wait_bounded(&sm.full[st], par, s, kErrFullTimeout)) break;
+        if (g >= kTmemSlots && !mbar_wait_bounded(&sm.tempty[t], ((g / kTmemSlots) - 1) & 1u, s, kErrTmemTimeout))
+          break;
+        tc_fence_after();
+        const uint32_t stage = smem_addr(sm.ring[st]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tcgen05_cp_128x256b(tmem + t * kTmemTileCols + h * 32 + c * 8,
+                                smem_desc_kmajor(stage + h * 16384 + c * 256, 128, 1024));
+        tcgen05_commit(&sm.tfull[t]);
+        tcgen05_commit(&sm.empty[st]);
+        ++g;
+      } else {
+        if (!mbar_wait_bounded(&sm.cempty[st], (cpar >> st) & 1u, s, kErrEmptyTimeout)) break;
+        cpar ^= 1u << st;
+        mbar_arrive(&sm.empty[st]);
+      }
+      ++it;
+    }
+    // TMEM is freed only after the consumers are done with it.  This wait
+    // ignores the abort word (consumers finish promptly after an abort: every
+    // wait of theirs is bounded) and is bounded by twice the wait limit.
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&sm.cdone, 0)) {
+      if (globaltimer_ns() - t0 > 2 * kWaitLimitNs) {
+        raise_error(s, kErrTmemTimeout);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_after();
+  tmem_dealloc(tmem, kTmemCols);
 }
 
 // Run by all 32 lanes of warp 0: lane 0 owns the ring (waits, expect_tx,
@@ -424,6 +523,14 @@ struct Consumer {
   uint32_t bar_k = 0;
   uint32_t epoch_base;  // LL epoch of phase p = epoch_base + p + 1
   int ph = 0;           // running phase index
+  uint32_t tmem = 0;    // TMEM slot ring base address
+  uint32_t tg = 0;      // TMEM-path tiles consumed so far
+  int rwt = 0;          // tile row of this warp: the row its TMEM lane quarter holds
+
+  // GEMV column (within a 2048-column chunk) of this lane's value v = 0..7:
+  // 512 (lane / 8) + 64 v + 8 (lane % 8) + [0, 8), the layout of a tile row in
+  // a TMEM lane (see run_mover); the shared-memory path reads the same columns.
+  __device__ __forceinline__ int colv(int v) const { return 512 * (lane >> 3) + 64 * v + 8 * (lane & 7); }
   // residual rows of this warp's first groups of the coming phase
   float rv_pre[kResidPrefetch][kRowsPerWarp];
 
@@ -452,7 +559,7 @@ struct Consumer {
   }
   __device__ __forceinline__ void release(int st) {
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[st]);
+    if (lane == 0) mbar_arrive(&sm.cempty[st]);
     ++r.it;
   }
 
@@ -523,7 +630,7 @@ struct Consumer {
       for (int i = 0; i < kResidPrefetch; ++i)
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = (rg.start + i) * kRows + kRowsPerWarp * w + rr;
+          const int row = (rg.start + i) * kRows + rwt + rr;
           rv_pre[i][rr] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
         }
     }
@@ -599,7 +706,7 @@ struct Consumer {
     if constexpr (C == 1) {
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
-        const int col = j * 256 + lane * 8;
+        const int col = colv(j);
         x0[j] = col < k ? *reinterpret_cast<const uint4*>(&sm.xs[col]) : make_uint4(0, 0, 0, 0);
       }
       if (flags & AICAS_F_NORM) {
@@ -612,7 +719,7 @@ struct Consumer {
       const float inv = rsqrtf(ss / (float)k + d.eps);
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
-        const int col = j * 256 + lane * 8;
+        const int col = colv(j);
         if (col < k) {
           const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
           __half2* hp = reinterpret_cast<__half2*>(&x0[j]);
@@ -632,7 +739,7 @@ struct Consumer {
       for (int c = 0; c < C; ++c)
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
-          const int col = c * kChunk + j * 256 + lane * 8;
+          const int col = c * kChunk + colv(j);
           if (col < k) *reinterpret_cast<uint4*>(xo + col) = C == 1 ? x0[j] : *reinterpret_cast<const uint4*>(&sm.nw[col]);
         }
     }
@@ -644,7 +751,7 @@ struct Consumer {
   __device__ __forceinline__ void x_chunk(int c, int k, const uint4 (&x0)[kVec], uint4 (&xc)[kVec]) {
 #pragma unroll
     for (int j = 0; j < kVec; ++j) {
-      const int col = c * kChunk + j * 256 + lane * 8;
+      const int col = c * kChunk + colv(j);
       // C > 1: inline-asm shared loads, so they stay after the tile wait they follow
       xc[j] = C == 1 ? x0[j] : (col < k ? lds_u4(smem_addr(&sm.nw[col])) : make_uint4(0, 0, 0, 0));
     }
@@ -690,13 +797,14 @@ struct Consumer {
     return lane_bits;
   }
 
-  // This lane's 64 columns of one tile row (shared address `row_s`) into
-  // registers; `jmask` skips columns beyond k.  Loading a tile completely
+  // This lane's 64 columns of one tile row into registers (`row_s`: shared
+  // address of the row plus the lane's offset 1024 (lane / 8) + 16 (lane % 8);
+  // value v sits 128 v bytes further); `jmask` skips columns beyond k.  Loading a tile completely
   // before the math lets the stage go back to the producer immediately, so
   // the FMAs overlap the next copies instead of lengthening the ring cycle.
   __device__ __forceinline__ static void row_load(uint32_t row_s, unsigned jmask, uint4 (&wv)[kVec]) {
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) wv[j] = ((jmask >> j) & 1u) ? lds_u4(row_s + j * 512) : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < kVec; ++j) wv[j] = ((jmask >> j) & 1u) ? lds_u4(row_s + j * 128) : make_uint4(0, 0, 0, 0);
   }
 
   // acc[0..3] += row . x (both fp16): exact fp16 products, fp32 accumulation
@@ -774,7 +882,8 @@ struct Consumer {
     const int last_len = k - (C - 1) * kChunk;
     unsigned jlast = 0;
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) jlast |= (j * 256 + lane * 8 < last_len ? 1u : 0u) << j;
+    for (int j = 0; j < kVec; ++j) jlast |= (colv(j) < last_len ? 1u : 0u) << j;
+    const bool use_tm = tmem_phase(kind, k);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     __half* logits = nullptr;
@@ -783,11 +892,17 @@ struct Consumer {
       logits = reinterpret_cast<__half*>(a.state->logits) + (size_t)(in.step % ring) * n;
     }
     // everything the tile loops touch lives in registers
-    const uint32_t ring_s = smem_addr(&sm.ring[0][0]);
+    const uint32_t ring_s = smem_addr(&sm.ring[0][0]) + 1024 * (lane >> 3) + 16 * (lane & 7);
     const uint32_t full_s = smem_addr(&sm.full[0]);
-    const uint32_t empty_s = smem_addr(&sm.empty[0]);
+    const uint32_t cempty_s = smem_addr(&sm.cempty[0]);
+    const uint32_t tfull_s = smem_addr(&sm.tfull[0]);
+    const uint32_t tempty_s = smem_addr(&sm.tempty[0]);
+    // this warp's row in the TMEM slot: lanes of its quarter, column half
+    const uint32_t tm_row = tmem + ((uint32_t)(32 * ((w + 1) & 3)) << 16) + 32 * (w >> 2);
+    uint32_t tgl = tg;
     AicasScratch* const scr = s;
-    const int ln = lane, wp = w;
+    const int ln = lane;
+    static_assert(kRowsPerWarp == 1, "one tile row per warp (its TMEM lane quarter and column half)");
     const bool timing = kTrace && tid == 0;
     uint64_t waited = 0;
     uint32_t it = r.it;
@@ -805,8 +920,30 @@ struct Consumer {
 #define AICAS_GIVE(st)                        \
   do {                                        \
     __syncwarp();                             \
-    if (ln == 0) mbar_arrive_s(empty_s + st * 8); \
+    if (ln == 0) mbar_arrive_s(cempty_s + st * 8); \
     ++it;                                     \
+  } while (0)
+// One tile row from the next TMEM slot (the whole warp) and the slot
+// released; after a failed wait the row reads as zeros.
+#define AICAS_TLOAD(wv_, valid_)                                                                  \
+  do {                                                                                            \
+    const uint32_t t_ = tgl % kTmemSlots;                                                         \
+    uint64_t t0_ = timing ? globaltimer_ns() : 0;                                                 \
+    bool ok_ = mbar_wait_bounded_s(tfull_s + t_ * 8, (tgl / kTmemSlots) & 1u, scr, kErrTmemTimeout); \
+    if (timing) waited += globaltimer_ns() - t0_;                                                 \
+    ok_ = __all_sync(0xffffffffu, ok_);                                                           \
+    tc_fence_after();                                                                             \
+    /* always in bounds: TMEM stays allocated until every consumer warp is done */              \
+    tmem_ld_32x32b_x32_u4(tm_row + t_ * kTmemTileCols, wv_);                                      \
+    tmem_wait_ld();                                                                               \
+    tc_fence_before();                                                                            \
+    __syncwarp();                                                                                 \
+    if (ln == 0) mbar_arrive_s(tempty_s + t_ * 8);                                                \
+    ++tgl;                                                                                        \
+    ++it;                                                                                         \
+    if (!(ok_ && (valid_))) {                                                                     \
+      _Pragma("unroll") for (int v_ = 0; v_ < kVec; ++v_) wv_[v_] = make_uint4(0, 0, 0, 0);      \
+    }                                                                                             \
   } while (0)
     uint4 xh[kVec];  // fp16 input slice of the running chunk (C > 1; C == 1 uses x0)
     if (chunk_major(C, kind, rg.count)) {
@@ -824,16 +961,16 @@ struct Consumer {
 #pragma unroll
         for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
           if (gi < rg.count) {
-            uint32_t st;
-            AICAS_TAKE(st);
             uint4 wv[kRowsPerWarp][kVec];
-#pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + kRowsPerWarp * wp + rr;
-              row_load(ring_s + st * kStageBytes + (kRowsPerWarp * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
-                       wv[rr]);
+            const int row = (rg.start + gi) * kRows + rwt;
+            if (use_tm) {
+              AICAS_TLOAD(wv[0], row < n);
+            } else {
+              uint32_t st;
+              AICAS_TAKE(st);
+              row_load(ring_s + st * kStageBytes + rwt * row_stride, row < n ? jmask : 0u, wv[0]);
+              AICAS_GIVE(st);
             }
-            AICAS_GIVE(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) if constexpr (C == 1) row_fma(wv[rr], x0, acc[gi][rr]); else row_fma(wv[rr], xh, acc[gi][rr]);
           }
@@ -843,7 +980,7 @@ struct Consumer {
       for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
         if (gi < rg.count) {
           float y[kRowsPerWarp];
-          const int row0 = (rg.start + gi) * kRows + kRowsPerWarp * wp;
+          const int row0 = (rg.start + gi) * kRows + rwt;
 #pragma unroll
           for (int rr = 0; rr < kRowsPerWarp; ++rr) {
             const int row = row0 + rr;
@@ -872,22 +1009,22 @@ struct Consumer {
           for (int c = 0; c < C; ++c) {
             if (C > 1) x_chunk<C>(c, k, x0, xh);
             const unsigned jmask = c < C - 1 ? 0xffu : jlast;
-            uint32_t st;
-            AICAS_TAKE(st);
             uint4 wv[kRowsPerWarp][kVec];
-#pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-              const int row = (rg.start + gi) * kRows + kRowsPerWarp * wp + rr;
-              row_load(ring_s + st * kStageBytes + (kRowsPerWarp * wp + rr) * row_stride + ln * 16, row < n ? jmask : 0u,
-                       wv[rr]);
+            const int row = (rg.start + gi) * kRows + rwt;
+            if (use_tm) {
+              AICAS_TLOAD(wv[0], row < n);
+            } else {
+              uint32_t st;
+              AICAS_TAKE(st);
+              row_load(ring_s + st * kStageBytes + rwt * row_stride, row < n ? jmask : 0u, wv[0]);
+              AICAS_GIVE(st);
             }
-            AICAS_GIVE(st);
 #pragma unroll
             for (int rr = 0; rr < kRowsPerWarp; ++rr) if constexpr (C == 1) row_fma(wv[rr], x0, acc[part][rr]); else row_fma(wv[rr], xh, acc[part][rr]);
           }
         }
         float y[kRowsPerWarp];
-        const int row0 = (rg.start + gi) * kRows + kRowsPerWarp * wp;
+        const int row0 = (rg.start + gi) * kRows + rwt;
 #pragma unroll
         for (int rr = 0; rr < kRowsPerWarp; ++rr) {
           const int row = row0 + rr;
@@ -902,9 +1039,11 @@ struct Consumer {
     }
 #undef AICAS_TAKE
 #undef AICAS_GIVE
+#undef AICAS_TLOAD
     stamp_field(7);
     wait_ns += waited;
     r.it = it;
+    tg = tgl;
     if (kind == AICAS_PH_LMHEAD) finish_argmax(d, best_v, best_i);
   }
 
@@ -1337,6 +1476,10 @@ struct Consumer {
       else run_matvec(d);
       stamp(ph, 2);
     }
+    // this warp is done with TMEM: the mover may free it
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.cdone);
     // the last CTA to finish moves the LL epoch base past this launch
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
@@ -1359,12 +1502,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], kConsumerWarps);
+      mbar_init(&sm.empty[i], 1);
+      mbar_init(&sm.cempty[i], kConsumerWarps);
     }
+    for (int i = 0; i < kTmemSlots; ++i) {
+      mbar_init(&sm.tfull[i], 1);
+      mbar_init(&sm.tempty[i], kConsumerWarps);
+    }
+    mbar_init(&sm.cdone, kConsumerWarps);
     sm.ring_it = 0;
     mbar_fence_init();
   }
+  if (threadIdx.x / 32 == kMoverWarp) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&sm.tmem_base);
   StepIn in{};
   if (a.state) {
     const volatile AicasStepState* st = a.state;
@@ -1377,7 +1530,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   }
   const AicasPhase* P = a.phases ? a.phases : a.inl;
   const int warp = threadIdx.x / 32;
-  if (AICAS_L2_WARP && warp == 1 + kConsumerWarps) {
+  if (warp == kMoverWarp) {
+    run_mover(a, sm, in, tmem);
+    return;
+  }
+  if (AICAS_L2_WARP && warp == kL2Warp) {
     run_l2_prefetcher(a, sm, in);
     return;
   }
@@ -1389,6 +1546,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   c.tid = threadIdx.x - 32;
   c.w = warp - 1;
   c.lane = threadIdx.x & 31;
+  c.tmem = tmem;
+  c.rwt = ((c.w + 1) & 3) + 4 * (c.w >> 2);
   c.nct = gridDim.x;
   c.cta = blockIdx.x;
   const uint64_t now = ld_relaxed_u64(&a.scratch->bar_count);
