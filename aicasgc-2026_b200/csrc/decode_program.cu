@@ -95,7 +95,7 @@ constexpr int kAttnChunk = 64;  // cache positions per attention tile
 constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
-constexpr int kResidPrefetch = 4;                 // residual rows kept in registers per warp
+constexpr int kEpiBatch = 16;  // row groups whose epilogues are done together (one lane each)
 
 static_assert(kAttnChunk * kHD * 2 * 2 == kStageBytes, "attention tile must fill one stage");
 static_assert(AICAS_MAX_K % kChunk == 0, "max K must be whole chunks");
@@ -115,6 +115,10 @@ struct __align__(128) Smem {
   __half nw[AICAS_MAX_K];  // norm weights of the running phase (prefetched before its barrier)
   AttnSmem at;
   __half xs[kChunk];            // C == 1 phases: the input vector, shared by the 8 warps
+  // batched epilogue: lane partial sums, [warp][group slot * 2 + part][lane]
+  // (rows padded to 33 floats: a lane summing a row reads a different bank
+  // from every other lane)
+  float epi[kConsumerWarps][2 * kEpiBatch][33];
   float ssq[kConsumerWarps];    // per-warp sums of squares for the RMSNorm prologue
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
@@ -532,7 +536,7 @@ struct Consumer {
   // a TMEM lane (see run_mover); the shared-memory path reads the same columns.
   __device__ __forceinline__ int colv(int v) const { return 512 * (lane >> 3) + 64 * v + 8 * (lane & 7); }
   // residual rows of this warp's first groups of the coming phase
-  float rv_pre[kResidPrefetch][kRowsPerWarp];
+  float rv_lane = 0.f;  // residual of the row this lane finishes in the phase's first epilogue batch
 
   // Waits never end the consumer loop early: after a failed (timed-out or
   // aborted) wait the CTA keeps walking the same program without waiting, so
@@ -624,15 +628,10 @@ struct Consumer {
       for (int v = tid; v < d.k / 8; v += kConsumerThreads)
         *reinterpret_cast<uint4*>(&sm.nw[v * 8]) = __ldg(reinterpret_cast<const uint4*>(nw) + v);
     }
-    if ((d.flags & AICAS_F_RESID) && lane == 0) {
+    if (d.flags & AICAS_F_RESID) {  // lane l: the row of group l of this CTA (first epilogue batch)
       const Range rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
-#pragma unroll
-      for (int i = 0; i < kResidPrefetch; ++i)
-#pragma unroll
-        for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = (rg.start + i) * kRows + rwt + rr;
-          rv_pre[i][rr] = (i < rg.count && row < d.n) ? resid_value(d, row) : 0.f;
-        }
+      const int row = (rg.start + lane) * kRows + rwt;
+      rv_lane = (lane < rg.count && lane < kEpiBatch && row < d.n) ? resid_value(d, row) : 0.f;
     }
   }
 
@@ -814,22 +813,43 @@ struct Consumer {
     for (int j = 0; j < kVec; ++j) acc[j & 3] = dot8_f16(wv[j], xh[j], acc[j & 3]);
   }
 
-  // Residual of one output row (lane 0 only): prefetched for the first
-  // groups, loaded otherwise.
-  __device__ __forceinline__ float resid_row(const AicasPhase& d, bool resid, int gi, int rr, int row, int n) {
-    if (!resid || lane != 0 || row >= n) return 0.f;
-    if (gi < kResidPrefetch) {
-      float v = 0.f;
+  // The 4 accumulation chains of a lane folded into its partial sum.
+  __device__ __forceinline__ static float fold4(const float (&a)[4]) { return (a[0] + a[1]) + (a[2] + a[3]); }
+
+  // Batched epilogue: the warp has written the lane partial sums of `cnt`
+  // row groups (group base `gbase` + slot, `parts` sums each) to sm.epi; lane
+  // l < cnt finishes group gbase + l: sums its 32 partials (in a fixed order),
+  // applies bias/residual/SiLU and rounding (row_value) and stores the row.
+  // One pass replaces a 5-shuffle reduction plus a lane-0 epilogue per group.
+  __device__ __forceinline__ void epi_flush(const AicasPhase& d, int kind, int flags, int n, int gbase, int cnt,
+                                            int parts, bool first_batch, const __half* bias, __half* logits,
+                                            __half* out, float& best_v, int& best_i) {
+    __syncwarp();
+    if (lane < cnt) {
+      float s2[2] = {0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kResidPrefetch; ++i)
-        if (i == gi) v = rv_pre[i][rr];
-      return v;
+      for (int p = 0; p < 2; ++p) {
+        if (p < parts) {
+          const float* e = &sm.epi[w][lane * parts + p][0];
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) c[j & 3] += e[j];
+          s2[p] = fold4(c);
+        }
+      }
+      const int row = (gbase + lane) * kRows + rwt;
+      if (row < n) {
+        const float rv = !(flags & AICAS_F_RESID) ? 0.f : (first_batch ? rv_lane : resid_value(d, row));
+        float y[kRowsPerWarp];
+        y[0] = row_value(kind, flags, row, s2[0], s2[1], rv, bias, logits, best_v, best_i);
+        store_rows(flags, n, row, y, out);
+      }
     }
-    return resid_value(d, row);
+    __syncwarp();
   }
 
-  // Output value of one row (lane 0) with the rounding points of HF's fp16
-  // path; the LM head also stores the logit and updates the running argmax.
+  // Output value of one row with the rounding points of HF's fp16 path; the
+  // LM head also stores the logit and updates the lane's running argmax.
   __device__ __forceinline__ static float row_value(int kind, int flags, int row, float sum0, float sum1, float rv,
                                                     const __half* bias, __half* logits, float& best_v, int& best_i) {
     if (kind == AICAS_PH_GATEUP) {
@@ -842,7 +862,7 @@ struct Consumer {
     if (flags & AICAS_F_RESID) y = r16(rv + y);
     if (kind == AICAS_PH_LMHEAD) {
       if (logits) logits[row] = __float2half_rn(y);
-      // this lane's rows ascend (row 2w before 2w+1, groups ascend): strict > keeps the first max
+      // a lane's rows ascend (its groups ascend): strict > keeps the first max
       if (y > best_v) {
         best_v = y;
         best_i = row;
@@ -851,7 +871,7 @@ struct Consumer {
     return y;
   }
 
-  // Lane 0 stores the warp's output rows: LL words or plain fp16.
+  // Stores output rows row0.. (LL words or plain fp16).
   __device__ __forceinline__ void store_rows(int flags, int n, int row0, const float (&y)[kRowsPerWarp], __half* out) {
     if (!out) return;
 #pragma unroll
@@ -873,7 +893,6 @@ struct Consumer {
     // descriptor fields in registers (the waits below clobber memory)
     const int n = d.n, k = d.k, flags = d.flags, kind = d.kind;
     const bool gateup = kind == AICAS_PH_GATEUP;
-    const bool resid = flags & AICAS_F_RESID;
     __half* const out = reinterpret_cast<__half*>(d.out);
     const __half* const bias = reinterpret_cast<const __half*>(d.bias);
     const Range rg = split_range((n + kRows - 1) / kRows, nct, cta, d.rot);
@@ -977,23 +996,12 @@ struct Consumer {
         }
       }
 #pragma unroll
-      for (int gi = 0; gi < kMaxCmajorGroups; ++gi) {
-        if (gi < rg.count) {
-          float y[kRowsPerWarp];
-          const int row0 = (rg.start + gi) * kRows + rwt;
-#pragma unroll
-          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-            const int row = row0 + rr;
-            const float rv = resid_row(d, resid, gi, rr, row, n);
-            const float sum = warp_sum((acc[gi][rr][0] + acc[gi][rr][1]) + (acc[gi][rr][2] + acc[gi][rr][3]));
-            y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum, 0.f, rv, bias, logits, best_v, best_i)
-                                         : 0.f;
-          }
-          if (ln == 0 && row0 < n) store_rows(flags, n, row0, y, out);
-        }
-      }
+      for (int gi = 0; gi < kMaxCmajorGroups; ++gi)
+        if (gi < rg.count) sm.epi[w][gi][ln] = fold4(acc[gi][0]);
+      epi_flush(d, kind, flags, n, rg.start, rg.count, 1, true, bias, logits, out, best_v, best_i);
     } else {
-
+      const int parts = gateup ? 2 : 1;
+      int gb = 0;  // first group of the running epilogue batch
       for (int gi = 0; gi < rg.count; ++gi) {
         float acc[2][kRowsPerWarp][4];
 #pragma unroll
@@ -1023,18 +1031,13 @@ struct Consumer {
             for (int rr = 0; rr < kRowsPerWarp; ++rr) if constexpr (C == 1) row_fma(wv[rr], x0, acc[part][rr]); else row_fma(wv[rr], xh, acc[part][rr]);
           }
         }
-        float y[kRowsPerWarp];
-        const int row0 = (rg.start + gi) * kRows + rwt;
-#pragma unroll
-        for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-          const int row = row0 + rr;
-          const float rv = resid_row(d, resid, gi, rr, row, n);
-          const float sum0 = warp_sum((acc[0][rr][0] + acc[0][rr][1]) + (acc[0][rr][2] + acc[0][rr][3]));
-          const float sum1 = gateup ? warp_sum((acc[1][rr][0] + acc[1][rr][1]) + (acc[1][rr][2] + acc[1][rr][3])) : 0.f;
-          y[rr] = (ln == 0 && row < n) ? row_value(kind, flags, row, sum0, sum1, rv, bias, logits, best_v, best_i)
-                                       : 0.f;
+        const int slot = gi - gb;
+        sm.epi[w][slot * parts][ln] = fold4(acc[0][0]);
+        if (gateup) sm.epi[w][slot * parts + 1][ln] = fold4(acc[1][0]);
+        if (slot == kEpiBatch - 1 || gi == rg.count - 1) {
+          epi_flush(d, kind, flags, n, rg.start + gb, slot + 1, parts, gb == 0, bias, logits, out, best_v, best_i);
+          gb = gi + 1;
         }
-        if (ln == 0 && row0 < n) store_rows(flags, n, row0, y, out);
       }
     }
 #undef AICAS_TAKE
@@ -1044,7 +1047,19 @@ struct Consumer {
     wait_ns += waited;
     r.it = it;
     tg = tgl;
-    if (kind == AICAS_PH_LMHEAD) finish_argmax(d, best_v, best_i);
+    if (kind == AICAS_PH_LMHEAD) {
+      // lanes -> warp: larger value, or the same value at a smaller row
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best_v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (v2 > best_v || (v2 == best_v && i2 < best_i)) {
+          best_v = v2;
+          best_i = i2;
+        }
+      }
+      finish_argmax(d, best_v, best_i);
+    }
   }
 
   __device__ __forceinline__ void run_matvec(const AicasPhase& d) {
