@@ -95,7 +95,11 @@ constexpr int kAttnChunk = 64;  // cache positions per attention tile
 constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
-constexpr int kEpiBatch = 16;  // row groups whose epilogues are done together (one lane each)
+#ifndef AICAS_EPI_BATCH
+#define AICAS_EPI_BATCH 16
+#endif
+constexpr int kEpiBatch = AICAS_EPI_BATCH;  // row groups whose epilogues are done together (one lane each, <= 32)
+static_assert(kEpiBatch <= 32, "one lane per row group");
 
 static_assert(kAttnChunk * kHD * 2 * 2 == kStageBytes, "attention tile must fill one stage");
 static_assert(AICAS_MAX_K % kChunk == 0, "max K must be whole chunks");
