@@ -69,6 +69,7 @@ class AicasStepState(ctypes.Structure):
         ("out_tokens", ctypes.c_void_p), ("max_steps", ctypes.c_int64), ("logits", ctypes.c_void_p),
         ("logits_ring", ctypes.c_int64), ("inv_freq", ctypes.c_float * 64),
         ("mrope_section", ctypes.c_int32 * 3), ("pad0", ctypes.c_int32),
+        ("eos_token", ctypes.c_int64), ("done_step", ctypes.c_int64),
     ]
 
 

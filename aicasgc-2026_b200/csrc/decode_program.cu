@@ -1126,6 +1126,9 @@ struct Consumer {
             stt->rope[2] = in.rope[2] + 1;
           }
           stt->step = nx;
+          // device-side end of sequence: a generated token (the script's
+          // last step onward) equal to eos_token ends the request
+          if (stt->eos_token >= 0 && bi2 == stt->eos_token && nx >= stt->script_len) stt->done_step = nx;
           __threadfence();
         }
       }
@@ -1518,6 +1521,10 @@ template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  // a request that produced its end-of-sequence token: nothing to do (every
+  // thread reads the same word, so the whole grid returns before any barrier,
+  // TMEM allocation or copy)
+  if (a.state && *reinterpret_cast<const volatile int64_t*>(&a.state->done_step) != 0) return;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);

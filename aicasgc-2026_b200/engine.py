@@ -183,8 +183,9 @@ class Qwen3VLDecodeEngine:
         self.n_phases = len(phases)
 
     # ------------------------------------------------------------------ state
-    def _write_state(self, token, cache_pos, rope, step, script_len):
+    def _write_state(self, token, cache_pos, rope, step, script_len, eos_token=-1):
         st = AicasStepState()
+        st.eos_token, st.done_step = int(eos_token), 0
         st.token, st.cache_pos = int(token), int(cache_pos)
         for i in range(3):
             st.rope[i] = int(rope[i])
@@ -201,11 +202,13 @@ class Qwen3VLDecodeEngine:
         host = torch.frombuffer(bytearray(bytes(st)), dtype=torch.uint8)
         self.state_dev.copy_(host, non_blocking=False)
 
-    def load_script(self, tokens, pos3=None, start_slot: int = 0):
+    def load_script(self, tokens, pos3=None, start_slot: int = 0, eos_token_id: int | None = None):
         """Forced inputs for the next len(tokens) steps: token i goes to cache
         slot start_slot + i with rope positions pos3[:, i] (default: the slot
         on all three axes).  After the script the engine decodes greedily
-        from slot start_slot + len(tokens), rope positions advancing by one."""
+        from slot start_slot + len(tokens), rope positions advancing by one.
+        With `eos_token_id`, the device ends the request at the first
+        generated token equal to it: every later launch returns at once."""
         tokens = torch.as_tensor(tokens, dtype=torch.int64).reshape(-1).cpu()
         P = tokens.numel()
         if P < 1 or start_slot + P > self.max_cache_len:
@@ -217,7 +220,8 @@ class Qwen3VLDecodeEngine:
         script = torch.stack([tokens, slots, pos3[0], pos3[1], pos3[2]], 1).contiguous()
         self.script = script.to(self.device)
         self.out_tokens.fill_(-1)
-        self._write_state(script[0, 0], script[0, 1], script[0, 2:5], 0, P)
+        self._write_state(script[0, 0], script[0, 1], script[0, 2:5], 0, P,
+                          -1 if eos_token_id is None else int(eos_token_id))
         self.script_len = P
 
     # ------------------------------------------------------------------ launch
@@ -295,6 +299,7 @@ class Qwen3VLDecodeEngine:
         st = self.state_dev.view(torch.int64)
         st[0:5].copy_(self._start_dev)
         st[5].fill_(self.script_len)
+        st[AicasStepState.done_step.offset // 8].fill_(0)
         self.run(n, graph_steps)
         out.copy_(self.out_tokens[self.script_len:self.script_len + n], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
@@ -307,12 +312,20 @@ class Qwen3VLDecodeEngine:
         self.state_dev.copy_(snap)
 
     # ------------------------------------------------------------------ API
-    def generate(self, prompt, max_new_tokens: int, pos3=None, graph_steps: int = 32) -> torch.Tensor:
+    def done_step(self) -> int:
+        """0 while the request runs; s + 1 once step s produced the
+        end-of-sequence token (reads the device state)."""
+        return int(self.state_dev.view(torch.int64)[AicasStepState.done_step.offset // 8].item())
+
+    def generate(self, prompt, max_new_tokens: int, pos3=None, graph_steps: int = 32,
+                 eos_token_id: int | None = None) -> torch.Tensor:
         """Greedy decode: prefill `prompt` (one step per token), then
         max_new_tokens - 1 decode steps.  Returns the new tokens (CPU int64),
         like `GreedyDecodeEngine.generate` (evaluation_wrapper.py:149-315)
-        minus the prompt."""
-        self.load_script(prompt, pos3)
+        minus the prompt; with `eos_token_id` the tokens end at the first
+        generated EOS (included), detected on the device (the reference polls
+        a pinned host copy of each token for it, evaluation_wrapper.py:317-463)."""
+        self.load_script(prompt, pos3, eos_token_id=eos_token_id)
         P = self.script_len
         total = P + max_new_tokens - 1
         if total > self.max_steps or P + max_new_tokens > self.max_cache_len:
@@ -321,6 +334,9 @@ class Qwen3VLDecodeEngine:
         self.run(max_new_tokens - 1, graph_steps)
         toks = self.out_tokens[P - 1:P - 1 + max_new_tokens].cpu()
         self.check_error()
+        done = self.done_step()
+        if done:
+            toks = toks[:done - (P - 1)]
         return toks
 
     def check_error(self):

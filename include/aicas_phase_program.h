@@ -98,6 +98,8 @@ typedef struct AicasStepState {
   float inv_freq[64];   // rotary inverse frequencies (host computes them like HF)
   int32_t mrope_section[3];
   int32_t pad0;
+  int64_t eos_token;    // end-of-sequence id, or -1: a generated step whose argmax is this id ends the request
+  int64_t done_step;    // 0 while running; after the EOS step s, s + 1 -- every later launch returns at once
 } AicasStepState;
 
 #define AICAS_MAX_CTAS 256

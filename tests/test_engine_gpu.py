@@ -96,6 +96,28 @@ def test_engine_cuda_graph_replay_is_deterministic(cuda_device, state2):
     assert torch.equal(a, b) and torch.equal(a, c)
 
 
+def test_engine_device_side_eos(cuda_device, state2):
+    """A generated token equal to eos_token_id ends the request on the
+    device: generate() returns the tokens up to and including it, the step
+    state stops advancing (later launches, graph replays included, return at
+    once) and a request without EOS is unaffected."""
+    prompt = synthetic_prompt(40, seed=5).numpy()
+    eng = Qwen3VLDecodeEngine(state2, QWEN3VL_2B.with_layers(2), max_cache_len=256, max_steps=256)
+    ref = eng.generate(prompt, 40, graph_steps=16)
+    assert eng.done_step() == 0
+    # EOS = the first generated token not seen before, from the 4th on if any
+    k = next((i for i in range(3, len(ref)) if int(ref[i]) not in ref[:i].tolist()), 0)
+    eos = int(ref[k])
+    got = eng.generate(prompt, 40, graph_steps=16, eos_token_id=eos)
+    assert torch.equal(got, ref[:k + 1]), (got, ref[:k + 1])
+    P = len(prompt)
+    assert eng.done_step() == P + k  # the EOS came out of step P - 1 + k
+    st = eng.state_dev.view(torch.int64)
+    assert int(st[1]) == P + k  # cache slot of the step after EOS: no later launch advanced it
+    again = eng.generate(prompt, 40, graph_steps=16)  # a new request without EOS runs in full
+    assert torch.equal(again, ref)
+
+
 def test_engine_full_model_vision_prefix(cuda_device):
     """BASELINE config 4 shapes: 28 layers, 1024-token prefix with a 16x16
     vision grid (3-axis MRoPE), then greedy decode (64 steps here)."""
