@@ -317,20 +317,59 @@ class Qwen3VLDecodeEngine:
         end-of-sequence token (reads the device state)."""
         return int(self.state_dev.view(torch.int64)[AicasStepState.done_step.offset // 8].item())
 
+    def prefill_prompt(self, prompt, pos3=None, eos_token_id: int | None = None) -> int:
+        """Prefill the whole prompt in one pass (prefill.py: library GEMMs over
+        all prompt tokens, K/V written to cache slots [0, P)) and set the step
+        state so the device loop continues from the first generated token,
+        which is returned (its logits go to the logits ring, its id to
+        out_tokens[P - 1], as with the one-token-per-launch prefill)."""
+        from prefill import prefill
+
+        tokens = torch.as_tensor(prompt, dtype=torch.int64).reshape(-1).cpu()
+        P = tokens.numel()
+        if P < 1 or P >= self.max_cache_len or P > self.max_steps:
+            raise AicasError("prompt does not fit the cache")
+        if pos3 is None:
+            pos3 = torch.arange(P, dtype=torch.int64).expand(3, P)
+        pos3 = torch.as_tensor(pos3, dtype=torch.int64).reshape(3, P).cpu()
+        s, dev = self.shape, self.device
+        with torch.cuda.device(dev):
+            logits = prefill(tokens.to(dev), pos3.to(dev), self.embed, self.final_norm, self.layers, self.k_cache,
+                             self.v_cache, num_heads=s.num_heads, num_kv_heads=s.num_kv_heads, head_dim=s.head_dim,
+                             eps=float(s.rms_eps), inv_freq=self._inv_freq.to(dev), mrope_section=s.mrope_section)
+            first = int(torch.argmax(logits))  # first index of the max, like the device argmax
+            if self.logits is not None:
+                self.logits[(P - 1) % self.logits_ring].copy_(logits.to(torch.float16))
+            self.out_tokens.fill_(-1)
+            self.out_tokens[P - 1] = first
+            # step == script_len == P: every following step decodes freely
+            self._write_state(first, P, (pos3[:, -1] + 1).tolist(), P, P,
+                              -1 if eos_token_id is None else int(eos_token_id))
+            if eos_token_id is not None and first == int(eos_token_id):
+                self.state_dev.view(torch.int64)[AicasStepState.done_step.offset // 8].fill_(P)
+        self.script_len = P
+        return first
+
     def generate(self, prompt, max_new_tokens: int, pos3=None, graph_steps: int = 32,
-                 eos_token_id: int | None = None) -> torch.Tensor:
-        """Greedy decode: prefill `prompt` (one step per token), then
-        max_new_tokens - 1 decode steps.  Returns the new tokens (CPU int64),
-        like `GreedyDecodeEngine.generate` (evaluation_wrapper.py:149-315)
-        minus the prompt; with `eos_token_id` the tokens end at the first
-        generated EOS (included), detected on the device (the reference polls
-        a pinned host copy of each token for it, evaluation_wrapper.py:317-463)."""
-        self.load_script(prompt, pos3, eos_token_id=eos_token_id)
-        P = self.script_len
-        total = P + max_new_tokens - 1
-        if total > self.max_steps or P + max_new_tokens > self.max_cache_len:
+                 eos_token_id: int | None = None, prefill: str = "decode") -> torch.Tensor:
+        """Greedy decode: prefill `prompt`, then max_new_tokens - 1 decode
+        steps.  Returns the new tokens (CPU int64), like
+        `GreedyDecodeEngine.generate` (evaluation_wrapper.py:149-315) minus the
+        prompt; with `eos_token_id` the tokens end at the first generated EOS
+        (included), detected on the device (the reference polls a pinned host
+        copy of each token for it, evaluation_wrapper.py:317-463).
+        `prefill`: "decode" runs the prompt through the decode kernel one token
+        per launch; "gemm" prefills it in one pass (prefill_prompt)."""
+        P = len(torch.as_tensor(prompt).reshape(-1))
+        if P + max_new_tokens - 1 > self.max_steps or P + max_new_tokens > self.max_cache_len:
             raise AicasError("request exceeds max_steps / max_cache_len")
-        self.launch(P)
+        if prefill == "gemm":
+            self.prefill_prompt(prompt, pos3, eos_token_id=eos_token_id)
+        elif prefill == "decode":
+            self.load_script(prompt, pos3, eos_token_id=eos_token_id)
+            self.launch(P)
+        else:
+            raise ValueError(f"unknown prefill mode {prefill!r}")
         self.run(max_new_tokens - 1, graph_steps)
         toks = self.out_tokens[P - 1:P - 1 + max_new_tokens].cpu()
         self.check_error()

@@ -118,6 +118,31 @@ def test_engine_device_side_eos(cuda_device, state2):
     assert torch.equal(again, ref)
 
 
+def test_engine_gemm_prefill_then_device_decode(cuda_device, state2):
+    """prefill="gemm" (the whole vision-grid prompt in one pass, K/V written
+    to the engine's cache) followed by device decode: teacher-forced logits of
+    every step against the oracle, and the same tokens as the one-token-per-
+    launch prefill up to the first step where the oracle's own top-2 gap is
+    within tolerance (a near tie may send the two trajectories apart)."""
+    P, n = 300, 12
+    pos3, rope_delta = vision_grid_positions(P)
+    prompt = synthetic_prompt(P, seed=4321).numpy()
+    eng = Qwen3VLDecodeEngine(state2, QWEN3VL_2B.with_layers(2), max_cache_len=P + n, logits_ring=n, max_steps=P + n)
+    toks = eng.generate(prompt, n, pos3=pos3.numpy(), prefill="gemm").numpy()
+    gl = np.stack([eng.step_logits(P - 1 + i).float().cpu().numpy() for i in range(n)])
+    o = Qwen3VLOracle(state2, 2, mode="fp16", max_cache_len=P + n, inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
+    _, ol = o.greedy(prompt, n, pos3_prompt=pos3.numpy(), rope_delta=rope_delta, forced=toks)
+    diff = np.abs(gl - ol).max(axis=-1)
+    assert diff.max() <= LOGIT_ATOL, f"max logit diff per step {diff}"
+    assert np.array_equal(toks, np.argmax(gl, axis=-1))
+    ref = eng.generate(prompt, n, pos3=pos3.numpy(), prefill="decode").numpy()
+    top2 = np.sort(ol, axis=-1)[:, -2:]
+    for i in range(n):
+        if toks[i] != ref[i]:
+            assert top2[i, 1] - top2[i, 0] <= 2 * LOGIT_ATOL, (i, toks[i], ref[i])
+            break
+
+
 def test_engine_full_model_vision_prefix(cuda_device):
     """BASELINE config 4 shapes: 28 layers, 1024-token prefix with a 16x16
     vision grid (3-axis MRoPE), then greedy decode (64 steps here)."""
