@@ -73,7 +73,11 @@ class AicasStepState(ctypes.Structure):
     ]
 
 
-# Offsets of the scratch words the host reads (AicasScratch).
+# Streams of one batched launch (AICAS_MAX_BATCH).
+MAX_BATCH = 8
+
+# Offsets of the scratch words the host reads (AicasScratch; the batch
+# scratch block starts with the same words).
 SCRATCH_ERROR_OFFSET = 16
 
 _P = ctypes.c_void_p
@@ -102,6 +106,10 @@ SIGNATURES = {
     "aicas_lm_head_argmax_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_decode_program_f16": (_I, [_P, _I, _P, _P, _P]),
     "aicas_decode_program_trace_f16": (_I, [_P, _I, _P, _P, _P, _P]),
+    "aicas_batch_scratch_bytes": (ctypes.c_size_t, []),
+    "aicas_validate_batch_phases": (_I, [ctypes.POINTER(AicasPhase), _I]),
+    "aicas_decode_batch_f16": (_I, [_P, _I, _P, _I, _P, _P]),
+    "aicas_tile_weight_f16": (_I, [_P, _P, _I64, _I64, _P]),
 }
 
 _lock = threading.Lock()
@@ -147,6 +155,10 @@ def check(rc: int, what: str) -> None:
 
 def scratch_bytes() -> int:
     return int(lib().aicas_scratch_bytes())
+
+
+def batch_scratch_bytes() -> int:
+    return int(lib().aicas_batch_scratch_bytes())
 
 
 def error_message(code: int) -> str:

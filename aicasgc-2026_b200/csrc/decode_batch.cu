@@ -1,0 +1,1329 @@
+// Batched greedy decode step for B200 (sm_100a): up to 8 requests per launch.
+//
+// The same phase programs as the batch-1 kernel (decode_program.cu), run for
+// nb independent requests ("streams") at once.  Each stream has its own step
+// state (token, ragged cache position, 3-axis rope position, script, EOS),
+// its own KV cache slice and its own rows of every activation vector.  The
+// weights stream from HBM once per step for all streams, so each projection
+// is an [nb, k] x [k, n] contraction, and it runs on the tensor cores:
+//
+//   warp 0      producer: the CTA's weight / KV tiles, phase after phase, into
+//               a 3-stage shared-memory ring (cp.async.bulk, L2 evict_first).
+//   warps 1..8  consumers: per GEMV phase, poll the input rows of every active
+//               stream (LL flag-in-data words), apply the RMSNorm prologue
+//               with HF's fp16 rounding points and write the A operand
+//               (streams x k, fp16) into shared memory; then two of them (the
+//               warps whose TMEM lane quarter holds accumulator rows 0..31)
+//               run the epilogues.  Attention: the split-KV units of all
+//               streams, as in the batch-1 kernel.
+//   warp 9      L2 prefetch cursor, kL2Ahead tiles ahead of the ring.
+//   warp 10     MMA issuer and TMEM owner: per 32 KB weight tile (8 rows x
+//               2048 columns) 128 x tcgen05.mma.kind::f16 with M = 64 (the A
+//               operand's 8 stream rows, repeated: its 8-row groups share one
+//               address), N = 8 (the tile's weight rows), K = 16, accumulating
+//               fp32 in a 16-column TMEM slot (gate_up: gate in columns 0..7,
+//               up in 8..15; down_proj: the 3 K-chunks of a row group into
+//               the same columns).  One tcgen05.commit frees the ring stage
+//               when the tile's MMAs are done, another marks the slot full.
+//
+// Weight tile layout (aicas_tile_weight_f16): the 8 x 2048 block is stored
+// as [256 column groups][8 rows][8 columns], the K-major no-swizzle canonical
+// layout of the tcgen05 shared-memory descriptor (8-row x 16-byte core
+// matrices, K-adjacent core matrices 128 bytes apart), so one bulk copy lands
+// a tile ready for the tensor core.  The A operand uses the same layout with
+// the 8 streams as rows.
+//
+// Accumulator layout (M = 64, cta_group::1): row i of D sits in TMEM lane
+// (i % 16) + 32 (i / 16); rows 0..7 are the streams, so a warp of lane
+// quarter 0 reads stream b's 8 (or 16) sums in lane b with one tcgen05.ld.
+//
+// Attention: units (stream, KV head, 64-slot chunk) over all active streams,
+// split contiguously over the CTAs; each (stream, head) merge group is
+// combined from its CTAs' (log-sum-exp, acc) partials in a fixed split order,
+// exactly as in the batch-1 kernel.  Every wait is bounded
+// (aicas_device.cuh); after a failed wait the kernel keeps walking the same
+// program without waiting and ends with the error recorded.
+//
+// Reference behaviour per stream (file:line in the reference checkout) is
+// that of the batch-1 step: decode_gemv_kernel_fused.cuh:99-185 and
+// :850-1076, decode_gemv_kernel_matvec.cuh:209-343,
+// decode_attention_v4_kernel.cu:647-900, decode_small_ops_kernel.cu:115-186,
+// evaluation_wrapper.py:952 (argmax, first max wins).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "aicas_decode.h"
+#include "aicas_device.cuh"
+#include "aicas_phase_program.h"
+
+namespace aicas {
+
+int record_cuda_error(cudaError_t e);  // decode_program.cu
+
+namespace bat {
+
+constexpr int kMaxB = AICAS_MAX_BATCH;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kL2Warp = 1 + kConsumerWarps;
+constexpr int kMmaWarp = kL2Warp + 1;
+constexpr int kThreads = 32 * (kMmaWarp + 1);
+constexpr int kRows = 8;                        // weight rows per tile (MMA N)
+constexpr int kChunk = 2048;                    // columns per tile
+constexpr int kTileBytes = kRows * kChunk * 2;  // 32 KB
+constexpr int kStages = 3;
+constexpr int kMaxC = AICAS_MAX_K / kChunk;     // K chunks of the longest reduction
+constexpr int kMmaK = 16;
+constexpr int kMmasPerTile = kChunk / kMmaK;
+constexpr int kDSlots = 16;
+constexpr int kDSlotCols = 16;
+constexpr int kTmemCols = kDSlots * kDSlotCols;
+constexpr int kAttnChunk = 64;
+constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
+constexpr int kHD = AICAS_HEAD_DIM;
+constexpr int kMergePer = 4;
+constexpr int kL2Ahead = 8;
+// epilogue warps: consumer warps 3 and 7 are CTA warps 4 and 8, whose TMEM
+// lane quarter (warp % 4 == 0) is lanes 0..31
+constexpr int kEpiW0 = 3, kEpiW1 = 7;
+// instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0), both
+// K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kRows >> 3) << 17) | ((uint32_t)(64 >> 4) << 24);
+
+static_assert(kAttnChunk * kHD * 2 * 2 == kTileBytes, "attention tile must fill one stage");
+static_assert(kTmemCols == 256, "TMEM allocation is a power of two >= 32 columns");
+static_assert(offsetof(AicasBatchScratch, bar_count) == offsetof(AicasScratch, bar_count) &&
+                  offsetof(AicasBatchScratch, epoch) == offsetof(AicasScratch, epoch) &&
+                  offsetof(AicasBatchScratch, error) == offsetof(AicasScratch, error) &&
+                  offsetof(AicasBatchScratch, abort) == offsetof(AicasScratch, abort) &&
+                  offsetof(AicasBatchScratch, argmax_done) == offsetof(AicasScratch, argmax_done) &&
+                  offsetof(AicasBatchScratch, exit_count) == offsetof(AicasScratch, exit_count),
+              "the batch scratch header must match AicasScratch's");
+
+struct StreamIn {
+  int64_t token, pos, rope[3], step;
+  int32_t active;  // b < nb and the request has not ended
+  int32_t pad;
+};
+
+struct AttnSmem {
+  float q[2][kHD];
+  float kf[kHD], vf[kHD];
+  float wm[kConsumerWarps][2];
+  float wl[kConsumerWarps][2];
+  float wacc[kConsumerWarps][2][kHD];
+  float sc[kConsumerWarps][2 * kPosPerWarp];
+  __half nw[2 * kHD];  // q_norm, k_norm weights of the running phase
+};
+
+struct __align__(128) Smem {
+  uint8_t ring[kStages][kTileBytes];
+  uint8_t xa[kMaxC * kTileBytes];  // A operand: [k/8 column groups][8 streams][8] fp16
+  AttnSmem at;
+  float rope_c[kMaxB][kHD / 2], rope_s[kMaxB][kHD / 2];
+  float ssq[kConsumerWarps][kMaxB];
+  float best_v[2][kMaxB];
+  int best_i[2][kMaxB];
+  StreamIn sin[kMaxB];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t cempty[kStages];
+  uint64_t dfull[kDSlots];
+  uint64_t dempty[kDSlots];
+  uint64_t xready;  // the A operand of the next GEMV phase is in shared memory
+  uint64_t cdone;   // all consumer warps are done with TMEM
+  uint64_t mdone;   // every MMA the issuer launched has completed
+  uint32_t ring_it;
+  uint32_t tmem_base;
+  int32_t last_cta;
+};
+
+struct BatchArgs {
+  const AicasPhase* phases;
+  int n_phases;
+  int nb;
+  AicasStepState* states;
+  AicasBatchScratch* scratch;
+};
+
+struct Range {
+  int start, count;
+};
+
+__device__ __forceinline__ Range split_range(int total, int nct, int cta, int rot) {
+  int c = (cta - rot) % nct;
+  if (c < 0) c += nct;
+  const int base = total / nct, extra = total % nct;
+  return {c * base + min(c, extra), base + (c < extra ? 1 : 0)};
+}
+
+__device__ __forceinline__ int owner_of(int u, int total, int nct) {
+  const int base = total / nct, extra = total % nct;
+  const int big = extra * (base + 1);
+  if (u < big) return u / (base + 1);
+  return extra + (u - big) / base;
+}
+
+__device__ __forceinline__ int attn_ctas(int U, int nct) { return max(1, min(nct, U)); }
+
+// Cache slots [0, valid) of stream b in an attention phase; 0 when the
+// stream is inactive or its position is outside the cache.
+__device__ __forceinline__ int stream_valid(const AicasPhase& d, const StreamIn& in) {
+  if (!in.active || in.pos < 0 || in.pos >= d.max_len) return 0;
+  return (int)in.pos + 1;
+}
+
+// The attention units of a phase: stream b owns units [pre[b], pre[b + 1]),
+// KV head h of b units pre[b] + h * cph[b] + [0, cph[b]).
+struct AttnUnits {
+  int pre[kMaxB + 1];
+  int cph[kMaxB];
+  int valid[kMaxB];
+  __device__ __forceinline__ void init(const AicasPhase& d, const StreamIn* sin, int nb) {
+    int U = 0;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      pre[b] = U;
+      valid[b] = b < nb ? stream_valid(d, sin[b]) : 0;
+      cph[b] = (valid[b] + kAttnChunk - 1) / kAttnChunk;
+      U += d.kv_heads * cph[b];
+    }
+    pre[kMaxB] = U;
+  }
+  __device__ __forceinline__ int total() const { return pre[kMaxB]; }
+  // stream of unit u: the last b with pre[b] <= u (streams without units are skipped)
+  __device__ __forceinline__ int stream_of(int u) const {
+    int s = 0;
+#pragma unroll
+    for (int b = 1; b < kMaxB; ++b)
+      if (pre[b] <= u) s = b;
+    return s;
+  }
+};
+
+// a[i] for a small array without dynamic indexing (keeps it in registers)
+template <int N>
+__device__ __forceinline__ int select_i(const int (&a)[N], int i) {
+  int v = a[0];
+#pragma unroll
+  for (int b = 1; b < N; ++b)
+    if (b == i) v = a[b];
+  return v;
+}
+
+struct TileDesc {
+  const uint8_t* src;
+  int64_t src_stride;
+  uint32_t bytes;
+  int pieces;
+  bool mma;        // GEMV tile for the tensor core (else an attention tile read in place)
+  int c;           // K chunk of the tile
+  int part;        // gate_up: 0 gate, 1 up (accumulator columns 8..15)
+  bool group_end;  // last tile of its row group: the accumulator slot is complete
+};
+
+// Walks this CTA's tiles of the program in the order the consumers take
+// them; the producer, the L2 prefetch warp and the MMA issuer each run one.
+struct Cursor {
+  const AicasPhase* P;
+  int n_phases, nct, cta, nb;
+  const StreamIn* sin;
+  int ph = -1, ti = 0, n = 0;
+  int kind, C, T, rows_total;
+  Range rg;
+  AttnUnits au;
+
+  __device__ __forceinline__ void enter(int phase) {
+    ph = phase;
+    ti = 0;
+    n = 0;
+    if (ph >= n_phases) return;
+    const AicasPhase& d = P[ph];
+    kind = d.kind;
+    if (kind == AICAS_PH_ATTN) {
+      au.init(d, sin, nb);
+      const int U = au.total();
+      const int na = attn_ctas(U, nct);
+      rg = (U > 0 && cta < na) ? split_range(U, na, cta, 0) : Range{0, 0};
+      n = rg.count;
+    } else {
+      C = d.k / kChunk;
+      T = kind == AICAS_PH_GATEUP ? 2 : C;
+      rows_total = kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
+      rg = split_range(d.n / kRows, nct, cta, d.rot);
+      n = rg.count * T;
+    }
+  }
+
+  __device__ __forceinline__ bool next(TileDesc& td) {
+    while (ti >= n) {
+      if (ph >= n_phases) return false;
+      enter(ph + 1);
+      if (ph >= n_phases) return false;
+    }
+    const AicasPhase& d = P[ph];
+    if (kind == AICAS_PH_ATTN) {
+      const int u = rg.start + ti;
+      const int b = au.stream_of(u);
+      const int cph = select_i(au.cph, b), valid = select_i(au.valid, b);
+      const int r = u - select_i(au.pre, b);
+      const int h = r / cph, j = r % cph;
+      const int p0 = j * kAttnChunk;
+      const size_t off = (((size_t)b * d.kv_heads + h) * d.max_len + p0) * kHD * 2;
+      td.src = reinterpret_cast<const uint8_t*>(d.k_cache) + off;
+      td.src_stride = reinterpret_cast<const uint8_t*>(d.v_cache) - reinterpret_cast<const uint8_t*>(d.k_cache);
+      td.bytes = min(kAttnChunk, valid - p0) * kHD * 2;
+      td.pieces = 2;
+      td.mma = false;
+      td.c = td.part = 0;
+      td.group_end = false;
+    } else {
+      const int g = rg.start + ti / T, t = ti % T;
+      const bool gu = kind == AICAS_PH_GATEUP;
+      const int c = gu ? 0 : t;
+      const int row0 = g * kRows + (gu && t == 1 ? d.n : 0);
+      td.src = reinterpret_cast<const uint8_t*>(d.w) + ((size_t)c * rows_total + row0) * kChunk * 2;
+      td.src_stride = 0;
+      td.bytes = kTileBytes;
+      td.pieces = 1;
+      td.mma = true;
+      td.c = c;
+      td.part = gu ? t : 0;
+      td.group_end = t == T - 1;
+    }
+    ++ti;
+    return true;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// tcgen05 pieces of the batch kernel
+// ---------------------------------------------------------------------------
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 8 LL words {fp16 value, epoch} with two 16-byte stores (each word is
+// written whole, which is all the LL protocol needs).
+__device__ __forceinline__ void ll_store8(uint32_t* p, const float (&y)[8], uint32_t epoch16) {
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w[j] = (epoch16 << 16) | (uint32_t)__half_as_ushort(__float2half_rn(y[j]));
+  asm volatile("st.relaxed.gpu.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3])
+               : "memory");
+  asm volatile("st.relaxed.gpu.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p + 4), "r"(w[4]), "r"(w[5]),
+               "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Producer, L2 prefetch, MMA issuer
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void run_producer(const BatchArgs& a, Smem& sm, AicasScratch* s) {
+  if ((threadIdx.x & 31) != 0) return;
+  const uint64_t pol = l2_evict_first_policy();
+  Cursor cur{a.phases, a.n_phases, (int)gridDim.x, (int)blockIdx.x, a.nb, sm.sin};
+  TileDesc td;
+  uint32_t it = 0;
+  while (cur.next(td)) {
+    const int st = it % kStages;
+    if (it >= (uint32_t)kStages && !mbar_wait_bounded(&sm.empty[st], ((it / kStages) - 1) & 1u, s, kErrEmptyTimeout))
+      break;
+    mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
+    for (int i = 0; i < td.pieces; ++i)
+      bulk_g2s(sm.ring[st] + i * (kTileBytes / 2), td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
+    ++it;
+    *reinterpret_cast<volatile uint32_t*>(&sm.ring_it) = it;
+  }
+  // every issued copy lands before the CTA may exit
+  const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0;
+  for (uint32_t k = first; k < it; ++k) {
+    const int st = k % kStages;
+    if (!mbar_wait_bounded(&sm.full[st], (k / kStages) & 1u, s, kErrDrainTimeout)) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.full[st], (k / kStages) & 1u)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void run_l2_prefetcher(const BatchArgs& a, Smem& sm, AicasScratch* s) {
+  if ((threadIdx.x & 31) != 0) return;
+  Cursor pf{a.phases, a.n_phases, (int)gridDim.x, (int)blockIdx.x, a.nb, sm.sin};
+  TileDesc td;
+  const uint64_t pol_last = l2_evict_last_policy();
+  for (uint32_t k = 0; pf.next(td); ++k) {
+    uint64_t t0 = 0;
+    uint32_t ri = 0;
+    for (uint32_t it = 0;; ++it) {
+      ri = *reinterpret_cast<volatile uint32_t*>(&sm.ring_it);
+      if (k < ri + (uint32_t)kL2Ahead) break;
+      if (it == 0) t0 = globaltimer_ns();
+      if ((it & 15u) == 15u && (ld_volatile_int(&s->abort) || globaltimer_ns() - t0 > kWaitLimitNs)) return;
+      __nanosleep(128);
+    }
+    if (k < ri) continue;
+    for (int i = 0; i < td.pieces; ++i) bulk_prefetch_l2_hint(td.src + i * td.src_stride, td.bytes, pol_last);
+  }
+}
+
+// MMA issuer (lane 0 of the last warp; the whole warp owns the TMEM
+// allocation).  GEMV tiles: wait for the phase's A operand (once per phase),
+// a free accumulator slot (first tile of a row group) and the landed tile,
+// issue the tile's 128 MMAs, commit the stage (and the slot at the group's
+// last tile).  Attention tiles: pass the consumers' in-place release on to
+// the producer.
+__device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScratch* s, uint32_t tmem) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    Cursor cur{a.phases, a.n_phases, (int)gridDim.x, (int)blockIdx.x, a.nb, sm.sin};
+    TileDesc td;
+    uint32_t it = 0, gc = 0, xph = 0, cpar = 0;
+    int x_phase = -1;
+    const uint32_t xa0 = smem_addr(sm.xa);
+    const uint32_t ring0 = smem_addr(sm.ring[0]);
+    while (cur.next(td)) {
+      const int st = it % kStages;
+      const uint32_t par = (it / kStages) & 1u;
+      if (td.mma) {
+        if (cur.ph != x_phase) {
+          if (!mbar_wait_bounded(&sm.xready, xph & 1u, s, kErrTmemTimeout)) break;
+          ++xph;
+          x_phase = cur.ph;
+        }
+        const uint32_t slot = gc % kDSlots;
+        if (td.c == 0 && td.part == 0 && gc >= (uint32_t)kDSlots &&
+            !mbar_wait_bounded(&sm.dempty[slot], ((gc / kDSlots) - 1) & 1u, s, kErrTmemTimeout))
+          break;
+        if (!mbar_wait_bounded(&sm.full[st], par, s, kErrFullTimeout)) break;
+        tc_fence_after();
+        // descriptors advance 256 bytes (16 units of the 16-byte start address field) per K step
+        const uint64_t adesc = smem_desc_kmajor(xa0 + td.c * kTileBytes, 128, 0);
+        const uint64_t bdesc = smem_desc_kmajor(ring0 + st * kTileBytes, 128, 1024);
+        const uint32_t d = tmem + slot * kDSlotCols + td.part * kRows;
+#pragma unroll 8
+        for (int kk = 0; kk < kMmasPerTile; ++kk)
+          umma_f16(d, adesc + 16u * kk, bdesc + 16u * kk, kIdesc, (kk > 0 || td.c > 0) ? 1u : 0u);
+        tcgen05_commit(&sm.empty[st]);
+        if (td.group_end) {
+          tcgen05_commit(&sm.dfull[slot]);
+          ++gc;
+        }
+      } else {
+        if (!mbar_wait_bounded(&sm.cempty[st], (cpar >> st) & 1u, s, kErrEmptyTimeout)) break;
+        cpar ^= 1u << st;
+        mbar_arrive(&sm.empty[st]);
+      }
+      ++it;
+    }
+    // every MMA launched so far has completed before TMEM may be freed
+    tcgen05_commit(&sm.mdone);
+    uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&sm.mdone, 0)) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrTmemTimeout);
+        break;
+      }
+    }
+    t0 = globaltimer_ns();
+    while (!mbar_try_wait(&sm.cdone, 0)) {
+      if (globaltimer_ns() - t0 > 2 * kWaitLimitNs) {
+        raise_error(s, kErrTmemTimeout);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_after();
+  tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Consumers (warps 1..8)
+// ---------------------------------------------------------------------------
+struct Consumer {
+  const BatchArgs& a;
+  Smem& sm;
+  AicasScratch* s;
+  AicasBatchScratch* bs;
+  int tid, w, lane, nct, cta, nb;
+  uint32_t tmem;
+  uint32_t epoch_base;
+  uint32_t gc = 0;   // accumulator groups consumed (epilogue warps)
+  uint32_t rit = 0;  // ring tiles passed (GEMV tiles via the MMA warp, attention tiles read in place)
+  int ph = 0;
+
+  __device__ __forceinline__ bool active(int b) const { return b < nb && sm.sin[b].active; }
+
+  __device__ __forceinline__ int64_t checked_token(int b, int rows) {
+    const int64_t t = sm.sin[b].token;
+    if (t >= 0 && t < rows) return t;
+    raise_error(s, kErrBadInput);
+    return 0;
+  }
+
+  // Interleaved-MRoPE cos/sin of every active stream's position, once per
+  // launch (modeling_qwen3_vl.py:352-386): frequency i takes axis 1 (h) when
+  // i % 3 == 1 and i < 3 section[1], axis 2 (w) when i % 3 == 2 and
+  // i < 3 section[2], else axis 0 (t); fp32 math, rounded to fp16.
+  __device__ __noinline__ void init_rope() {
+    for (int e = tid; e < kMaxB * (kHD / 2); e += kConsumerThreads) {
+      const int b = e / (kHD / 2), i = e % (kHD / 2);
+      if (!active(b)) continue;
+      const AicasStepState* stt = a.states + b;
+      int axis = 0;
+      if (i % 3 == 1 && i < 3 * stt->mrope_section[1]) axis = 1;
+      else if (i % 3 == 2 && i < 3 * stt->mrope_section[2]) axis = 2;
+      const float ang = stt->inv_freq[i] * (float)sm.sin[b].rope[axis];
+      sm.rope_c[b][i] = r16(cosf(ang));
+      sm.rope_s[b][i] = r16(sinf(ang));
+    }
+  }
+
+  // The A operand of a GEMV phase: thread (b = tid % 8, g = tid / 8) takes
+  // column groups v = g + 32 i of stream b (8 columns each), so the 8 lanes
+  // of a lane octet write one contiguous 128-byte core-matrix row set.
+  // RMSNorm (F_NORM, k == 2048) with HF's rounding points
+  // (modeling_qwen3_vl.py:398-403).  Inactive streams read as zeros.
+  __device__ __forceinline__ void build_x(const AicasPhase& d) {
+    const int k = d.k, C = k / kChunk;
+    const int b = tid & 7, g = tid >> 3;
+    const bool act = active(b);
+    const uint32_t ep = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
+    const bool ll = d.flags & AICAS_F_LL_IN;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(d.x) + (size_t)b * k;
+    const __half* xh = reinterpret_cast<const __half*>(d.x);
+    if (d.flags & AICAS_F_X_EMBED) xh += (act ? (size_t)checked_token(b, d.embed_rows) : 0) * k;
+    else xh += (size_t)b * k;
+    for (int i0 = 0; i0 < 8 * C; i0 += 8) {
+      int cols[8];
+      uint4 raw[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cols[i] = act ? 8 * (g + 32 * (i0 + i)) : -1;
+      if (ll) {
+        ll_poll8_n<8>(xw, cols, ep, s, raw);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) raw[i] = cols[i] >= 0 ? ldcg_u4(xh + cols[i]) : make_uint4(0, 0, 0, 0);
+      }
+      if (d.flags & AICAS_F_NORM) {  // k == 2048: this is the only round
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw[i]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(hp[q]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+        // lanes l, l ^ 8, l ^ 16, l ^ 24 hold the same stream
+        ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+        if (lane < 8) sm.ssq[w][lane] = ss;
+        consumer_sync(kConsumerThreads);
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kConsumerWarps; ++i) tot += sm.ssq[i][b];
+        const float inv = rsqrtf(tot / (float)k + d.eps);
+        const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 wr = __ldg(reinterpret_cast<const uint4*>(nw + 8 * (g + 32 * i)));
+          __half2* hp = reinterpret_cast<__half2*>(&raw[i]);
+          const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(hp[q]);
+            const float2 wf = __half22float2(wp[q]);
+            hp[q] = __floats2half2_rn(wf.x * r16(f.x * inv), wf.y * r16(f.y * inv));
+          }
+          if (!act) raw[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = g + 32 * (i0 + i);  // column group 0 .. k/8 - 1
+        *reinterpret_cast<uint4*>(sm.xa + (v / 256) * kTileBytes + (v % 256) * 128 + b * 16) = raw[i];
+      }
+    }
+    // the MMA reads the operand through the async proxy
+    fence_proxy_async_smem();
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) mbar_arrive(&sm.xready);
+  }
+
+  __device__ __forceinline__ void run_gemv(const AicasPhase& d) {
+    const int n = d.n, flags = d.flags, kind = d.kind;
+    const Range rg = split_range(n / kRows, nct, cta, d.rot);
+    const bool lm = kind == AICAS_PH_LMHEAD;
+    // the MMA warp consumes these tiles; the ring position moves past them
+    rit += rg.count * (kind == AICAS_PH_GATEUP ? 2 : d.k / kChunk);
+    if (rg.count > 0) build_x(d);
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+    if ((w == kEpiW0 || w == kEpiW1) && rg.count > 0) {
+      const bool gu = kind == AICAS_PH_GATEUP;
+      const int b = lane;
+      const bool act = b < kMaxB && active(b);
+      const uint32_t ep16 = (epoch_base + (uint32_t)ph + 1) & 0xffffu;
+      uint32_t* const out = reinterpret_cast<uint32_t*>(d.out);
+      const __half* const bias = reinterpret_cast<const __half*>(d.bias);
+      __half* logits = nullptr;
+      if (lm && act) {
+        const AicasStepState* stt = a.states + b;
+        if (stt->logits) {
+          const int64_t ring = stt->logits_ring > 0 ? stt->logits_ring : 1;
+          logits = reinterpret_cast<__half*>(stt->logits) + (size_t)(sm.sin[b].step % ring) * n;
+        }
+      }
+      const __half* embed_row = nullptr;
+      if ((flags & AICAS_F_RESID_EMBED) && act)
+        embed_row = reinterpret_cast<const __half*>(d.resid) + (size_t)checked_token(b, d.embed_rows) * n;
+      const uint32_t mine = w == kEpiW1 ? 1u : 0u;
+      for (int gi = 0; gi < rg.count; ++gi, ++gc) {
+        if ((gc & 1u) != mine) continue;
+        const uint32_t slot = gc % kDSlots;
+        mbar_wait_bounded(&sm.dfull[slot], (gc / kDSlots) & 1u, s, kErrTmemTimeout);
+        tc_fence_after();
+        uint32_t v[16];
+        if (gu) tmem_ld_x16(tmem + slot * kDSlotCols, v);
+        else tmem_ld_x8(tmem + slot * kDSlotCols, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.dempty[slot]);
+        if (!act) continue;
+        const int row0 = (rg.start + gi) * kRows;
+        float y[8];
+        if (gu) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float gq = r16(__uint_as_float(v[j])), uq = r16(__uint_as_float(v[8 + j]));
+            const float sl = r16(gq / (1.0f + expf(-gq)));
+            y[j] = r16(sl * uq);
+          }
+        } else {
+          float rv[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) rv[j] = 0.f;
+          if (flags & AICAS_F_RESID) {
+            if (flags & AICAS_F_LL_RESID) {  // complete before this phase: data only
+              const uint32_t* rw = reinterpret_cast<const uint32_t*>(d.resid) + (size_t)b * n + row0;
+              const uint4 r0 = ll_load4w(rw), r1 = ll_load4w(rw + 4);
+              const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+              for (int j = 0; j < 8; ++j) rv[j] = __half2float(__ushort_as_half((unsigned short)(rr[j] & 0xffffu)));
+            } else {
+              const __half* rp = embed_row ? embed_row : reinterpret_cast<const __half*>(d.resid) + (size_t)b * n;
+              const uint4 r = ldcg_u4(rp + row0);
+              const __half2* hp = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                rv[2 * q] = __low2float(hp[q]);
+                rv[2 * q + 1] = __high2float(hp[q]);
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float acc = __uint_as_float(v[j]);
+            if (flags & AICAS_F_BIAS) acc += __half2float(bias[row0 + j]);
+            y[j] = r16(acc);
+            if (flags & AICAS_F_RESID) y[j] = r16(rv[j] + y[j]);
+          }
+        }
+        if (lm) {
+          if (logits) {
+            __half2 hv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) hv[q] = __floats2half2_rn(y[2 * q], y[2 * q + 1]);
+            *reinterpret_cast<uint4*>(logits + row0) = *reinterpret_cast<const uint4*>(hv);
+          }
+          // this lane's rows ascend: strict > keeps the first max
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (y[j] > best_v) {
+              best_v = y[j];
+              best_i = row0 + j;
+            }
+        } else {
+          ll_store8(out + (size_t)b * n + row0, y, ep16);
+        }
+      }
+    } else if (w == kEpiW0 || w == kEpiW1) {
+      gc += rg.count;  // (rg.count == 0: nothing to consume)
+    }
+    if (lm) finish_argmax(best_v, best_i);
+  }
+
+  // Per stream: the best (value, row) of the two epilogue warps, then of all
+  // CTAs (the last CTA to arrive reduces, one warp per stream, and advances
+  // the stream's step state exactly like the batch-1 kernel).
+  __device__ __forceinline__ void finish_argmax(float bv, int bi) {
+    if ((w == kEpiW0 || w == kEpiW1) && lane < kMaxB) {
+      sm.best_v[w == kEpiW1][lane] = bv;
+      sm.best_i[w == kEpiW1][lane] = bi;
+    }
+    consumer_sync(kConsumerThreads);
+    if (tid < kMaxB) {
+      float v = sm.best_v[0][tid];
+      int i = sm.best_i[0][tid];
+      if (sm.best_v[1][tid] > v || (sm.best_v[1][tid] == v && sm.best_i[1][tid] < i)) {
+        v = sm.best_v[1][tid];
+        i = sm.best_i[1][tid];
+      }
+      bs->am_val[cta][tid] = v;
+      bs->am_idx[cta][tid] = i;
+    }
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      __threadfence();
+      const uint32_t prev = atomicAdd(&bs->argmax_done, 1u);
+      sm.last_cta = prev == (uint32_t)nct - 1;
+    }
+    consumer_sync(kConsumerThreads);
+    if (!sm.last_cta) return;
+    __threadfence();
+    const int b = w;  // one warp per stream
+    if (active(b)) {
+      float v = -INFINITY;
+      int i = 0x7fffffff;
+      for (int c = lane; c < nct; c += 32) {
+        const float cv = __ldcg(&bs->am_val[c][b]);
+        const int ci = __ldcg(&bs->am_idx[c][b]);
+        if (cv > v || (cv == v && ci < i)) {
+          v = cv;
+          i = ci;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+        if (v2 > v || (v2 == v && i2 < i)) {
+          v = v2;
+          i = i2;
+        }
+      }
+      if (lane == 0) {
+        AicasStepState* stt = a.states + b;
+        const StreamIn& in = sm.sin[b];
+        const int64_t step = in.step;
+        if (stt->out_tokens && step < stt->max_steps) stt->out_tokens[step] = i;
+        const int64_t nx = step + 1;
+        if (stt->script && nx < stt->script_len) {
+          const int64_t* e = stt->script + nx * 5;
+          stt->token = e[0];
+          stt->cache_pos = e[1];
+          stt->rope[0] = e[2];
+          stt->rope[1] = e[3];
+          stt->rope[2] = e[4];
+        } else {
+          stt->token = i;
+          stt->cache_pos = in.pos + 1;
+          stt->rope[0] = in.rope[0] + 1;
+          stt->rope[1] = in.rope[1] + 1;
+          stt->rope[2] = in.rope[2] + 1;
+        }
+        stt->step = nx;
+        if (stt->eos_token >= 0 && i == stt->eos_token && nx >= stt->script_len) stt->done_step = nx;
+        __threadfence();
+      }
+    }
+    if (tid == 0) bs->argmax_done = 0;
+  }
+
+  // One 128-dim head per warp (lane l holds dims 4l..4l+3): per-head RMSNorm
+  // (modeling_qwen3_vl.py:398-403) and rotary embedding (:124-128, :427-431).
+  __device__ __forceinline__ void norm_rope_head(float (&v)[4], const __half* nw, float eps, const float (&cs)[4],
+                                                 const float (&sn)[4]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
+    const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
+    float xn[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) xn[e] = r16(__half2float(nw[lane * 4 + e]) * r16(v[e] * inv));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
+      const float rot = lane < 16 ? -p : p;
+      v[e] = r16(r16(xn[e] * cs[e]) + r16(rot * sn[e]));
+    }
+  }
+
+  // Reduce-scatter of 16 per-lane partial sums across the warp: lane l ends
+  // with the warp total of value index idx (see the batch-1 kernel).
+  __device__ __forceinline__ float reduce_scatter16(float (&a)[16], int& idx) {
+    int base = 0;
+    int o = 16;
+#pragma unroll
+    for (int n = 16; n > 1; n >>= 1, o >>= 1) {
+      const bool hi = lane & o;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = hi ? a[i] : a[i + n / 2];
+        const float keep = hi ? a[i + n / 2] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+      base += hi ? n / 2 : 0;
+    }
+    float t = a[0];
+#pragma unroll
+    for (; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    idx = base;
+    return t;
+  }
+
+  __device__ __forceinline__ void run_attention(const AicasPhase& d) {
+    AttnSmem& at = sm.at;
+    AttnUnits au;
+    au.init(d, sm.sin, nb);
+    const int U = au.total();
+    if (tid == 0 && cta == 0) {
+      for (int b = 0; b < nb; ++b)
+        if (active(b) && au.valid[b] == 0) raise_error(s, kErrBadInput);
+    }
+    if (U == 0) return;
+    const int na = attn_ctas(U, nct);
+    const Range rg = cta < na ? split_range(U, na, cta, 0) : Range{0, 0};
+    const uint32_t* qkv_w = reinterpret_cast<const uint32_t*>(d.x);
+    const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
+    __half* kc = reinterpret_cast<__half*>(d.k_cache);
+    __half* vc = reinterpret_cast<__half*>(d.v_cache);
+    const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
+    const float scale = d.scale;
+    const uint32_t ep = epoch_base + (uint32_t)ph + 1;
+    float m[2], l[2], acc[2][4];
+    float qreg[2][4];
+    int cur_b = -1;
+    float cs[4], sn[4];
+    for (int u = rg.start; u < rg.start + rg.count; ++u) {
+      const int b = au.stream_of(u);
+      const int cph = select_i(au.cph, b), valid = select_i(au.valid, b);
+      const int r = u - select_i(au.pre, b);
+      const int h = r / cph, j = r % cph;
+      const int pos = valid - 1, jpos = pos / kAttnChunk;
+      const bool seg_start = (u == rg.start) || (j == 0);
+      const bool seg_end = (u == rg.start + rg.count - 1) || (j == cph - 1);
+      const size_t head_off = ((size_t)b * d.kv_heads + h) * d.max_len;
+      if (b != cur_b) {
+        cur_b = b;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          cs[e] = sm.rope_c[b][(lane * 4 + e) % (kHD / 2)];
+          sn[e] = sm.rope_s[b][(lane * 4 + e) % (kHD / 2)];
+        }
+      }
+      if (seg_start) {
+        const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
+        const bool has_pos = jpos >= j && jpos <= last_j;
+        const uint32_t* xw = qkv_w + (size_t)b * d.k;
+        if (w < 2) {  // query heads 2h, 2h+1 of stream b
+          const int col = (h * 2 + w) * kHD + lane * 4;
+          const uint2 raw = ll_poll4(xw, col, x_epoch, s);
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+          norm_rope_head(v, at.nw, d.eps, cs, sn);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) at.q[w][lane * 4 + e] = v[e];
+        } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
+          const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
+          const uint2 raw = ll_poll4(xw, off, x_epoch, s);
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+          if (w == 2) norm_rope_head(v, at.nw + kHD, d.eps, cs, sn);
+          float* dst = w == 2 ? at.kf : at.vf;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
+          __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
+          __half* cache = w == 2 ? kc : vc;
+          *reinterpret_cast<uint2*>(cache + (head_off + pos) * kHD + lane * 4) = *reinterpret_cast<uint2*>(o);
+        }
+        consumer_sync(kConsumerThreads);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) qreg[g][e] = at.q[g][lane * 4 + e];
+          m[g] = -INFINITY;
+          l[g] = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+        }
+      }
+      const int st = rit % kStages;
+      mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
+      const int p0 = j * kAttnChunk;
+      const uint8_t* kt = sm.ring[st];
+      const uint8_t* vt = sm.ring[st] + kTileBytes / 2;
+      float kv[kPosPerWarp][4];
+#pragma unroll
+      for (int i = 0; i < kPosPerWarp; ++i) {
+        const int p = p0 + w * kPosPerWarp + i;
+        if (p == pos) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kv[i][e] = at.kf[lane * 4 + e];
+        } else {
+          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
+          const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+          kv[i][0] = __low2float(kh[0]);
+          kv[i][1] = __high2float(kh[0]);
+          kv[i][2] = __low2float(kh[1]);
+          kv[i][3] = __high2float(kh[1]);
+        }
+      }
+      float part[2 * kPosPerWarp];
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int i = 0; i < kPosPerWarp; ++i)
+          part[g * kPosPerWarp + i] =
+              qreg[g][0] * kv[i][0] + qreg[g][1] * kv[i][1] + qreg[g][2] * kv[i][2] + qreg[g][3] * kv[i][3];
+      int vidx;
+      const float tot = reduce_scatter16(part, vidx);
+      if ((lane & 1) == 0) at.sc[w][vidx] = tot;
+      __syncwarp();
+      const int pw = p0 + w * kPosPerWarp;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        float cmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kPosPerWarp; ++i)
+          if (pw + i < valid) cmax = fmaxf(cmax, at.sc[w][g * kPosPerWarp + i] * scale);
+        const float mn = fmaxf(m[g], cmax);
+        if (mn == -INFINITY) continue;
+        const float corr = expf(m[g] - mn);
+        l[g] *= corr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+        m[g] = mn;
+      }
+#pragma unroll 1
+      for (int i = 0; i < kPosPerWarp && pw + i < valid; ++i) {
+        const int p = pw + i;
+        float vv[4];
+        if (p == pos) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
+        } else {
+          const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
+          const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+          vv[0] = __low2float(vh[0]);
+          vv[1] = __high2float(vh[0]);
+          vv[2] = __low2float(vh[1]);
+          vv[3] = __high2float(vh[1]);
+        }
+        const float pr0 = expf(at.sc[w][i] * scale - m[0]);
+        const float pr1 = expf(at.sc[w][kPosPerWarp + i] * scale - m[1]);
+        l[0] += pr0;
+        l[1] += pr1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[0][e] += pr0 * vv[e];
+          acc[1][e] += pr1 * vv[e];
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.cempty[st]);
+      ++rit;
+      if (seg_end) {
+        if (lane == 0) {
+          at.wm[w][0] = m[0];
+          at.wm[w][1] = m[1];
+          at.wl[w][0] = l[0];
+          at.wl[w][1] = l[1];
+        }
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
+        consumer_sync(kConsumerThreads);
+        const int G = b * d.kv_heads + h;  // merge group (stream, KV head)
+        const int gfirst = select_i(au.pre, b) + h * cph;
+        const int first_owner = owner_of(gfirst, U, na);
+        const int last_owner = owner_of(gfirst + cph - 1, U, na);
+        const int split = cta - first_owner;
+        const int nsplit = last_owner - first_owner + 1;
+        const int g = tid / kHD, t = tid % kHD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
+        float L = 0.f, A = 0.f;
+#pragma unroll 1
+        for (int i = 0; i < kConsumerWarps; ++i) {
+          const float mi = at.wm[i][g];
+          if (mi != -INFINITY) {
+            const float f = expf(mi - M);
+            L += at.wl[i][g] * f;
+            A += at.wacc[i][g][t] * f;
+          }
+        }
+        const float lse = M + logf(L), o = A / L;
+        uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
+        if (nsplit == 1) {
+          ll_store(out_w + (h * 2 + g) * kHD + t, o, ep & 0xffffu);
+        } else {
+          uint64_t* const hp = &bs->part[G][0][0][0];
+          constexpr int kSplitStride = 2 * (kHD + 1);
+          if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
+          ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
+          // every CTA of the group merges a 1/nsplit slice of its 256
+          // outputs over all splits in order (see the batch-1 kernel)
+          const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
+          const int npairs = q1 - q0;
+          int tpo = 16;
+          while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
+          const int nact = npairs * tpo;
+          if ((tid & ~31) < nact) {
+            const bool actv = tid < nact;
+            const int pl = tid / tpo, sub = tid % tpo;
+            const int q = q0 + (actv ? pl : 0), gq = q / kHD, tq = q % kHD;
+            const uint64_t* const base = hp + gq * (kHD + 1);
+            float mx = -INFINITY, S = 0.f, ac = 0.f;
+#pragma unroll 1
+            for (int b0 = actv ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
+              uint64_t lw[kMergePer], ow[kMergePer];
+              uint32_t lpend = 0u;
+#pragma unroll
+              for (int i = 0; i < kMergePer; ++i)
+                if (b0 + i * tpo < nsplit) lpend |= 1u << i;
+              uint32_t opend = lpend;
+              const uint32_t have = lpend;
+              uint64_t t0 = 0;
+#pragma unroll 1
+              for (uint32_t it = 0;; ++it) {
+                const uint32_t lp = lpend, op = opend;
+#pragma unroll
+                for (int i = 0; i < kMergePer; ++i) {
+                  const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
+                  if (lp & (1u << i)) lw[i] = ll64_load(sp);
+                  if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
+                }
+                lpend = opend = 0u;
+#pragma unroll
+                for (int i = 0; i < kMergePer; ++i) {
+                  if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
+                  if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
+                }
+                if ((lpend | opend) == 0u) break;
+                if (it == 0) t0 = globaltimer_ns();
+                if ((it & 31u) == 31u) {
+                  if (ld_volatile_int(&s->abort)) break;
+                  if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    raise_error(s, kErrInputTimeout);
+                    break;
+                  }
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < kMergePer; ++i) {
+                if (have & (1u << i)) {
+                  const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
+                  if (li > mx) {
+                    const float c = expf(mx - li);
+                    S = S * c + 1.f;
+                    ac = ac * c + oi;
+                    mx = li;
+                  } else {
+                    const float c = expf(li - mx);
+                    S += c;
+                    ac += c * oi;
+                  }
+                }
+              }
+            }
+            for (int o2 = 1; o2 < tpo; o2 <<= 1) {
+              const float m2 = __shfl_xor_sync(0xffffffffu, mx, o2);
+              const float s2 = __shfl_xor_sync(0xffffffffu, S, o2);
+              const float a2 = __shfl_xor_sync(0xffffffffu, ac, o2);
+              const float mm = fmaxf(mx, m2);
+              if (mm != -INFINITY) {
+                const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
+                const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
+                S = S * f1 + s2 * f2;
+                ac = ac * f1 + a2 * f2;
+                mx = mm;
+              }
+            }
+            if (actv && sub == 0) ll_store(out_w + (h * 2 + gq) * kHD + tq, ac / S, ep & 0xffffu);
+          }
+        }
+      }
+    }
+  }
+
+  __device__ __forceinline__ void run() {
+    init_rope();
+    for (ph = 0; ph < a.n_phases; ++ph) {
+      const AicasPhase& d = a.phases[ph];
+      consumer_sync(kConsumerThreads);  // every warp is done with the previous phase's shared buffers
+      if (d.kind == AICAS_PH_ATTN) {
+        if (tid < 2 * kHD / 8) {
+          const __half* src = reinterpret_cast<const __half*>(tid < kHD / 8 ? d.norm_w : d.norm_w2);
+          const int v = tid % (kHD / 8);
+          *reinterpret_cast<uint4*>(&sm.at.nw[(tid / (kHD / 8)) * kHD + v * 8]) =
+              __ldg(reinterpret_cast<const uint4*>(src) + v);
+        }
+        consumer_sync(kConsumerThreads);
+        run_attention(d);
+      } else {
+        run_gemv(d);
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.cdone);
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(&bs->exit_count, 1u) == (uint32_t)nct - 1) {
+        bs->exit_count = 0;
+        bs->epoch = epoch_base + (uint32_t)a.n_phases + 1;
+        __threadfence();
+      }
+    }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_constant__ BatchArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  AicasScratch* s = reinterpret_cast<AicasScratch*>(a.scratch);
+  if (threadIdx.x < kMaxB) {
+    const int b = threadIdx.x;
+    StreamIn in{};
+    if (b < a.nb) {
+      const volatile AicasStepState* st = a.states + b;
+      in.active = st->done_step == 0 ? 1 : 0;
+      in.token = st->token;
+      in.pos = st->cache_pos;
+      in.rope[0] = st->rope[0];
+      in.rope[1] = st->rope[1];
+      in.rope[2] = st->rope[2];
+      in.step = st->step;
+    }
+    sm.sin[b] = in;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+      mbar_init(&sm.cempty[i], kConsumerWarps);
+    }
+    for (int i = 0; i < kDSlots; ++i) {
+      mbar_init(&sm.dfull[i], 1);
+      mbar_init(&sm.dempty[i], 1);
+    }
+    mbar_init(&sm.xready, 1);
+    mbar_init(&sm.cdone, kConsumerWarps);
+    mbar_init(&sm.mdone, 1);
+    sm.ring_it = 0;
+    sm.last_cta = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  int any = 0;
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) any |= sm.sin[b].active;
+  if (!any) return;  // every request has ended: the whole grid returns before any barrier or copy
+  const int warp = threadIdx.x / 32;
+  if (warp == kMmaWarp) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&sm.tmem_base);
+  if (warp == kMmaWarp) {
+    run_mma(a, sm, s, tmem);
+    return;
+  }
+  if (warp == kL2Warp) {
+    run_l2_prefetcher(a, sm, s);
+    return;
+  }
+  if (warp == 0) {
+    run_producer(a, sm, s);
+    return;
+  }
+  Consumer c{a, sm, s, a.scratch};
+  c.tid = threadIdx.x - 32;
+  c.w = warp - 1;
+  c.lane = threadIdx.x & 31;
+  c.nct = gridDim.x;
+  c.cta = blockIdx.x;
+  c.nb = a.nb;
+  c.tmem = tmem;
+  c.epoch_base = *reinterpret_cast<volatile uint32_t*>(&a.scratch->epoch);
+  c.run();
+}
+
+// dst tile (c, g) = [256 column groups][8 rows][8] of rows 8g.. and columns
+// 2048c.. of the row-major w[n, k]; one thread per 16-byte piece.
+__global__ void tile_weight_kernel(const uint4* __restrict__ w, uint4* __restrict__ dst, int64_t n, int64_t k) {
+  const int64_t total = n * k / 8;  // 16-byte pieces
+  const int64_t kg = k / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    // destination order: tile (c, g), column group v, row r
+    const int64_t r = i % 8, v = (i / 8) % 256, tile = i / 2048;
+    const int64_t groups = n / 8, g = tile % groups, c = tile / groups;
+    const int64_t row = 8 * g + r, colg = 256 * c + v;
+    dst[i] = w[row * kg + colg];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static constexpr int kMaxDevices = 64;
+static int g_setup_done[kMaxDevices];
+static int g_ctas[kMaxDevices];
+
+static int setup(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
+  if (!g_setup_done[dev]) {
+    const void* fn = reinterpret_cast<const void*>(decode_batch_kernel);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    if (e != cudaSuccess) return record_cuda_error(e);
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, sizeof(Smem));
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (per_sm < 1) return record_cuda_error(cudaErrorLaunchOutOfResources);
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
+    g_ctas[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
+    g_setup_done[dev] = 1;
+  }
+  *dev_out = dev;
+  return AICAS_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int validate(const AicasPhase& d) {
+  constexpr int kUnsupported = AICAS_F_X_ADD | AICAS_F_RESID_ADD | AICAS_F_STORE_X | AICAS_F_BARRIER;
+  if (d.flags & kUnsupported) return AICAS_ERR_ARG;
+  switch (d.kind) {
+    case AICAS_PH_GEMV:
+    case AICAS_PH_GATEUP:
+    case AICAS_PH_LMHEAD:
+      if (d.n < kRows || d.n % kRows != 0) return AICAS_ERR_SHAPE;
+      if (d.k < kChunk || d.k % kChunk != 0 || d.k > AICAS_MAX_K) return AICAS_ERR_SHAPE;
+      if (d.k > kChunk && !(d.flags & AICAS_F_KBLOCKED)) return AICAS_ERR_SHAPE;
+      if (!d.w || !aligned16(d.w) || !d.x || !aligned16(d.x)) return AICAS_ERR_ALIGN;
+      if ((d.flags & AICAS_F_NORM) && (d.k != kChunk || !d.norm_w || !aligned16(d.norm_w))) return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_LL_IN) && ((d.flags & AICAS_F_X_EMBED) || d.x_src < 0)) return AICAS_ERR_ARG;
+      if ((d.flags & (AICAS_F_X_EMBED | AICAS_F_RESID_EMBED)) && d.embed_rows < 1) return AICAS_ERR_ARG;
+      if (d.kind == AICAS_PH_GATEUP && (d.k != kChunk || (d.flags & (AICAS_F_RESID | AICAS_F_BIAS))))
+        return AICAS_ERR_ARG;
+      if ((d.flags & AICAS_F_RESID) && (!d.resid || !aligned16(d.resid))) return AICAS_ERR_ALIGN;
+      if ((d.flags & AICAS_F_BIAS) && !d.bias) return AICAS_ERR_ARG;
+      if (d.kind != AICAS_PH_LMHEAD) {
+        if (!(d.flags & AICAS_F_LL_OUT) || !d.out || !aligned16(d.out)) return AICAS_ERR_ARG;
+      }
+      return AICAS_OK;
+    case AICAS_PH_ATTN:
+      if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
+      if (d.max_len < 1) return AICAS_ERR_SHAPE;
+      if (d.k != (d.q_heads + 2 * d.kv_heads) * kHD || d.n != d.q_heads * kHD) return AICAS_ERR_SHAPE;
+      if ((d.flags & AICAS_F_Q_READY) || !(d.flags & AICAS_F_LL_IN) || !(d.flags & AICAS_F_LL_OUT) || d.x_src < 0)
+        return AICAS_ERR_ARG;
+      if (!d.k_cache || !d.v_cache || !aligned16(d.k_cache) || !aligned16(d.v_cache)) return AICAS_ERR_ALIGN;
+      if (!d.x || !d.out || !aligned16(d.x) || !aligned16(d.out)) return AICAS_ERR_ALIGN;
+      if (!d.norm_w || !d.norm_w2 || !aligned16(d.norm_w) || !aligned16(d.norm_w2)) return AICAS_ERR_ALIGN;
+      return AICAS_OK;
+    default:
+      return AICAS_ERR_ARG;
+  }
+}
+
+}  // namespace bat
+}  // namespace aicas
+
+using namespace aicas;
+
+extern "C" {
+
+AICAS_API size_t aicas_batch_scratch_bytes(void) { return sizeof(AicasBatchScratch); }
+
+AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n) {
+  if (!phases || n < 1) return AICAS_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const int rc = bat::validate(phases[i]);
+    if (rc) return rc;
+    if ((phases[i].flags & AICAS_F_LL_IN) && phases[i].x_src >= i) return AICAS_ERR_ARG;
+  }
+  return AICAS_OK;
+}
+
+AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
+                                     void* scratch, cudaStream_t stream) {
+  if (!device_phases || n_phases < 1 || !states || !scratch) return AICAS_ERR_ARG;
+  if (nb < 1 || nb > AICAS_MAX_BATCH) return AICAS_ERR_ARG;
+  int dev;
+  const int rc = bat::setup(&dev);
+  if (rc) return rc;
+  bat::BatchArgs a;
+  memset(&a, 0, sizeof(a));
+  a.phases = device_phases;
+  a.n_phases = n_phases;
+  a.nb = nb;
+  a.states = states;
+  a.scratch = reinterpret_cast<AicasBatchScratch*>(scratch);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(bat::g_ctas[dev]);
+  cfg.blockDim = dim3(bat::kThreads);
+  cfg.dynamicSmemBytes = sizeof(bat::Smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, bat::decode_batch_kernel, a);
+  return e == cudaSuccess ? AICAS_OK : record_cuda_error(e);
+}
+
+AICAS_API int aicas_tile_weight_f16(const void* w, void* dst, int64_t n, int64_t k, cudaStream_t stream) {
+  if (!w || !dst) return AICAS_ERR_ARG;
+  if (n < 8 || n % 8 != 0 || k < 2048 || k % 2048 != 0 || n > (int64_t)1 << 30) return AICAS_ERR_SHAPE;
+  if (!bat::aligned16(w) || !bat::aligned16(dst)) return AICAS_ERR_ALIGN;
+  const int64_t pieces = n * k / 8;
+  int64_t blocks = (pieces + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  bat::tile_weight_kernel<<<(unsigned)blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(w),
+                                                                 reinterpret_cast<uint4*>(dst), n, k);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AICAS_OK : record_cuda_error(e);
+}
+
+}  // extern "C"

@@ -1598,6 +1598,9 @@ static int cuda_fail(cudaError_t e) {
   g_last_cuda_error = (int)e;
   return AICAS_ERR_CUDA;
 }
+// Shared with the batched kernel's translation unit (hidden symbol).
+int record_cuda_error(cudaError_t e) { return cuda_fail(e); }
+
 static int g_attr_done[kMaxDevices];
 static int g_num_sms[kMaxDevices];
 static int g_cooperative = 1;
@@ -1749,6 +1752,8 @@ AICAS_API const char* aicas_error_string(int code) {
     case kErrDrainTimeout: return "device: in-flight copies did not drain in time";
     case kErrBadPhase: return "device: bad phase descriptor";
     case kErrBadInput: return "device: token id or cache position out of range";
+    case kErrInputTimeout: return "device: an input vector did not arrive in time";
+    case kErrTmemTimeout: return "device: a tensor-memory hand-off did not complete in time";
     default: return "unknown error";
   }
 }

@@ -172,6 +172,47 @@ AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, in
                                              AicasStepState* state, void* scratch, int64_t* trace,
                                              aicas_stream_t stream);
 
+/* ---- batched decode: up to AICAS_MAX_BATCH requests per launch ----------
+ *
+ * One decode step of `nb` independent requests ("streams", each with its own
+ * token, ragged cache position, KV cache slice and step state) as one
+ * persistent launch: the weights stream from HBM once per step for all
+ * streams, and every projection runs on the tensor cores (tcgen05.mma, fp16
+ * operands, fp32 accumulation in tensor memory).  The reference serves one
+ * request per engine (`GreedyDecodeEngine` rejects batch > 1,
+ * evaluation_wrapper.py:110-111, and its attention kernel reads only
+ * cache_position[0], cuda_extensions/decode_attention_v4_kernel.cu:647-900);
+ * this is the batch-8 request-parallel configuration built on the same phase
+ * programs.
+ *
+ * Phase list: the kinds of aicas_phase_program.h with these batch rules
+ * (checked by aicas_validate_batch_phases):
+ *   - activations are LL vectors [nb][len] (stream b's row starts at word
+ *     b * len), every GEMV-type phase has F_LL_OUT except the LM head, and
+ *     inputs are F_LL_IN or F_X_EMBED (stream b's token row);
+ *   - GEMV weights are in the tensor-core tile layout: n % 8 == 0,
+ *     k in {2048, 4096, 6144} (k > 2048 also F_KBLOCKED), and each 8-row x
+ *     2048-column block (32 KB, at the block address of the batch-1 layouts)
+ *     stored as [256 column groups][8 rows][8 columns];
+ *     aicas_tile_weight_f16 converts a row-major [n, k] matrix;
+ *   - attention: x is [nb][q_heads*128 + 2*kv_heads*128] (q, k, v of each
+ *     stream; phase field k = that row length), out is [nb][q_heads*128]
+ *     (phase field n), K/V caches [nb][kv_heads][max_len][128] (HF StaticLayer
+ *     of batch nb), q/k norm + MRoPE + KV write always on (no F_Q_READY);
+ *   - the LM head writes stream b's logits to states[b].logits (if set) and
+ *     advances states[b] (out_tokens, script, EOS) like the batch-1 step.
+ * A stream whose state has done_step != 0 is inactive: it is skipped (no KV
+ * write, no state change); a launch with no active stream returns at once.
+ * Scratch: aicas_batch_scratch_bytes() bytes (sizeof(AicasBatchScratch)),
+ * zero-filled once, ordered launches only (as for the batch-1 scratch). */
+AICAS_API size_t aicas_batch_scratch_bytes(void);
+AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n);
+AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
+                                     void* scratch, aicas_stream_t stream);
+/* dst = W [n, k] (row-major, device) in the tensor-core tile layout above
+ * (dst must not overlap w; n % 8 == 0, k % 2048 == 0). */
+AICAS_API int aicas_tile_weight_f16(const void* w, void* dst, int64_t n, int64_t k, aicas_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

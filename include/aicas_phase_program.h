@@ -127,6 +127,25 @@ typedef struct AicasScratch {
   uint64_t part[AICAS_MAX_KV_HEADS][AICAS_MAX_SPLITS][2][AICAS_HEAD_DIM + 1];
 } AicasScratch;
 
+// Batched decode (aicas_decode_batch_f16): up to AICAS_MAX_BATCH requests
+// ("streams") per launch.  The first eight words are laid out exactly as in
+// AicasScratch (the grid barrier, epoch, error and exit words are shared code).
+#define AICAS_MAX_BATCH 8
+
+typedef struct AicasBatchScratch {
+  uint64_t bar_count;
+  uint32_t epoch;
+  uint32_t pad0;
+  int32_t error;
+  int32_t abort;
+  uint32_t argmax_done;
+  uint32_t exit_count;
+  float am_val[AICAS_MAX_CTAS][AICAS_MAX_BATCH];   // per-CTA best logit of each stream
+  int32_t am_idx[AICAS_MAX_CTAS][AICAS_MAX_BATCH];
+  // split-KV partials per (stream, KV head) merge group (64-bit LL words, as above)
+  uint64_t part[AICAS_MAX_BATCH * AICAS_MAX_KV_HEADS][AICAS_MAX_SPLITS][2][AICAS_HEAD_DIM + 1];
+} AicasBatchScratch;
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,85 @@
+"""Host side of the batched decode step, on the CPU: the tensor-core tile
+layout of the weights, the batch rules of the C ABI's phase validation and the
+batch scratch size.  No kernel is launched."""
+import numpy as np
+import pytest
+import torch
+
+import _native
+from batch_engine import tile_weight
+
+
+def test_tile_weight_layout():
+    g = torch.Generator().manual_seed(0)
+    n, k = 24, 4096
+    w = torch.randn(n, k, generator=g).half()
+    t = tile_weight(w)
+    assert t.shape == (2, 3, 256, 8, 8)
+    flat = t.reshape(-1)
+    # element (row, col) sits in block (c, g) = (col // 2048, row // 8) at [column group][row][column]
+    for row, col in [(0, 0), (7, 2047), (8, 2048), (23, 4095), (13, 3001), (16, 9)]:
+        c, gg = col // 2048, row // 8
+        v, e, r = (col % 2048) // 8, col % 8, row % 8
+        off = ((c * (n // 8) + gg) * 256 + v) * 64 + r * 8 + e
+        assert flat[off] == w[row, col], (row, col)
+    # a block is its 8 x 2048 sub-matrix with rows interleaved per 8-column group
+    blk = t[1, 2]  # rows 16..23, columns 2048..4095
+    np.testing.assert_array_equal(blk.permute(1, 0, 2).reshape(8, 2048).numpy(), w[16:24, 2048:4096].numpy())
+    # blocks are chunk-major (the K-blocked order of the batch-1 down_proj)
+    assert torch.equal(t[0].reshape(-1), tile_weight(w[:, :2048].contiguous()).reshape(-1))
+
+
+def test_tile_weight_rejects_bad_shapes():
+    with pytest.raises(_native.AicasError):
+        tile_weight(torch.zeros(12, 2048))
+    with pytest.raises(_native.AicasError):
+        tile_weight(torch.zeros(16, 1000))
+
+
+def test_batch_scratch_bytes():
+    cta, b, heads, splits, hd = 256, 8, 8, 256, 128
+    assert _native.batch_scratch_bytes() == 32 + cta * b * 4 * 2 + b * heads * splits * 2 * (hd + 1) * 8
+
+
+def _gemv(**kw):
+    p = _native.AicasPhase()
+    p.kind, p.flags = _native.PH_GEMV, _native.F_LL_OUT
+    p.n, p.k = 2048, 2048
+    p.w = p.x = p.out = 4096
+    for key, val in kw.items():
+        setattr(p, key, val)
+    return p
+
+
+def _attn(**kw):
+    p = _native.AicasPhase()
+    p.kind, p.flags = _native.PH_ATTN, _native.F_LL_IN | _native.F_LL_OUT
+    p.kv_heads, p.q_heads, p.max_len = 8, 16, 64
+    p.k, p.n, p.x_src = 4096, 2048, 0
+    p.x = p.out = p.k_cache = p.v_cache = p.norm_w = p.norm_w2 = 4096
+    for key, val in kw.items():
+        setattr(p, key, val)
+    return p
+
+
+def _check(*phases):
+    return _native.lib().aicas_validate_batch_phases((_native.AicasPhase * len(phases))(*phases), len(phases))
+
+
+def test_batch_validation_rules():
+    ll_in = _native.F_LL_OUT | _native.F_LL_IN
+    assert _check(_gemv()) == 0
+    assert _check(_gemv(n=2044)) == 2  # rows: whole 8-row tiles
+    assert _check(_gemv(k=1024)) == 2  # columns: whole 2048-column tiles
+    assert _check(_gemv(k=6144)) == 2  # k > 2048 must be K-blocked
+    assert _check(_gemv(k=6144, flags=_native.F_LL_OUT | _native.F_KBLOCKED)) == 0
+    assert _check(_gemv(flags=0)) == 1  # outputs are LL vectors
+    assert _check(_gemv(w=4100)) == 3
+    assert _check(_gemv(flags=_native.F_LL_OUT | _native.F_BARRIER)) == 1
+    assert _check(_gemv(flags=ll_in, x_src=0)) == 1  # an LL input comes from an earlier phase
+    assert _check(_gemv(), _gemv(flags=ll_in, x_src=0)) == 0
+    assert _check(_gemv(kind=_native.PH_GATEUP, k=4096, flags=_native.F_LL_OUT | _native.F_KBLOCKED)) == 1
+    assert _check(_gemv(), _attn()) == 0
+    assert _check(_gemv(), _attn(k=2048)) == 2  # x row length = q + k + v of a stream
+    assert _check(_gemv(), _attn(flags=_native.F_LL_IN | _native.F_LL_OUT | _native.F_Q_READY)) == 1
+    assert _check(_gemv(), _attn(q_heads=8)) == 2
