@@ -290,6 +290,35 @@ class Qwen3VLBatchDecodeEngine:
             outs.append(toks)
         return outs
 
+    def decode_host(self, start: torch.Tensor, n: int, out: torch.Tensor | None = None,
+                    graph_steps: int = 32) -> torch.Tensor:
+        """Public host-buffer decode call for all max_batch streams (each
+        prefilled by add_request): `start` is a (pinned) CPU int64 tensor
+        [max_batch, 5] = (token, cache_slot, t, h, w) of every stream's first
+        step; runs `n` batched steps and returns the tokens [max_batch, n] in
+        a (pinned) CPU tensor.  The host->device copy of the inputs and the
+        device->host copy of the tokens are part of the call."""
+        B = self.max_batch
+        if out is None:
+            out = torch.empty((B, n), dtype=torch.int64, pin_memory=True)
+        if getattr(self, "_start_dev", None) is None or self._start_dev.shape[0] != B:
+            self._start_dev = torch.empty((B, 5), dtype=torch.int64, device=self.device)
+            self._first_slot = torch.tensor(self.prompt_len, dtype=torch.int64, device=self.device)
+            self._gather = torch.arange(n, dtype=torch.int64, device=self.device)
+        if self._gather.numel() != n:
+            self._gather = torch.arange(n, dtype=torch.int64, device=self.device)
+        self._first_slot.copy_(torch.tensor(self.prompt_len, dtype=torch.int64), non_blocking=True)
+        self._start_dev.copy_(start, non_blocking=True)
+        st = self.state_dev.view(torch.int64)  # [stream, state words]
+        st[:, 0:5].copy_(self._start_dev)
+        st[:, 5].copy_(st[:, 6])  # step restarts at the script end (the prompt length)
+        st[:, _DONE].fill_(0)
+        self.run(n, graph_steps)
+        idx = self._first_slot[:, None] + self._gather[None, :]
+        out.copy_(torch.gather(self.out_tokens, 1, idx), non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
     def done_step(self, b: int) -> int:
         """0 while stream b runs; s + 1 once its step s produced EOS (1 for a
         slot never started or ended by end_request)."""

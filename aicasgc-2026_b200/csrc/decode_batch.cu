@@ -78,24 +78,31 @@ constexpr int kTileBytes = kRows * kChunk * 2;  // 32 KB
 constexpr int kStages = 3;
 constexpr int kMaxC = AICAS_MAX_K / kChunk;     // K chunks of the longest reduction
 constexpr int kMmaK = 16;
-constexpr int kMmasPerTile = kChunk / kMmaK;
-constexpr int kDSlots = 16;
-constexpr int kDSlotCols = 16;
-constexpr int kTmemCols = kDSlots * kDSlotCols;
+// One tile (8 weight rows x 2048 columns) is read by the tensor core as a
+// 128 x 128 operand: row (block j, weight row r) = columns 128 j .. 128 j + 127
+// of weight row r.  The streams' operand is built the same way: row (block
+// j', stream s).  So one tile is 8 MMAs of M = 128, N = 128, K = 16, and
+// D[(j, r)][(j', s)] is the product of block j of row r with block j' of
+// stream s; the epilogue adds the 16 diagonal blocks j == j'.
+constexpr int kBlocks = 16;
+constexpr int kBlockCols = kChunk / kBlocks;     // 128
+constexpr int kKSteps = kBlockCols / kMmaK;      // 8 MMAs per tile
+constexpr int kOpSbo = kBlockCols / 8 * 128;     // 2048 bytes between 8-row core-matrix groups
+constexpr int kTmemCols = 512;
+constexpr int kDCols = kBlocks * kRows;          // 128 accumulator columns per part
+constexpr int kDSlots = 2;                       // one per epilogue warp set
+constexpr int kDSlotCols = 2 * kDCols;           // gate and up parts
+static_assert(kDSlots * kDSlotCols == kTmemCols, "two slots fill the allocation");
 constexpr int kAttnChunk = 64;
 constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kMergePer = 4;
 constexpr int kL2Ahead = 8;
-// epilogue warps: consumer warps 3 and 7 are CTA warps 4 and 8, whose TMEM
-// lane quarter (warp % 4 == 0) is lanes 0..31
-constexpr int kEpiW0 = 3, kEpiW1 = 7;
 // instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0), both
 // K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kRows >> 3) << 17) | ((uint32_t)(64 >> 4) << 24);
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
 static_assert(kAttnChunk * kHD * 2 * 2 == kTileBytes, "attention tile must fill one stage");
-static_assert(kTmemCols == 256, "TMEM allocation is a power of two >= 32 columns");
 static_assert(offsetof(AicasBatchScratch, bar_count) == offsetof(AicasScratch, bar_count) &&
                   offsetof(AicasBatchScratch, epoch) == offsetof(AicasScratch, epoch) &&
                   offsetof(AicasBatchScratch, error) == offsetof(AicasScratch, error) &&
@@ -126,6 +133,8 @@ struct __align__(128) Smem {
   AttnSmem at;
   float rope_c[kMaxB][kHD / 2], rope_s[kMaxB][kHD / 2];
   float ssq[kConsumerWarps][kMaxB];
+  // epilogue: per warp set, double-buffered, per lane quarter: [part][row][stream] sums of 4 blocks
+  float red[2][2][4][2][kRows][kMaxB];
   float best_v[2][kMaxB];
   int best_i[2][kMaxB];
   StreamIn sin[kMaxB];
@@ -313,22 +322,6 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-
 // 8 LL words {fp16 value, epoch} with two 16-byte stores (each word is
 // written whole, which is all the LL protocol needs).
 __device__ __forceinline__ void ll_store8(uint32_t* p, const float (&y)[8], uint32_t epoch16) {
@@ -425,13 +418,15 @@ __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScrat
           break;
         if (!mbar_wait_bounded(&sm.full[st], par, s, kErrFullTimeout)) break;
         tc_fence_after();
-        // descriptors advance 256 bytes (16 units of the 16-byte start address field) per K step
-        const uint64_t adesc = smem_desc_kmajor(xa0 + td.c * kTileBytes, 128, 0);
-        const uint64_t bdesc = smem_desc_kmajor(ring0 + st * kTileBytes, 128, 1024);
-        const uint32_t d = tmem + slot * kDSlotCols + td.part * kRows;
-#pragma unroll 8
-        for (int kk = 0; kk < kMmasPerTile; ++kk)
-          umma_f16(d, adesc + 16u * kk, bdesc + 16u * kk, kIdesc, (kk > 0 || td.c > 0) ? 1u : 0u);
+        // A = the weight tile, B = the streams' chunk c: 8-row core-matrix
+        // groups (blocks) 2 KB apart, K-adjacent core matrices 128 B apart;
+        // K step ks starts 256 bytes further (16 units of the address field)
+        const uint64_t adesc = smem_desc_kmajor(ring0 + st * kTileBytes, 128, kOpSbo);
+        const uint64_t bdesc = smem_desc_kmajor(xa0 + td.c * kTileBytes, 128, kOpSbo);
+        const uint32_t d = tmem + slot * kDSlotCols + td.part * kDCols;
+#pragma unroll
+        for (int ks = 0; ks < kKSteps; ++ks)
+          umma_f16(d, adesc + 16u * ks, bdesc + 16u * ks, kIdesc, (ks > 0 || td.c > 0) ? 1u : 0u);
         tcgen05_commit(&sm.empty[st]);
         if (td.group_end) {
           tcgen05_commit(&sm.dfull[slot]);
@@ -590,10 +585,18 @@ struct Consumer {
     if (rg.count > 0) build_x(d);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
-    if ((w == kEpiW0 || w == kEpiW1) && rg.count > 0) {
+    if (rg.count > 0) {
+      // Row groups alternate between two sets of 4 warps (consumer warps
+      // 0..3 and 4..7: TMEM lane quarters 1, 2, 3, 0 each) and the two
+      // accumulator slots.  Warp of quarter q reads the 32 columns of its
+      // 4 blocks j = 4q .. 4q + 3 (lane l: block 4q + l / 8, weight row
+      // l % 8), keeps its diagonal block, sums its 4 blocks by shuffles and
+      // hands the row sums to the set's leader warp through shared memory.
       const bool gu = kind == AICAS_PH_GATEUP;
-      const int b = lane;
-      const bool act = b < kMaxB && active(b);
+      const int set = w >> 2, q = (w + 1) & 3, sub = lane >> 3;
+      const bool leader = (w & 3) == 0;
+      const int b = lane;  // leader lanes: one stream each
+      const bool act = leader && b < kMaxB && active(b);
       const uint32_t ep16 = (epoch_base + (uint32_t)ph + 1) & 0xffffu;
       uint32_t* const out = reinterpret_cast<uint32_t*>(d.out);
       const __half* const bias = reinterpret_cast<const __half*>(d.bias);
@@ -608,26 +611,59 @@ struct Consumer {
       const __half* embed_row = nullptr;
       if ((flags & AICAS_F_RESID_EMBED) && act)
         embed_row = reinterpret_cast<const __half*>(d.resid) + (size_t)checked_token(b, d.embed_rows) * n;
-      const uint32_t mine = w == kEpiW1 ? 1u : 0u;
+      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + 32 * q;  // lanes 32q.., columns of blocks 4q..
       for (int gi = 0; gi < rg.count; ++gi, ++gc) {
-        if ((gc & 1u) != mine) continue;
-        const uint32_t slot = gc % kDSlots;
-        mbar_wait_bounded(&sm.dfull[slot], (gc / kDSlots) & 1u, s, kErrTmemTimeout);
+        if ((int)(gc & 1u) != set) continue;
+        const uint32_t slot = gc & 1u;  // == set
+        const int buf = (gc >> 1) & 1;
+        mbar_wait_bounded(&sm.dfull[slot], (gc >> 1) & 1u, s, kErrTmemTimeout);
         tc_fence_after();
-        uint32_t v[16];
-        if (gu) tmem_ld_x16(tmem + slot * kDSlotCols, v);
-        else tmem_ld_x8(tmem + slot * kDSlotCols, v);
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(tq + slot * kDSlotCols, v[0]);
+        if (gu) tmem_ld_32x32b_x32(tq + slot * kDSlotCols + kDCols, v[1]);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.dempty[slot]);
+#pragma unroll
+        for (int p2 = 0; p2 < 2; ++p2) {
+          if (p2 == 1 && !gu) break;
+          float part[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // the diagonal block's column of stream j
+            const uint32_t x0 = v[p2][j], x1 = v[p2][8 + j], x2 = v[p2][16 + j], x3 = v[p2][24 + j];
+            part[j] = __uint_as_float(sub == 0 ? x0 : sub == 1 ? x1 : sub == 2 ? x2 : x3);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // blocks of the quarter: lanes l, l ^ 8, l ^ 16, l ^ 24
+            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 8);
+            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 16);
+          }
+          if (lane < kRows) {  // lane r: weight row r of the group
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sm.red[set][buf][q][p2][lane][j] = part[j];
+          }
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(2 + set) : "memory");
         if (!act) continue;
+        float sum[2][8];
+#pragma unroll
+        for (int p2 = 0; p2 < 2; ++p2)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            float t = 0.f;
+            if (p2 == 0 || gu) {
+#pragma unroll
+              for (int q2 = 0; q2 < 4; ++q2) t += sm.red[set][buf][q2][p2][r][b];
+            }
+            sum[p2][r] = t;
+          }
         const int row0 = (rg.start + gi) * kRows;
         float y[8];
         if (gu) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float gq = r16(__uint_as_float(v[j])), uq = r16(__uint_as_float(v[8 + j]));
+            const float gq = r16(sum[0][j]), uq = r16(sum[1][j]);
             const float sl = r16(gq / (1.0f + expf(-gq)));
             y[j] = r16(sl * uq);
           }
@@ -647,15 +683,15 @@ struct Consumer {
               const uint4 r = ldcg_u4(rp + row0);
               const __half2* hp = reinterpret_cast<const __half2*>(&r);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                rv[2 * q] = __low2float(hp[q]);
-                rv[2 * q + 1] = __high2float(hp[q]);
+              for (int h2 = 0; h2 < 4; ++h2) {
+                rv[2 * h2] = __low2float(hp[h2]);
+                rv[2 * h2 + 1] = __high2float(hp[h2]);
               }
             }
           }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float acc = __uint_as_float(v[j]);
+            float acc = sum[0][j];
             if (flags & AICAS_F_BIAS) acc += __half2float(bias[row0 + j]);
             y[j] = r16(acc);
             if (flags & AICAS_F_RESID) y[j] = r16(rv[j] + y[j]);
@@ -665,7 +701,7 @@ struct Consumer {
           if (logits) {
             __half2 hv[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) hv[q] = __floats2half2_rn(y[2 * q], y[2 * q + 1]);
+            for (int h2 = 0; h2 < 4; ++h2) hv[h2] = __floats2half2_rn(y[2 * h2], y[2 * h2 + 1]);
             *reinterpret_cast<uint4*>(logits + row0) = *reinterpret_cast<const uint4*>(hv);
           }
           // this lane's rows ascend: strict > keeps the first max
@@ -679,8 +715,6 @@ struct Consumer {
           ll_store8(out + (size_t)b * n + row0, y, ep16);
         }
       }
-    } else if (w == kEpiW0 || w == kEpiW1) {
-      gc += rg.count;  // (rg.count == 0: nothing to consume)
     }
     if (lm) finish_argmax(best_v, best_i);
   }
@@ -689,9 +723,9 @@ struct Consumer {
   // CTAs (the last CTA to arrive reduces, one warp per stream, and advances
   // the stream's step state exactly like the batch-1 kernel).
   __device__ __forceinline__ void finish_argmax(float bv, int bi) {
-    if ((w == kEpiW0 || w == kEpiW1) && lane < kMaxB) {
-      sm.best_v[w == kEpiW1][lane] = bv;
-      sm.best_i[w == kEpiW1][lane] = bi;
+    if ((w & 3) == 0 && lane < kMaxB) {  // the two sets' leader warps
+      sm.best_v[w >> 2][lane] = bv;
+      sm.best_i[w >> 2][lane] = bi;
     }
     consumer_sync(kConsumerThreads);
     if (tid < kMaxB) {
@@ -967,12 +1001,9 @@ struct Consumer {
 #pragma unroll
           for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
         consumer_sync(kConsumerThreads);
-        const int G = b * d.kv_heads + h;  // merge group (stream, KV head)
         const int gfirst = select_i(au.pre, b) + h * cph;
         const int first_owner = owner_of(gfirst, U, na);
-        const int last_owner = owner_of(gfirst + cph - 1, U, na);
-        const int split = cta - first_owner;
-        const int nsplit = last_owner - first_owner + 1;
+        const int nsplit = owner_of(gfirst + cph - 1, U, na) - first_owner + 1;
         const int g = tid / kHD, t = tid % kHD;
         float M = -INFINITY;
 #pragma unroll
@@ -988,97 +1019,121 @@ struct Consumer {
           }
         }
         const float lse = M + logf(L), o = A / L;
-        uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
-        if (nsplit == 1) {
+        if (nsplit == 1) {  // the whole group is this CTA's
+          uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
           ll_store(out_w + (h * 2 + g) * kHD + t, o, ep & 0xffffu);
-        } else {
-          uint64_t* const hp = &bs->part[G][0][0][0];
-          constexpr int kSplitStride = 2 * (kHD + 1);
-          if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
-          ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
-          // every CTA of the group merges a 1/nsplit slice of its 256
-          // outputs over all splits in order (see the batch-1 kernel)
-          const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
-          const int npairs = q1 - q0;
-          int tpo = 16;
-          while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
-          const int nact = npairs * tpo;
-          if ((tid & ~31) < nact) {
-            const bool actv = tid < nact;
-            const int pl = tid / tpo, sub = tid % tpo;
-            const int q = q0 + (actv ? pl : 0), gq = q / kHD, tq = q % kHD;
-            const uint64_t* const base = hp + gq * (kHD + 1);
-            float mx = -INFINITY, S = 0.f, ac = 0.f;
+        } else {  // this CTA's partial as 64-bit LL words; merged below
+          uint64_t* const hp = &bs->part[b * d.kv_heads + h][cta - first_owner][0][0];
+          if (t == 0) ll64_store(hp + g * (kHD + 1), lse, ep);
+          ll64_store(hp + g * (kHD + 1) + 1 + t, o, ep);
+        }
+      }
+    }
+    // Merges, after every partial of this CTA is stored: a CTA only waits for
+    // partials that other CTAs store before they wait on anything, so the
+    // merges of consecutive groups never queue behind one another.
+    for (int u = rg.start; u < rg.start + rg.count;) {
+      const int b = au.stream_of(u);
+      const int cph = select_i(au.cph, b);
+      const int r = u - select_i(au.pre, b);
+      const int h = r / cph, j = r % cph;
+      const int seg = min(cph - j, rg.start + rg.count - u);
+      u += seg;
+      const int gfirst = select_i(au.pre, b) + h * cph;
+      const int first_owner = owner_of(gfirst, U, na);
+      const int nsplit = owner_of(gfirst + cph - 1, U, na) - first_owner + 1;
+      if (nsplit == 1) continue;
+      merge_group(d, b, h, cta - first_owner, nsplit, ep);
+    }
+  }
+
+  // Every CTA of a (stream, KV head) group merges a 1/nsplit slice of its 256
+  // outputs over all splits in order (the same order whichever CTA merges):
+  // each output by a group of tpo lanes (a power of two <= 16), lane `sub` of
+  // the group polling splits sub, sub + tpo, ... kMergePer at a time, then a
+  // fixed xor-shuffle tree combines the lanes' (max, sum, acc) triples.
+  __device__ __noinline__ void merge_group(const AicasPhase& d, int b, int h, int split, int nsplit, uint32_t ep) {
+    uint64_t* const hp = &bs->part[b * d.kv_heads + h][0][0][0];
+    uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
+    constexpr int kSplitStride = 2 * (kHD + 1);
+    const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
+    const int npairs = q1 - q0;
+    int tpo = 16;
+    while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
+    const int nact = npairs * tpo;
+    if ((tid & ~31) >= nact) return;  // warps without an active lane
+    const bool actv = tid < nact;
+    const int pl = tid / tpo, sub = tid % tpo;
+    const int q = q0 + (actv ? pl : 0), gq = q / kHD, tq = q % kHD;
+    const uint64_t* const base = hp + gq * (kHD + 1);
+    float mx = -INFINITY, S = 0.f, ac = 0.f;
 #pragma unroll 1
-            for (int b0 = actv ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
-              uint64_t lw[kMergePer], ow[kMergePer];
-              uint32_t lpend = 0u;
+    for (int b0 = actv ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
+      uint64_t lw[kMergePer], ow[kMergePer];
+      uint32_t lpend = 0u;
 #pragma unroll
-              for (int i = 0; i < kMergePer; ++i)
-                if (b0 + i * tpo < nsplit) lpend |= 1u << i;
-              uint32_t opend = lpend;
-              const uint32_t have = lpend;
-              uint64_t t0 = 0;
+      for (int i = 0; i < kMergePer; ++i)
+        if (b0 + i * tpo < nsplit) lpend |= 1u << i;
+      uint32_t opend = lpend;
+      const uint32_t have = lpend;
+      uint64_t t0 = 0;
 #pragma unroll 1
-              for (uint32_t it = 0;; ++it) {
-                const uint32_t lp = lpend, op = opend;
+      for (uint32_t it = 0;; ++it) {
+        // predicates from the round's starting masks: one round trip per round
+        const uint32_t lp = lpend, op = opend;
 #pragma unroll
-                for (int i = 0; i < kMergePer; ++i) {
-                  const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
-                  if (lp & (1u << i)) lw[i] = ll64_load(sp);
-                  if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
-                }
-                lpend = opend = 0u;
+        for (int i = 0; i < kMergePer; ++i) {
+          const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
+          if (lp & (1u << i)) lw[i] = ll64_load(sp);
+          if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
+        }
+        lpend = opend = 0u;
 #pragma unroll
-                for (int i = 0; i < kMergePer; ++i) {
-                  if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
-                  if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
-                }
-                if ((lpend | opend) == 0u) break;
-                if (it == 0) t0 = globaltimer_ns();
-                if ((it & 31u) == 31u) {
-                  if (ld_volatile_int(&s->abort)) break;
-                  if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                    raise_error(s, kErrInputTimeout);
-                    break;
-                  }
-                }
-              }
+        for (int i = 0; i < kMergePer; ++i) {
+          if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
+          if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
+        }
+        if ((lpend | opend) == 0u) break;
+        if (it == 0) t0 = globaltimer_ns();
+        if ((it & 31u) == 31u) {
+          if (ld_volatile_int(&s->abort)) break;
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            raise_error(s, kErrInputTimeout);
+            break;
+          }
+        }
+      }
 #pragma unroll
-              for (int i = 0; i < kMergePer; ++i) {
-                if (have & (1u << i)) {
-                  const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
-                  if (li > mx) {
-                    const float c = expf(mx - li);
-                    S = S * c + 1.f;
-                    ac = ac * c + oi;
-                    mx = li;
-                  } else {
-                    const float c = expf(li - mx);
-                    S += c;
-                    ac += c * oi;
-                  }
-                }
-              }
-            }
-            for (int o2 = 1; o2 < tpo; o2 <<= 1) {
-              const float m2 = __shfl_xor_sync(0xffffffffu, mx, o2);
-              const float s2 = __shfl_xor_sync(0xffffffffu, S, o2);
-              const float a2 = __shfl_xor_sync(0xffffffffu, ac, o2);
-              const float mm = fmaxf(mx, m2);
-              if (mm != -INFINITY) {
-                const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
-                const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
-                S = S * f1 + s2 * f2;
-                ac = ac * f1 + a2 * f2;
-                mx = mm;
-              }
-            }
-            if (actv && sub == 0) ll_store(out_w + (h * 2 + gq) * kHD + tq, ac / S, ep & 0xffffu);
+      for (int i = 0; i < kMergePer; ++i) {
+        if (have & (1u << i)) {
+          const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
+          if (li > mx) {
+            const float c = expf(mx - li);
+            S = S * c + 1.f;
+            ac = ac * c + oi;
+            mx = li;
+          } else {
+            const float c = expf(li - mx);
+            S += c;
+            ac += c * oi;
           }
         }
       }
     }
+    for (int o2 = 1; o2 < tpo; o2 <<= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, mx, o2);
+      const float s2 = __shfl_xor_sync(0xffffffffu, S, o2);
+      const float a2 = __shfl_xor_sync(0xffffffffu, ac, o2);
+      const float mm = fmaxf(mx, m2);
+      if (mm != -INFINITY) {
+        const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
+        const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
+        S = S * f1 + s2 * f2;
+        ac = ac * f1 + a2 * f2;
+        mx = mm;
+      }
+    }
+    if (actv && sub == 0) ll_store(out_w + (h * 2 + gq) * kHD + tq, ac / S, ep & 0xffffu);
   }
 
   __device__ __forceinline__ void run() {
@@ -1141,7 +1196,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
     }
     for (int i = 0; i < kDSlots; ++i) {
       mbar_init(&sm.dfull[i], 1);
-      mbar_init(&sm.dempty[i], 1);
+      mbar_init(&sm.dempty[i], 4);
     }
     mbar_init(&sm.xready, 1);
     mbar_init(&sm.cdone, kConsumerWarps);

@@ -348,6 +348,140 @@ def run_ours(args, rank: int, world: int):
         dist.destroy_process_group()
 
 
+BATCH_NEW = 512  # decode steps per stream per bench step (config 5)
+BATCH_CTX = (512, 4096)  # per-stream context lengths, uniform, seeded
+
+
+def batch_contexts(batch: int, rank: int) -> list[int]:
+    import numpy as np
+
+    rng = np.random.default_rng(5 + rank)
+    return [int(x) for x in rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, size=batch)]
+
+
+def run_batch(args, rank: int, world: int):
+    """BASELINE config 5 on each GPU: `--batch` ragged requests decoded
+    together by the batched kernel (one launch per step for all streams).
+    One bench STEP = BATCH_NEW batched decode steps from the prefilled
+    caches (B x BATCH_NEW tokens)."""
+    import torch
+    import torch.distributed as dist
+
+    from batch_engine import Qwen3VLBatchDecodeEngine
+    from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state, vision_grid_positions
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    B = args.batch
+    ctx = batch_contexts(B, rank)
+    shape = QWEN3VL_2B.with_layers(args.layers)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16)
+    lmax = max(ctx) + BATCH_NEW + 8
+    eng = Qwen3VLBatchDecodeEngine(st, shape, max_batch=B, max_cache_len=lmax, device=dev, max_steps=lmax)
+    firsts, pos_next = [], []
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    p0.record()
+    for b, P in enumerate(ctx):
+        pos3, _ = vision_grid_positions(P)
+        firsts.append(eng.add_request(b, synthetic_prompt(P, seed=2000 + 17 * rank + b), pos3))
+        pos_next.append([int(x) + 1 for x in pos3[:, -1]])
+    p1.record()
+    torch.cuda.synchronize(dev)
+    prefill_ms = p0.elapsed_time(p1)
+    start_state = eng.state_dev.clone()
+    graph_steps = 32
+    eng.graph(graph_steps)
+
+    def one_step():
+        eng.state_dev.copy_(start_state)
+        eng.run(BATCH_NEW, graph_steps)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize(dev)
+    eng.check_error()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        one_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    eng.check_error()
+    toks = torch.stack([eng.out_tokens[b, P:P + BATCH_NEW] for b, P in enumerate(ctx)]).cpu()
+
+    # e2e: the same steps through the host-buffer call (inputs H2D, tokens D2H)
+    start_host = torch.tensor([[f, P, *pn] for f, P, pn in zip(firsts, ctx, pos_next)],
+                              dtype=torch.int64).pin_memory()
+    out_host = torch.empty((B, BATCH_NEW), dtype=torch.int64).pin_memory()
+    eng.decode_host(start_host, BATCH_NEW, out_host, graph_steps)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        eng.decode_host(start_host, BATCH_NEW, out_host, graph_steps)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max(f0.elapsed_time(f1), 1000 * (time.perf_counter() - t0))
+    barrier()
+    e2e_ok = bool(torch.equal(out_host, toks))
+
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world)
+    tok_per_step = B * BATCH_NEW
+    value = args.steps * tok_per_step * world / (ms / 1000.0)
+    e2e_value = args.steps * tok_per_step * world / (e2e_ms / 1000.0)
+    bytes_step = sum(eng.algorithmic_bytes([P + i for P in ctx]) for i in range(BATCH_NEW))
+    per_launch_s = ms / 1000.0 / (args.steps * BATCH_NEW)
+    achieved = bytes_step / BATCH_NEW / per_launch_s / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    line = {
+        "metric": f"batch-{B} decode tok/s", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"BASELINE config 5 per GPU: Qwen3-VL-2B text decoder, 28 layers fp16, {B} ragged "
+                               f"requests (contexts {ctx}, U[512, 4096] seeded), {BATCH_NEW} greedy decode steps "
+                               f"per request per bench step, one batched launch per step, CUDA graph",
+                   "model": "Qwen3-VL-2B text decoder (random init N(0,0.02))", "batch": B,
+                   "contexts": ctx, "decode_steps_per_request": BATCH_NEW, "parallelism": f"request-dp{world}",
+                   "l2": "inputs larger than L2: 3.44 GB of weights + the requests' KV streamed per step"},
+        "us_per_batched_step": 1000.0 * ms / (args.steps * BATCH_NEW),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "decode_batch_kernel (one launch per batched step)",
+                     "algorithmic_bytes_per_launch": bytes_step / BATCH_NEW},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40 * B,
+                "d2h_bytes_per_step": 8 * B * BATCH_NEW, "tokens_match_device_run": e2e_ok},
+        "gpu_launches": args.steps * BATCH_NEW,
+        "prefill_ms_all_requests": prefill_ms,
+        "clocks": clocks,
+    }
+    if args.layers != QWEN3VL_2B.num_layers:
+        line["config"]["workload"] = f"profiling case ({args.layers} layers), not the config-5 workload"
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def write_trace_summary(eng, start_state, path):
     """One traced decode step at cache slot 1024.  Per phase kind (summed
     over layers, averaged over CTAs): time waiting for inputs, time from
@@ -390,6 +524,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--trace", default="", help="write a per-phase timeline summary (JSON) to this path")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="requests per GPU: 1 = BASELINE config 4 (the headline); 2..8 = config 5's batched "
+                         "decode of ragged requests (contexts U[512, 4096], 512 decode steps each)")
     ap.add_argument("--layers", type=int, default=28,
                     help="profiling case only: a smaller model (the headline is 28 layers)")
     args = ap.parse_args()
@@ -397,6 +534,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.batch > 1:
+        run_batch(args, rank, world)
     else:
         run_ours(args, rank, world)
 
