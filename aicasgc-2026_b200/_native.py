@@ -109,6 +109,7 @@ SIGNATURES = {
     "aicas_batch_scratch_bytes": (ctypes.c_size_t, []),
     "aicas_validate_batch_phases": (_I, [ctypes.POINTER(AicasPhase), _I]),
     "aicas_decode_batch_f16": (_I, [_P, _I, _P, _I, _P, _P]),
+    "aicas_decode_batch_trace_f16": (_I, [_P, _I, _P, _I, _P, _P, _P]),
     "aicas_tile_weight_f16": (_I, [_P, _P, _I64, _I64, _P]),
 }
 

@@ -236,6 +236,20 @@ class Qwen3VLBatchDecodeEngine:
                                                   ctypes.c_void_p(self.scratch.data_ptr()), stream)
             check(rc, "aicas_decode_batch_f16")
 
+    def launch_traced(self) -> torch.Tensor:
+        """One batched step with per-CTA per-phase %globaltimer stamps
+        (aicas_decode_batch_trace_f16); returns trace [num_ctas, n_phases, 8]
+        after synchronising."""
+        trace = torch.zeros((self.num_ctas, self.n_phases, 8), dtype=torch.int64, device=self.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        rc = self._lib.aicas_decode_batch_trace_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
+                                                    ctypes.c_void_p(self.state_dev.data_ptr()), self.max_batch,
+                                                    ctypes.c_void_p(self.scratch.data_ptr()),
+                                                    ctypes.c_void_p(trace.data_ptr()), stream)
+        check(rc, "aicas_decode_batch_trace_f16")
+        torch.cuda.synchronize(self.device)
+        return trace.cpu()
+
     def graph(self, steps: int) -> torch.cuda.CUDAGraph:
         """A CUDA graph of `steps` consecutive batched steps (captured once;
         replays advance the device step states)."""

@@ -118,12 +118,11 @@ struct StreamIn {
 };
 
 struct AttnSmem {
-  float q[2][kHD];
   float kf[kHD], vf[kHD];
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
-  float sc[kConsumerWarps][2 * kPosPerWarp];
+  __align__(16) __half qh[2][kHD];  // the segment's queries as fp16 (their values are fp16-rounded)
   __half nw[2 * kHD];  // q_norm, k_norm weights of the running phase
 };
 
@@ -157,7 +156,18 @@ struct BatchArgs {
   int nb;
   AicasStepState* states;
   AicasBatchScratch* scratch;
+  int64_t* trace;  // traced variant: [grid][n_phases][kTraceFields]
 };
+
+// consumer: phase start, inputs ready, phase end; MMA warp: operand ready,
+// last MMA of the phase issued; row groups (or attention units) of the CTA;
+// ns consumer warp 0 waited for attention tiles; ns the producer waited for
+// free ring stages while issuing the phase's tiles
+constexpr int kTraceFields = 8;
+
+__device__ __forceinline__ void trace_put(const BatchArgs& a, int ph, int field, int64_t v) {
+  a.trace[((size_t)blockIdx.x * a.n_phases + ph) * kTraceFields + field] = v;
+}
 
 struct Range {
   int start, count;
@@ -339,22 +349,33 @@ __device__ __forceinline__ void ll_store8(uint32_t* p, const float (&y)[8], uint
 // ---------------------------------------------------------------------------
 // Producer, L2 prefetch, MMA issuer
 // ---------------------------------------------------------------------------
+template <bool kTrace>
 __device__ __forceinline__ void run_producer(const BatchArgs& a, Smem& sm, AicasScratch* s) {
   if ((threadIdx.x & 31) != 0) return;
   const uint64_t pol = l2_evict_first_policy();
   Cursor cur{a.phases, a.n_phases, (int)gridDim.x, (int)blockIdx.x, a.nb, sm.sin};
   TileDesc td;
   uint32_t it = 0;
+  int tph = 0;
+  uint64_t waited = 0;
   while (cur.next(td)) {
     const int st = it % kStages;
+    if (kTrace && cur.ph != tph) {
+      trace_put(a, tph, 7, (int64_t)waited);
+      waited = 0;
+      tph = cur.ph;
+    }
+    const uint64_t w0 = kTrace ? globaltimer_ns() : 0;
     if (it >= (uint32_t)kStages && !mbar_wait_bounded(&sm.empty[st], ((it / kStages) - 1) & 1u, s, kErrEmptyTimeout))
       break;
+    if (kTrace) waited += globaltimer_ns() - w0;
     mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
     for (int i = 0; i < td.pieces; ++i)
       bulk_g2s(sm.ring[st] + i * (kTileBytes / 2), td.src + i * td.src_stride, td.bytes, &sm.full[st], pol);
     ++it;
     *reinterpret_cast<volatile uint32_t*>(&sm.ring_it) = it;
   }
+  if (kTrace) trace_put(a, tph, 7, (int64_t)waited);
   // every issued copy lands before the CTA may exit
   const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0;
   for (uint32_t k = first; k < it; ++k) {
@@ -394,6 +415,7 @@ __device__ __forceinline__ void run_l2_prefetcher(const BatchArgs& a, Smem& sm, 
 // issue the tile's 128 MMAs, commit the stage (and the slot at the group's
 // last tile).  Attention tiles: pass the consumers' in-place release on to
 // the producer.
+template <bool kTrace>
 __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScratch* s, uint32_t tmem) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
@@ -411,6 +433,7 @@ __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScrat
           if (!mbar_wait_bounded(&sm.xready, xph & 1u, s, kErrTmemTimeout)) break;
           ++xph;
           x_phase = cur.ph;
+          if (kTrace) trace_put(a, cur.ph, 3, (int64_t)globaltimer_ns());
         }
         const uint32_t slot = gc % kDSlots;
         if (td.c == 0 && td.part == 0 && gc >= (uint32_t)kDSlots &&
@@ -427,6 +450,7 @@ __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScrat
 #pragma unroll
         for (int ks = 0; ks < kKSteps; ++ks)
           umma_f16(d, adesc + 16u * ks, bdesc + 16u * ks, kIdesc, (ks > 0 || td.c > 0) ? 1u : 0u);
+        if (kTrace) trace_put(a, cur.ph, 4, (int64_t)globaltimer_ns());
         tcgen05_commit(&sm.empty[st]);
         if (td.group_end) {
           tcgen05_commit(&sm.dfull[slot]);
@@ -464,6 +488,7 @@ __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScrat
 // ---------------------------------------------------------------------------
 // Consumers (warps 1..8)
 // ---------------------------------------------------------------------------
+template <bool kTrace>
 struct Consumer {
   const BatchArgs& a;
   Smem& sm;
@@ -574,12 +599,14 @@ struct Consumer {
     fence_proxy_async_smem();
     consumer_sync(kConsumerThreads);
     if (tid == 0) mbar_arrive(&sm.xready);
+    if (kTrace && tid == 0) trace_put(a, ph, 1, (int64_t)globaltimer_ns());
   }
 
   __device__ __forceinline__ void run_gemv(const AicasPhase& d) {
     const int n = d.n, flags = d.flags, kind = d.kind;
     const Range rg = split_range(n / kRows, nct, cta, d.rot);
     const bool lm = kind == AICAS_PH_LMHEAD;
+    if (kTrace && tid == 0) trace_put(a, ph, 5, rg.count);
     // the MMA warp consumes these tiles; the ring position moves past them
     rit += rg.count * (kind == AICAS_PH_GATEUP ? 2 : d.k / kChunk);
     if (rg.count > 0) build_x(d);
@@ -815,29 +842,6 @@ struct Consumer {
     }
   }
 
-  // Reduce-scatter of 16 per-lane partial sums across the warp: lane l ends
-  // with the warp total of value index idx (see the batch-1 kernel).
-  __device__ __forceinline__ float reduce_scatter16(float (&a)[16], int& idx) {
-    int base = 0;
-    int o = 16;
-#pragma unroll
-    for (int n = 16; n > 1; n >>= 1, o >>= 1) {
-      const bool hi = lane & o;
-#pragma unroll
-      for (int i = 0; i < n / 2; ++i) {
-        const float send = hi ? a[i] : a[i + n / 2];
-        const float keep = hi ? a[i + n / 2] : a[i];
-        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-      }
-      base += hi ? n / 2 : 0;
-    }
-    float t = a[0];
-#pragma unroll
-    for (; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    idx = base;
-    return t;
-  }
-
   __device__ __forceinline__ void run_attention(const AicasPhase& d) {
     AttnSmem& at = sm.at;
     AttnUnits au;
@@ -850,6 +854,8 @@ struct Consumer {
     if (U == 0) return;
     const int na = attn_ctas(U, nct);
     const Range rg = cta < na ? split_range(U, na, cta, 0) : Range{0, 0};
+    if (kTrace && tid == 0) trace_put(a, ph, 5, rg.count);
+    uint64_t tile_wait = 0, seg_ns = 0;
     const uint32_t* qkv_w = reinterpret_cast<const uint32_t*>(d.x);
     const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
     __half* kc = reinterpret_cast<__half*>(d.k_cache);
@@ -858,7 +864,7 @@ struct Consumer {
     const float scale = d.scale;
     const uint32_t ep = epoch_base + (uint32_t)ph + 1;
     float m[2], l[2], acc[2][4];
-    float qreg[2][4];
+    const int pi = lane >> 2, qc = lane & 3;  // score lanes: position within the warp's 8, dim quarter
     int cur_b = -1;
     float cs[4], sn[4];
     for (int u = rg.start; u < rg.start + rg.count; ++u) {
@@ -878,6 +884,7 @@ struct Consumer {
           sn[e] = sm.rope_s[b][(lane * 4 + e) % (kHD / 2)];
         }
       }
+      const uint64_t ss0 = kTrace ? globaltimer_ns() : 0;
       if (seg_start) {
         const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
         const bool has_pos = jpos >= j && jpos <= last_j;
@@ -888,8 +895,8 @@ struct Consumer {
           const __half2* hp = reinterpret_cast<const __half2*>(&raw);
           float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
           norm_rope_head(v, at.nw, d.eps, cs, sn);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) at.q[w][lane * 4 + e] = v[e];
+          *reinterpret_cast<__half2*>(&at.qh[w][lane * 4]) = __floats2half2_rn(v[0], v[1]);
+          *reinterpret_cast<__half2*>(&at.qh[w][lane * 4 + 2]) = __floats2half2_rn(v[2], v[3]);
         } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
           const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
           const uint2 raw = ll_poll4(xw, off, x_epoch, s);
@@ -904,68 +911,89 @@ struct Consumer {
           *reinterpret_cast<uint2*>(cache + (head_off + pos) * kHD + lane * 4) = *reinterpret_cast<uint2*>(o);
         }
         consumer_sync(kConsumerThreads);
+        if (kTrace && tid == 0 && u == rg.start) trace_put(a, ph, 1, (int64_t)globaltimer_ns());
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) qreg[g][e] = at.q[g][lane * 4 + e];
           m[g] = -INFINITY;
           l[g] = 0.f;
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
         }
       }
+      if (kTrace && seg_start) seg_ns += globaltimer_ns() - ss0;
       const int st = rit % kStages;
-      mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
+      if (kTrace && tid == 0) {
+        const uint64_t w0 = globaltimer_ns();
+        mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
+        tile_wait += globaltimer_ns() - w0;
+      } else {
+        mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
+      }
       const int p0 = j * kAttnChunk;
       const uint8_t* kt = sm.ring[st];
       const uint8_t* vt = sm.ring[st] + kTileBytes / 2;
-      float kv[kPosPerWarp][4];
+      // Scores: lane (position pi, dim quarter c) dots its position's dims
+      // c*32 .. c*32+31 with both queries (exact fp16 products, fp32 sums),
+      // reading the K row's 16-byte pieces in an order rotated by pi (no
+      // shared-memory bank conflicts); two shuffles finish each score.
+      const int pq = p0 + w * kPosPerWarp + pi;
+      float sg[2] = {0.f, 0.f};
+      if (pq == pos) {  // this step's k: from at.kf (the tile may predate its write)
 #pragma unroll
-      for (int i = 0; i < kPosPerWarp; ++i) {
-        const int p = p0 + w * kPosPerWarp + i;
-        if (p == pos) {
+        for (int jj = 0; jj < 4; ++jj) {
+          const float* kf = at.kf + qc * 32 + 8 * ((jj + pi) & 3);
+          uint4 kv;
+          __half2* kh = reinterpret_cast<__half2*>(&kv);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) kv[i][e] = at.kf[lane * 4 + e];
-        } else {
-          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
-          const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-          kv[i][0] = __low2float(kh[0]);
-          kv[i][1] = __high2float(kh[0]);
-          kv[i][2] = __low2float(kh[1]);
-          kv[i][3] = __high2float(kh[1]);
+          for (int e = 0; e < 4; ++e) kh[e] = __floats2half2_rn(kf[2 * e], kf[2 * e + 1]);
+          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
+          sg[0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[0]);
+          sg[1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[1]);
+        }
+      } else {
+        const uint8_t* krow = kt + (w * kPosPerWarp + pi) * (kHD * 2) + qc * 64;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(krow + 16 * ((jj + pi) & 3));
+          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
+          sg[0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[0]);
+          sg[1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[1]);
         }
       }
-      float part[2 * kPosPerWarp];
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-#pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i)
-          part[g * kPosPerWarp + i] =
-              qreg[g][0] * kv[i][0] + qreg[g][1] * kv[i][1] + qreg[g][2] * kv[i][2] + qreg[g][3] * kv[i][3];
-      int vidx;
-      const float tot = reduce_scatter16(part, vidx);
-      if ((lane & 1) == 0) at.sc[w][vidx] = tot;
-      __syncwarp();
-      const int pw = p0 + w * kPosPerWarp;
+      float pr[2];
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
-        float cmax = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i)
-          if (pw + i < valid) cmax = fmaxf(cmax, at.sc[w][g * kPosPerWarp + i] * scale);
-        const float mn = fmaxf(m[g], cmax);
-        if (mn == -INFINITY) continue;
+        sg[g] += __shfl_xor_sync(0xffffffffu, sg[g], 1);
+        sg[g] += __shfl_xor_sync(0xffffffffu, sg[g], 2);
+        const float x = pq < valid ? sg[g] * scale : -INFINITY;
+        float cm = x;  // the warp's 8 positions: lanes differing in bits 2..4
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+        const float mn = fmaxf(m[g], cm);
+        pr[g] = 0.f;
+        if (mn == -INFINITY) continue;  // (warp-uniform) no valid position yet
+        pr[g] = x == -INFINITY ? 0.f : expf(x - mn);
+        float ps = pr[g];
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
         const float corr = expf(m[g] - mn);
-        l[g] *= corr;
+        l[g] = l[g] * corr + ps;
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
         m[g] = mn;
       }
-#pragma unroll 1
-      for (int i = 0; i < kPosPerWarp && pw + i < valid; ++i) {
-        const int p = pw + i;
+      // P V: lane l accumulates dims 4l .. 4l+3 of both heads; position i's
+      // probabilities come from its lane 4 i
+      const int pw = p0 + w * kPosPerWarp;
+#pragma unroll
+      for (int i = 0; i < kPosPerWarp; ++i) {
+        if (pw + i >= valid) break;
+        const float pr0 = __shfl_sync(0xffffffffu, pr[0], 4 * i);
+        const float pr1 = __shfl_sync(0xffffffffu, pr[1], 4 * i);
         float vv[4];
-        if (p == pos) {
+        if (pw + i == pos) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
         } else {
@@ -976,10 +1004,6 @@ struct Consumer {
           vv[2] = __low2float(vh[1]);
           vv[3] = __high2float(vh[1]);
         }
-        const float pr0 = expf(at.sc[w][i] * scale - m[0]);
-        const float pr1 = expf(at.sc[w][kPosPerWarp + i] * scale - m[1]);
-        l[0] += pr0;
-        l[1] += pr1;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           acc[0][e] += pr0 * vv[e];
@@ -1028,6 +1052,11 @@ struct Consumer {
           ll64_store(hp + g * (kHD + 1) + 1 + t, o, ep);
         }
       }
+    }
+    if (kTrace && tid == 0) {
+      trace_put(a, ph, 6, (int64_t)tile_wait);
+      trace_put(a, ph, 3, (int64_t)globaltimer_ns());  // units done (merges follow)
+      trace_put(a, ph, 4, (int64_t)seg_ns);             // ns in segment starts (query loads)
     }
     // Merges, after every partial of this CTA is stored: a CTA only waits for
     // partials that other CTAs store before they wait on anything, so the
@@ -1141,6 +1170,7 @@ struct Consumer {
     for (ph = 0; ph < a.n_phases; ++ph) {
       const AicasPhase& d = a.phases[ph];
       consumer_sync(kConsumerThreads);  // every warp is done with the previous phase's shared buffers
+      if (kTrace && tid == 0) trace_put(a, ph, 0, (int64_t)globaltimer_ns());
       if (d.kind == AICAS_PH_ATTN) {
         if (tid < 2 * kHD / 8) {
           const __half* src = reinterpret_cast<const __half*>(tid < kHD / 8 ? d.norm_w : d.norm_w2);
@@ -1153,6 +1183,7 @@ struct Consumer {
       } else {
         run_gemv(d);
       }
+      if (kTrace && tid == 0) trace_put(a, ph, 2, (int64_t)globaltimer_ns());
     }
     tc_fence_before();
     __syncwarp();
@@ -1169,6 +1200,7 @@ struct Consumer {
   }
 };
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_constant__ BatchArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1217,7 +1249,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&sm.tmem_base);
   if (warp == kMmaWarp) {
-    run_mma(a, sm, s, tmem);
+    run_mma<kTrace>(a, sm, s, tmem);
     return;
   }
   if (warp == kL2Warp) {
@@ -1225,10 +1257,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
     return;
   }
   if (warp == 0) {
-    run_producer(a, sm, s);
+    run_producer<kTrace>(a, sm, s);
     return;
   }
-  Consumer c{a, sm, s, a.scratch};
+  Consumer<kTrace> c{a, sm, s, a.scratch};
   c.tid = threadIdx.x - 32;
   c.w = warp - 1;
   c.lane = threadIdx.x & 31;
@@ -1266,13 +1298,16 @@ static int setup(int* dev_out) {
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
   if (!g_setup_done[dev]) {
-    const void* fn = reinterpret_cast<const void*>(decode_batch_kernel);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
-    if (e != cudaSuccess) return record_cuda_error(e);
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, sizeof(Smem));
-    if (e != cudaSuccess) return record_cuda_error(e);
-    if (per_sm < 1) return record_cuda_error(cudaErrorLaunchOutOfResources);
+    for (int v = 0; v < 2; ++v) {
+      const void* fn = v ? reinterpret_cast<const void*>(decode_batch_kernel<true>)
+                         : reinterpret_cast<const void*>(decode_batch_kernel<false>);
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+      if (e != cudaSuccess) return record_cuda_error(e);
+      int per_sm = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, sizeof(Smem));
+      if (e != cudaSuccess) return record_cuda_error(e);
+      if (per_sm < 1) return record_cuda_error(cudaErrorLaunchOutOfResources);
+    }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
     g_ctas[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
@@ -1340,8 +1375,8 @@ AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n) {
   return AICAS_OK;
 }
 
-AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
-                                     void* scratch, cudaStream_t stream) {
+static int launch_batch(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
+                        void* scratch, int64_t* trace, cudaStream_t stream) {
   if (!device_phases || n_phases < 1 || !states || !scratch) return AICAS_ERR_ARG;
   if (nb < 1 || nb > AICAS_MAX_BATCH) return AICAS_ERR_ARG;
   int dev;
@@ -1354,6 +1389,7 @@ AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phas
   a.nb = nb;
   a.states = states;
   a.scratch = reinterpret_cast<AicasBatchScratch*>(scratch);
+  a.trace = trace;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(bat::g_ctas[dev]);
   cfg.blockDim = dim3(bat::kThreads);
@@ -1364,8 +1400,20 @@ AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phas
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, bat::decode_batch_kernel, a);
+  const cudaError_t e = trace ? cudaLaunchKernelEx(&cfg, bat::decode_batch_kernel<true>, a)
+                              : cudaLaunchKernelEx(&cfg, bat::decode_batch_kernel<false>, a);
   return e == cudaSuccess ? AICAS_OK : record_cuda_error(e);
+}
+
+AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
+                                     void* scratch, cudaStream_t stream) {
+  return launch_batch(device_phases, n_phases, states, nb, scratch, nullptr, stream);
+}
+
+AICAS_API int aicas_decode_batch_trace_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states,
+                                           int nb, void* scratch, int64_t* trace, cudaStream_t stream) {
+  if (!trace) return AICAS_ERR_ARG;
+  return launch_batch(device_phases, n_phases, states, nb, scratch, trace, stream);
 }
 
 AICAS_API int aicas_tile_weight_f16(const void* w, void* dst, int64_t n, int64_t k, cudaStream_t stream) {

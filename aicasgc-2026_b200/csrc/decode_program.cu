@@ -1155,6 +1155,104 @@ struct Consumer {
     }
   }
 
+  // Every CTA of a KV head merges a 1/nsplit slice of the head's 256
+  // outputs, one output per group of tpo lanes (a power of two <= 16, as
+  // many as the CTA's threads allow): lane `sub` of the group takes splits
+  // sub, sub + tpo, ... in order (the same order whichever CTA merges),
+  // polling up to kMergePer of them per round, then the group combines its
+  // (max, sum, acc) triples with a fixed xor-shuffle tree.
+  __device__ __forceinline__ void merge_head(const AicasPhase& d, int h, int split, int nsplit, uint32_t ep) {
+    uint64_t* const hp = &s->part[h][0][0][0];
+    constexpr int kSplitStride = 2 * (kHD + 1);
+    uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out);
+    __half* const out_h = reinterpret_cast<__half*>(d.out);
+    const bool ll_out = d.flags & AICAS_F_LL_OUT;
+    const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
+    const int npairs = q1 - q0;
+    int tpo = 16;
+    while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
+    const int nact = npairs * tpo;
+    if ((tid & ~31) < nact) {  // warps holding at least one active lane
+      const bool act = tid < nact;
+      const int pl = tid / tpo, sub = tid % tpo;
+      const int q = q0 + (act ? pl : 0), gq = q / kHD, tq = q % kHD;
+      const uint64_t* const base = hp + gq * (kHD + 1);
+      float mx = -INFINITY, S = 0.f, acc = 0.f;
+#pragma unroll 1
+      for (int b0 = act ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
+        uint64_t lw[kMergePer], ow[kMergePer];
+        uint32_t lpend = 0u;
+#pragma unroll
+        for (int i = 0; i < kMergePer; ++i)
+          if (b0 + i * tpo < nsplit) lpend |= 1u << i;
+        uint32_t opend = lpend;
+        const uint32_t have = lpend;
+        uint64_t t0 = 0;
+#pragma unroll 1
+        for (uint32_t it = 0;; ++it) {
+          // predicates from the round's starting masks: no load waits
+          // for another load's result, so a round is one round trip
+          const uint32_t lp = lpend, op = opend;
+#pragma unroll
+          for (int i = 0; i < kMergePer; ++i) {
+            const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
+            if (lp & (1u << i)) lw[i] = ll64_load(sp);
+            if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
+          }
+          lpend = opend = 0u;
+#pragma unroll
+          for (int i = 0; i < kMergePer; ++i) {
+            if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
+            if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
+          }
+          if ((lpend | opend) == 0u) break;
+          if (it == 0) t0 = globaltimer_ns();
+          if ((it & 31u) == 31u) {
+            if (ld_volatile_int(&s->abort)) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              raise_error(s, kErrInputTimeout);
+              break;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kMergePer; ++i) {
+          if (have & (1u << i)) {
+            const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
+            if (li > mx) {
+              const float c = expf(mx - li);
+              S = S * c + 1.f;
+              acc = acc * c + oi;
+              mx = li;
+            } else {
+              const float c = expf(li - mx);
+              S += c;
+              acc += c * oi;
+            }
+          }
+        }
+      }
+      for (int o = 1; o < tpo; o <<= 1) {  // tpo is the same in every lane
+        const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
+        const float a2 = __shfl_xor_sync(0xffffffffu, acc, o);
+        const float mm = fmaxf(mx, m2);
+        if (mm != -INFINITY) {
+          const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
+          const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
+          S = S * f1 + s2 * f2;
+          acc = acc * f1 + a2 * f2;
+          mx = mm;
+        }
+      }
+      if (act && sub == 0) {
+        const int oidx = (h * 2 + gq) * kHD + tq;
+        if (ll_out) ll_store(out_w + oidx, acc / S, ep & 0xffffu);
+        else out_h[oidx] = __float2half_rn(acc / S);
+      }
+    }
+  }
+
   __device__ __forceinline__ void run_attention(const AicasPhase& d) {
     AttnSmem& at = sm.at;
     const bool q_ready = d.flags & AICAS_F_Q_READY;
@@ -1364,105 +1462,17 @@ struct Consumer {
           constexpr int kSplitStride = 2 * (kHD + 1);
           if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
           ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
-          // 2) every CTA of the head merges a 1/nsplit slice of its 256
-          // outputs, one thread per output, over splits 0..nsplit-1 in order
-          // (the same order whichever CTA merges).  A CTA only waits for
-          // partials of its current head, which every owner stores before it
-          // waits on anything later, so the waits cannot form a cycle.
-          // Each output is merged by a group of tpo lanes (a power of two
-          // <= 16, as many as the CTA's threads allow): lane `sub` of the
-          // group takes splits sub, sub + tpo, ... in order, polling up to
-          // kMergePer of them per round, then the group combines its
-          // (max, sum, acc) triples with a fixed xor-shuffle tree.
-          const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
-          const int npairs = q1 - q0;
-          int tpo = 16;
-          while (tpo > 1 && tpo * npairs > kConsumerThreads) tpo >>= 1;
-          const int nact = npairs * tpo;
-          if ((tid & ~31) < nact) {  // warps holding at least one active lane
-            const bool act = tid < nact;
-            const int pl = tid / tpo, sub = tid % tpo;
-            const int q = q0 + (act ? pl : 0), gq = q / kHD, tq = q % kHD;
-            const uint64_t* const base = hp + gq * (kHD + 1);
-            float mx = -INFINITY, S = 0.f, acc = 0.f;
-#pragma unroll 1
-            for (int b0 = act ? sub : nsplit; b0 < nsplit; b0 += tpo * kMergePer) {
-              uint64_t lw[kMergePer], ow[kMergePer];
-              uint32_t lpend = 0u;
-#pragma unroll
-              for (int i = 0; i < kMergePer; ++i)
-                if (b0 + i * tpo < nsplit) lpend |= 1u << i;
-              uint32_t opend = lpend;
-              const uint32_t have = lpend;
-              uint64_t t0 = 0;
-#pragma unroll 1
-              for (uint32_t it = 0;; ++it) {
-                // predicates from the round's starting masks: no load waits
-                // for another load's result, so a round is one round trip
-                const uint32_t lp = lpend, op = opend;
-#pragma unroll
-                for (int i = 0; i < kMergePer; ++i) {
-                  const uint64_t* sp = base + (b0 + i * tpo) * kSplitStride;
-                  if (lp & (1u << i)) lw[i] = ll64_load(sp);
-                  if (op & (1u << i)) ow[i] = ll64_load(sp + 1 + tq);
-                }
-                lpend = opend = 0u;
-#pragma unroll
-                for (int i = 0; i < kMergePer; ++i) {
-                  if ((lp & (1u << i)) && ll64_epoch(lw[i]) != ep) lpend |= 1u << i;
-                  if ((op & (1u << i)) && ll64_epoch(ow[i]) != ep) opend |= 1u << i;
-                }
-                if ((lpend | opend) == 0u) break;
-                if (it == 0) t0 = globaltimer_ns();
-                if ((it & 31u) == 31u) {
-                  if (ld_volatile_int(&s->abort)) break;
-                  if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                    raise_error(s, kErrInputTimeout);
-                    break;
-                  }
-                }
-              }
-#pragma unroll
-              for (int i = 0; i < kMergePer; ++i) {
-                if (have & (1u << i)) {
-                  const float li = ll64_value(lw[i]), oi = ll64_value(ow[i]);
-                  if (li > mx) {
-                    const float c = expf(mx - li);
-                    S = S * c + 1.f;
-                    acc = acc * c + oi;
-                    mx = li;
-                  } else {
-                    const float c = expf(li - mx);
-                    S += c;
-                    acc += c * oi;
-                  }
-                }
-              }
-            }
-            for (int o = 1; o < tpo; o <<= 1) {  // tpo is the same in every lane
-              const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
-              const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
-              const float a2 = __shfl_xor_sync(0xffffffffu, acc, o);
-              const float mm = fmaxf(mx, m2);
-              if (mm != -INFINITY) {
-                const float f1 = mx == -INFINITY ? 0.f : expf(mx - mm);
-                const float f2 = m2 == -INFINITY ? 0.f : expf(m2 - mm);
-                S = S * f1 + s2 * f2;
-                acc = acc * f1 + a2 * f2;
-                mx = mm;
-              }
-            }
-            if (act && sub == 0) {
-              const int oidx = (h * 2 + gq) * kHD + tq;
-              if (ll_out) ll_store(out_w + oidx, acc / S, ep & 0xffffu);
-              else out_h[oidx] = __float2half_rn(acc / S);
-            }
-          }
+          // 2) every CTA of the head merges its slice of the head's outputs
+          // over all splits (merge_head).  A CTA only waits for partials of
+          // its current head, which every owner stores before it waits on
+          // anything later, so the waits cannot form a cycle.
+          merge_head(d, h, split, nsplit, ep);
           stamp_field(7);
         }
       }
     }
   }
+
 
   // Interleaved-MRoPE cos/sin of the step's position, once per launch
   // (every attention phase of the step uses the same table):

@@ -209,6 +209,18 @@ AICAS_API size_t aicas_batch_scratch_bytes(void);
 AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n);
 AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
                                      void* scratch, aicas_stream_t stream);
+/* Profiling variant of aicas_decode_batch_f16: also writes, per CTA and
+ * phase, trace[cta][phase][8] (int64, aicas_num_ctas() * n_phases * 8
+ * entries): the %globaltimer (ns) when the consumers started the phase, when
+ * its inputs were ready (GEMV: the streams' operand built; attention: the
+ * first segment's queries loaded), when the phase ended; when the MMA warp
+ * saw the operand ready and when it issued the phase's last MMA (GEMV
+ * phases; attention: when the CTA's units were done, before its merges, and
+ * the ns spent loading the segments' queries); the CTA's row groups or attention units in the phase; the ns one
+ * consumer warp waited for attention tiles to land; and the ns the producer
+ * waited for free ring stages while issuing the phase's tiles. */
+AICAS_API int aicas_decode_batch_trace_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states,
+                                           int nb, void* scratch, int64_t* trace, aicas_stream_t stream);
 /* dst = W [n, k] (row-major, device) in the tensor-core tile layout above
  * (dst must not overlap w; n % 8 == 0, k % 2048 == 0). */
 AICAS_API int aicas_tile_weight_f16(const void* w, void* dst, int64_t n, int64_t k, aicas_stream_t stream);
