@@ -349,6 +349,11 @@ def run_ours(args, rank: int, world: int):
 
 
 BATCH_NEW = 512  # decode steps per stream per bench step (config 5)
+# DRAM bytes per algorithmic byte of decode_batch_kernel, from one `ncu --set
+# full` capture of the 2-layer batch-8 profiling case (bench.py --batch 8
+# --layers 2; summarised under profiles/): (983.835392e6 + 21.94944e6) /
+# 981263360 (reads 0.3 % above the algorithmic bytes, the rest writes).
+BATCH_DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0249897
 BATCH_CTX = (512, 4096)  # per-stream context lengths, uniform, seeded
 
 
@@ -465,7 +470,11 @@ def run_batch(args, rank: int, world: int):
                    "l2": "inputs larger than L2: 3.44 GB of weights + the requests' KV streamed per step"},
         "us_per_batched_step": 1000.0 * ms / (args.steps * BATCH_NEW),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind,
+                     "traffic": BATCH_DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_step / BATCH_NEW,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 2-layer batch-8 "
+                                       "launch (983.8 MB + 21.9 MB vs 981.3 MB algorithmic), scaled to this "
+                                       "launch by algorithmic bytes",
                      "kernel": "decode_batch_kernel (one launch per batched step)",
                      "algorithmic_bytes_per_launch": bytes_step / BATCH_NEW},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40 * B,
