@@ -94,7 +94,6 @@ constexpr int kDSlots = 2;                       // one per epilogue warp set
 constexpr int kDSlotCols = 2 * kDCols;           // gate and up parts
 static_assert(kDSlots * kDSlotCols == kTmemCols, "two slots fill the allocation");
 constexpr int kAttnChunk = 64;
-constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kMergePer = 4;
 constexpr int kL2Ahead = 8;
@@ -123,6 +122,7 @@ struct AttnSmem {
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
   __align__(16) __half qh[2][kHD];  // the segment's queries as fp16 (their values are fp16-rounded)
+  float2 sc[kConsumerWarps][16];     // per warp: the probabilities (both heads) of its 16 positions
   __half nw[2 * kHD];  // q_norm, k_norm weights of the running phase
 };
 
@@ -842,6 +842,106 @@ struct Consumer {
     }
   }
 
+  // One warp's 16 positions p0 .. p0 + 15 of a 64-slot K/V tile (ring stage
+  // `tile`): online-softmax update of (m, l, acc) for both query heads.
+  // Scores: lane (pi, qc) dots positions p0 + pi and p0 + 8 + pi over dims
+  // qc*32 .. qc*32+31 (exact fp16 products, fp32 sums; K rows read in an
+  // order rotated by pi, free of bank conflicts); two shuffles finish each.
+  // P V: lane l accumulates dims 4l .. 4l+3; the probabilities pass through
+  // the warp's shared-memory row.  Slot `pos` (this step's k / v) comes from
+  // at.kf / at.vf: the tile may have been loaded before it was written.
+  __device__ __forceinline__ void attend_tile(const uint8_t* tile, int p0, int pos, int valid, float scale, int pi,
+                                              int qc, float (&m)[2], float (&l)[2], float (&acc)[2][4]) {
+    AttnSmem& at = sm.at;
+    const int row0 = p0 % kAttnChunk;  // the warp's first row in the tile
+    float sg[2][2];
+#pragma unroll
+    for (int a2 = 0; a2 < 2; ++a2) {
+      sg[a2][0] = sg[a2][1] = 0.f;
+      const int prow = row0 + 8 * a2 + pi;
+      if (p0 + 8 * a2 + pi == pos) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
+          uint4 kv;
+          __half2* kh = reinterpret_cast<__half2*>(&kv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kh[e] = __floats2half2_rn(at.kf[qo + 2 * e], at.kf[qo + 2 * e + 1]);
+          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
+          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
+        }
+      } else {
+        const uint8_t* krow = tile + prow * (kHD * 2) + qc * 64;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int jr = (jj + pi) & 3;
+          const uint4 kv = *reinterpret_cast<const uint4*>(krow + 16 * jr);
+          const int qo = qc * 32 + 8 * jr;
+          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
+          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
+        }
+      }
+    }
+    float pr[2][2];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      float x[2];
+#pragma unroll
+      for (int a2 = 0; a2 < 2; ++a2) {
+        float v = sg[a2][g];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        x[a2] = p0 + 8 * a2 + pi < valid ? v * scale : -INFINITY;
+      }
+      float cm = fmaxf(x[0], x[1]);  // the warp's 16 positions: pairs, then lanes differing in bits 2..4
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+      const float mn = fmaxf(m[g], cm);
+      pr[0][g] = pr[1][g] = 0.f;
+      if (mn == -INFINITY) continue;  // (warp-uniform) no valid position yet
+#pragma unroll
+      for (int a2 = 0; a2 < 2; ++a2) pr[a2][g] = x[a2] == -INFINITY ? 0.f : expf(x[a2] - mn);
+      float ps = pr[0][g] + pr[1][g];
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      const float corr = expf(m[g] - mn);
+      l[g] = l[g] * corr + ps;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+      m[g] = mn;
+    }
+    if (qc == 0) {
+      at.sc[w][pi] = make_float2(pr[0][0], pr[0][1]);
+      at.sc[w][8 + pi] = make_float2(pr[1][0], pr[1][1]);
+    }
+    __syncwarp();
+    const uint8_t* vt = tile + kTileBytes / 2;
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      if (p0 + i >= valid) break;
+      const float2 pp = at.sc[w][i];
+      float vv[4];
+      if (p0 + i == pos) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
+      } else {
+        const uint2 vr = *reinterpret_cast<const uint2*>(vt + (row0 + i) * kHD * 2 + lane * 8);
+        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+        vv[0] = __low2float(vh[0]);
+        vv[1] = __high2float(vh[0]);
+        vv[2] = __low2float(vh[1]);
+        vv[3] = __high2float(vh[1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[0][e] += pp.x * vv[e];
+        acc[1][e] += pp.y * vv[e];
+      }
+    }
+  }
+
   __device__ __forceinline__ void run_attention(const AicasPhase& d) {
     AttnSmem& at = sm.at;
     AttnUnits au;
@@ -864,30 +964,30 @@ struct Consumer {
     const float scale = d.scale;
     const uint32_t ep = epoch_base + (uint32_t)ph + 1;
     float m[2], l[2], acc[2][4];
-    const int pi = lane >> 2, qc = lane & 3;  // score lanes: position within the warp's 8, dim quarter
-    int cur_b = -1;
-    float cs[4], sn[4];
-    for (int u = rg.start; u < rg.start + rg.count; ++u) {
-      const int b = au.stream_of(u);
+    // Tiles of a segment go in pairs: warps 0..3 take the first, warps 4..7
+    // the second (slot = w / 4); warp wq = w % 4 of a slot owns the tile's
+    // positions 16 wq .. 16 wq + 15.  Score lanes: (pi = lane / 4, dim quarter
+    // qc = lane % 4) handle positions 16 wq + pi and 16 wq + 8 + pi.
+    const int slot = w >> 2, wq = w & 3;
+    const int pi = lane >> 2, qc = lane & 3;
+    bool first_seg = true;
+    for (int u0 = rg.start; u0 < rg.start + rg.count;) {
+      const int b = au.stream_of(u0);
       const int cph = select_i(au.cph, b), valid = select_i(au.valid, b);
-      const int r = u - select_i(au.pre, b);
-      const int h = r / cph, j = r % cph;
+      const int r0 = u0 - select_i(au.pre, b);
+      const int h = r0 / cph, j0 = r0 % cph;
+      const int nseg = min(cph - j0, rg.start + rg.count - u0);  // this CTA's units of the (b, h) group
       const int pos = valid - 1, jpos = pos / kAttnChunk;
-      const bool seg_start = (u == rg.start) || (j == 0);
-      const bool seg_end = (u == rg.start + rg.count - 1) || (j == cph - 1);
       const size_t head_off = ((size_t)b * d.kv_heads + h) * d.max_len;
-      if (b != cur_b) {
-        cur_b = b;
+      const uint64_t ss0 = kTrace ? globaltimer_ns() : 0;
+      {  // segment start: queries, and this step's k / v when the segment holds its slot
+        float cs[4], sn[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           cs[e] = sm.rope_c[b][(lane * 4 + e) % (kHD / 2)];
           sn[e] = sm.rope_s[b][(lane * 4 + e) % (kHD / 2)];
         }
-      }
-      const uint64_t ss0 = kTrace ? globaltimer_ns() : 0;
-      if (seg_start) {
-        const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
-        const bool has_pos = jpos >= j && jpos <= last_j;
+        const bool has_pos = jpos >= j0 && jpos < j0 + nseg;
         const uint32_t* xw = qkv_w + (size_t)b * d.k;
         if (w < 2) {  // query heads 2h, 2h+1 of stream b
           const int col = (h * 2 + w) * kHD + lane * 4;
@@ -910,121 +1010,51 @@ struct Consumer {
           __half* cache = w == 2 ? kc : vc;
           *reinterpret_cast<uint2*>(cache + (head_off + pos) * kHD + lane * 4) = *reinterpret_cast<uint2*>(o);
         }
-        consumer_sync(kConsumerThreads);
-        if (kTrace && tid == 0 && u == rg.start) trace_put(a, ph, 1, (int64_t)globaltimer_ns());
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          m[g] = -INFINITY;
-          l[g] = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
-        }
       }
-      if (kTrace && seg_start) seg_ns += globaltimer_ns() - ss0;
-      const int st = rit % kStages;
+      consumer_sync(kConsumerThreads);
       if (kTrace && tid == 0) {
-        const uint64_t w0 = globaltimer_ns();
-        mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
-        tile_wait += globaltimer_ns() - w0;
-      } else {
-        mbar_wait_bounded(&sm.full[st], (rit / kStages) & 1u, s, kErrFullTimeout);
+        if (first_seg) trace_put(a, ph, 1, (int64_t)globaltimer_ns());
+        seg_ns += globaltimer_ns() - ss0;
       }
-      const int p0 = j * kAttnChunk;
-      const uint8_t* kt = sm.ring[st];
-      const uint8_t* vt = sm.ring[st] + kTileBytes / 2;
-      // Scores: lane (position pi, dim quarter c) dots its position's dims
-      // c*32 .. c*32+31 with both queries (exact fp16 products, fp32 sums),
-      // reading the K row's 16-byte pieces in an order rotated by pi (no
-      // shared-memory bank conflicts); two shuffles finish each score.
-      const int pq = p0 + w * kPosPerWarp + pi;
-      float sg[2] = {0.f, 0.f};
-      if (pq == pos) {  // this step's k: from at.kf (the tile may predate its write)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float* kf = at.kf + qc * 32 + 8 * ((jj + pi) & 3);
-          uint4 kv;
-          __half2* kh = reinterpret_cast<__half2*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) kh[e] = __floats2half2_rn(kf[2 * e], kf[2 * e + 1]);
-          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
-          sg[0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[0]);
-          sg[1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[1]);
-        }
-      } else {
-        const uint8_t* krow = kt + (w * kPosPerWarp + pi) * (kHD * 2) + qc * 64;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const uint4 kv = *reinterpret_cast<const uint4*>(krow + 16 * ((jj + pi) & 3));
-          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
-          sg[0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[0]);
-          sg[1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[1]);
-        }
-      }
-      float pr[2];
+      first_seg = false;
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
-        sg[g] += __shfl_xor_sync(0xffffffffu, sg[g], 1);
-        sg[g] += __shfl_xor_sync(0xffffffffu, sg[g], 2);
-        const float x = pq < valid ? sg[g] * scale : -INFINITY;
-        float cm = x;  // the warp's 8 positions: lanes differing in bits 2..4
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-        const float mn = fmaxf(m[g], cm);
-        pr[g] = 0.f;
-        if (mn == -INFINITY) continue;  // (warp-uniform) no valid position yet
-        pr[g] = x == -INFINITY ? 0.f : expf(x - mn);
-        float ps = pr[g];
-        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-        const float corr = expf(m[g] - mn);
-        l[g] = l[g] * corr + ps;
+        m[g] = -INFINITY;
+        l[g] = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
-        m[g] = mn;
+        for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
       }
-      // P V: lane l accumulates dims 4l .. 4l+3 of both heads; position i's
-      // probabilities come from its lane 4 i
-      const int pw = p0 + w * kPosPerWarp;
-#pragma unroll
-      for (int i = 0; i < kPosPerWarp; ++i) {
-        if (pw + i >= valid) break;
-        const float pr0 = __shfl_sync(0xffffffffu, pr[0], 4 * i);
-        const float pr1 = __shfl_sync(0xffffffffu, pr[1], 4 * i);
-        float vv[4];
-        if (pw + i == pos) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
-        } else {
-          const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
-          const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-          vv[0] = __low2float(vh[0]);
-          vv[1] = __high2float(vh[0]);
-          vv[2] = __low2float(vh[1]);
-          vv[3] = __high2float(vh[1]);
+#pragma unroll 1
+      for (int t = 0; t < nseg; t += 2) {
+        if (t + slot < nseg) {
+          const uint32_t ri = rit + slot;
+          const int st = ri % kStages;
+          if (kTrace && tid == 0) {
+            const uint64_t w0 = globaltimer_ns();
+            mbar_wait_bounded(&sm.full[st], (ri / kStages) & 1u, s, kErrFullTimeout);
+            tile_wait += globaltimer_ns() - w0;
+          } else {
+            mbar_wait_bounded(&sm.full[st], (ri / kStages) & 1u, s, kErrFullTimeout);
+          }
+          attend_tile(sm.ring[st], (j0 + t + slot) * kAttnChunk + 16 * wq, pos, valid, scale, pi, qc, m, l, acc);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.cempty[st]);
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[0][e] += pr0 * vv[e];
-          acc[1][e] += pr1 * vv[e];
-        }
+        rit += t + 1 < nseg ? 2 : 1;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.cempty[st]);
-      ++rit;
-      if (seg_end) {
-        if (lane == 0) {
-          at.wm[w][0] = m[0];
-          at.wm[w][1] = m[1];
-          at.wl[w][0] = l[0];
-          at.wl[w][1] = l[1];
-        }
+      // segment end: merge the 8 warps' states into this CTA's partial
+      if (lane == 0) {
+        at.wm[w][0] = m[0];
+        at.wm[w][1] = m[1];
+        at.wl[w][0] = l[0];
+        at.wl[w][1] = l[1];
+      }
 #pragma unroll
-        for (int g = 0; g < 2; ++g)
+      for (int g = 0; g < 2; ++g)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
-        consumer_sync(kConsumerThreads);
+        for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
+      consumer_sync(kConsumerThreads);
+      {
         const int gfirst = select_i(au.pre, b) + h * cph;
         const int first_owner = owner_of(gfirst, U, na);
         const int nsplit = owner_of(gfirst + cph - 1, U, na) - first_owner + 1;
@@ -1052,6 +1082,7 @@ struct Consumer {
           ll64_store(hp + g * (kHD + 1) + 1 + t, o, ep);
         }
       }
+      u0 += nseg;
     }
     if (kTrace && tid == 0) {
       trace_put(a, ph, 6, (int64_t)tile_wait);
@@ -1224,7 +1255,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
-      mbar_init(&sm.cempty[i], kConsumerWarps);
+      mbar_init(&sm.cempty[i], kConsumerWarps / 2);  // attention tiles: 4 warps each
     }
     for (int i = 0; i < kDSlots; ++i) {
       mbar_init(&sm.dfull[i], 1);
