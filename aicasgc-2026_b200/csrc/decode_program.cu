@@ -30,8 +30,10 @@
 // read from shared memory exactly once (conflict-free 512-byte warp accesses)
 // and a row needs one warp reduction.
 //
-// Attention tile: K and V rows of 64 cache positions of one KV head (32 KB),
-// 8 positions per consumer warp.  Work units (KV head, 64-position chunk) are
+// Attention tile: K and V rows of 64 cache positions of one KV head (32 KB).
+// A CTA's tiles go in pairs: consumer warps 0..3 take one, 4..7 the next,
+// each warp 16 positions (a lane scores two positions over a quarter of the
+// head dims, so it runs four independent dot chains).  Work units (KV head, 64-position chunk) are
 // split into contiguous ranges over the CTAs; each CTA's segment of a head
 // yields one (log-sum-exp, normalised acc) partial, stored as 64-bit LL words;
 // every CTA of the head then merges a slice of the head's outputs over all
@@ -92,7 +94,6 @@ constexpr int kStageBytes = kRows * kRowBytes;  // 32 KB: one bulk copy per tile
 #endif
 constexpr int kStages = AICAS_STAGES;
 constexpr int kAttnChunk = 64;  // cache positions per attention tile
-constexpr int kPosPerWarp = kAttnChunk / kConsumerWarps;
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kVec = kChunk / 256;                // uint4 per lane per chunk
 #ifndef AICAS_EPI_BATCH
@@ -105,13 +106,13 @@ static_assert(kAttnChunk * kHD * 2 * 2 == kStageBytes, "attention tile must fill
 static_assert(AICAS_MAX_K % kChunk == 0, "max K must be whole chunks");
 
 struct AttnSmem {
-  float q[2][kHD];         // rotated queries of the head pair
   float kf[kHD], vf[kHD];  // this step's k (normed+rotated) / v of the current KV head
   float wm[kConsumerWarps][2];
   float wl[kConsumerWarps][2];
   float wacc[kConsumerWarps][2][kHD];
   float rope_c[kHD / 2], rope_s[kHD / 2];  // this launch's MRoPE cos/sin (fp16-rounded)
-  float sc[kConsumerWarps][2 * kPosPerWarp];  // raw q.k scores of each warp's positions
+  __align__(16) __half qh[2][kHD];   // the segment's queries as fp16 (their values are fp16)
+  float2 sc[kConsumerWarps][16];     // per warp: probabilities (both heads) of its 16 positions
 };
 
 struct __align__(128) Smem {
@@ -760,46 +761,6 @@ struct Consumer {
     }
   }
 
-  // Reduce-scatter of NV per-lane partial sums (NV = 2, 4, 8 or 16) across the
-  // warp: halve the kept values at lane offsets 16, 8, ... then finish with a
-  // full butterfly.  Lane l ends with the warp total of value index
-  // sum over steps of (lane bit set ? half : 0), see scatter_lane.
-  template <int NV>
-  __device__ __forceinline__ float reduce_scatter(float (&a)[NV], int& idx) {
-    int base = 0;
-    int o = 16;
-#pragma unroll
-    for (int n = NV; n > 1; n >>= 1, o >>= 1) {
-      const bool hi = lane & o;
-#pragma unroll
-      for (int i = 0; i < n / 2; ++i) {
-        const float send = hi ? a[i] : a[i + n / 2];
-        const float keep = hi ? a[i + n / 2] : a[i];
-        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-      }
-      base += hi ? n / 2 : 0;
-    }
-    float t = a[0];
-#pragma unroll
-    for (; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    idx = base;
-    return t;
-  }
-
-  // A lane that holds value index v after reduce_scatter<NV>.
-  template <int NV>
-  __device__ __forceinline__ static int scatter_lane(int v) {
-    int lane_bits = 0, o = 16;
-#pragma unroll
-    for (int n = NV; n > 1; n >>= 1, o >>= 1) {
-      if (v >= n / 2) {
-        lane_bits |= o;
-        v -= n / 2;
-      }
-    }
-    return lane_bits;
-  }
-
   // This lane's 64 columns of one tile row into registers (`row_s`: shared
   // address of the row plus the lane's offset 1024 (lane / 8) + 16 (lane % 8);
   // value v sits 128 v bytes further); `jmask` skips columns beyond k.  Loading a tile completely
@@ -1253,6 +1214,113 @@ struct Consumer {
     }
   }
 
+  // One warp's 16 positions p0 .. p0 + 15 of a 64-slot K/V tile (shared
+  // address `tile`): online-softmax update of (m, l, acc) for both query
+  // heads.  Scores: lane (pi = lane / 4, dim quarter qc = lane % 4) dots
+  // positions p0 + pi and p0 + 8 + pi over dims qc*32 .. qc*32+31 (exact fp16
+  // products, fp32 sums; K rows read in an order rotated by pi, free of bank
+  // conflicts); two shuffles finish each score.  P V: lane l accumulates dims
+  // 4l .. 4l+3; the probabilities pass through the warp's shared-memory row.
+  // Slot `pos` (this step's k / v; -1: none) comes from at.kf / at.vf: the tile
+  // may have been loaded before it was written.
+  __device__ __forceinline__ void attend_tile(const uint8_t* tile, int p0, int pos, int valid, float scale,
+                                              float (&m)[2], float (&l)[2], float (&acc)[2][4]) {
+    AttnSmem& at = sm.at;
+    const int pi = lane >> 2, qc = lane & 3;
+    const int row0 = p0 % kAttnChunk;
+    float sg[2][2];
+#pragma unroll
+    for (int a2 = 0; a2 < 2; ++a2) {
+      sg[a2][0] = sg[a2][1] = 0.f;
+      const int prow = row0 + 8 * a2 + pi;
+      if (p0 + 8 * a2 + pi == pos) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
+          uint4 kv;
+          __half2* kh = reinterpret_cast<__half2*>(&kv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kh[e] = __floats2half2_rn(at.kf[qo + 2 * e], at.kf[qo + 2 * e + 1]);
+          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
+          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
+        }
+      } else {
+        const uint8_t* krow = tile + prow * (kHD * 2) + qc * 64;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int jr = (jj + pi) & 3;
+          const uint4 kv = *reinterpret_cast<const uint4*>(krow + 16 * jr);
+          const int qo = qc * 32 + 8 * jr;
+          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
+          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
+        }
+      }
+    }
+    float pr[2][2];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      float x[2];
+#pragma unroll
+      for (int a2 = 0; a2 < 2; ++a2) {
+        float v = sg[a2][g];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        x[a2] = p0 + 8 * a2 + pi < valid ? v * scale : -INFINITY;
+      }
+      float cm = fmaxf(x[0], x[1]);
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+      const float mn = fmaxf(m[g], cm);
+      pr[0][g] = pr[1][g] = 0.f;
+      if (mn == -INFINITY) continue;  // (warp-uniform) no valid position yet
+#pragma unroll
+      for (int a2 = 0; a2 < 2; ++a2) pr[a2][g] = x[a2] == -INFINITY ? 0.f : expf(x[a2] - mn);
+      float ps = pr[0][g] + pr[1][g];
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      const float corr = expf(m[g] - mn);
+      l[g] = l[g] * corr + ps;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+      m[g] = mn;
+    }
+    if (qc == 0) {
+      at.sc[w][pi] = make_float2(pr[0][0], pr[0][1]);
+      at.sc[w][8 + pi] = make_float2(pr[1][0], pr[1][1]);
+    }
+    __syncwarp();
+    const uint8_t* vt = tile + kStageBytes / 2;
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      if (p0 + i >= valid) break;
+      const float2 pp = at.sc[w][i];
+      float vv[4];
+      if (p0 + i == pos) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
+      } else {
+        const uint2 vr = *reinterpret_cast<const uint2*>(vt + (row0 + i) * kHD * 2 + lane * 8);
+        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+        vv[0] = __low2float(vh[0]);
+        vv[1] = __high2float(vh[0]);
+        vv[2] = __low2float(vh[1]);
+        vv[3] = __high2float(vh[1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[0][e] += pp.x * vv[e];
+        acc[1][e] += pp.y * vv[e];
+      }
+    }
+  }
+
+  // Attention phase: the CTA's units (KV head x 64-slot chunk) segment by
+  // segment; the tiles of a segment go in pairs (warps 0..3 and 4..7, each
+  // warp 16 positions of its tile), and each segment ends with this CTA's
+  // partial for the head (or the head's output when the CTA has all of it)
+  // and its slice of the head's merge.
   __device__ __forceinline__ void run_attention(const AicasPhase& d) {
     AttnSmem& at = sm.at;
     const bool q_ready = d.flags & AICAS_F_Q_READY;
@@ -1283,197 +1351,113 @@ struct Consumer {
     }
     const float scale = d.scale;
     const int jpos = pos / kAttnChunk;
+    const int kpos = q_ready ? -1 : pos;  // the slot whose k / v come from shared memory
+    const int slot = w >> 2, wq = w & 3;
     bool stamped = false;
-    // per-warp online-softmax state for the 2 query heads of the current KV head
     float m[2], l[2], acc[2][4];
-    float qreg[2][4];
-    for (int u = rg.start; u < rg.start + rg.count; ++u) {
-      const int h = u / cph, j = u % cph;
-      const bool seg_start = (u == rg.start) || (j == 0);
-      const bool seg_end = (u == rg.start + rg.count - 1) || (j == cph - 1);
-      if (seg_start) {
-        const int last_j = min(cph - 1, j + (rg.start + rg.count - 1 - u));
-        const bool has_pos = !q_ready && jpos >= j && jpos <= last_j;
-        if (w < 2) {  // query heads 2h, 2h+1
-          const int col = (h * 2 + w) * kHD + lane * 4;
-          const uint2 raw = ll_in ? ll_poll4(qkv_w, col, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + col));
-          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
-          if (!q_ready) norm_rope_head(v, sm.nw, d.eps, cs, sn);
+    for (int u0 = rg.start; u0 < rg.start + rg.count;) {
+      const int h = u0 / cph, j0 = u0 % cph;
+      const int nseg = min(cph - j0, rg.start + rg.count - u0);
+      const bool has_pos = !q_ready && jpos >= j0 && jpos < j0 + nseg;
+      if (w < 2) {  // query heads 2h, 2h+1
+        const int col = (h * 2 + w) * kHD + lane * 4;
+        const uint2 raw = ll_in ? ll_poll4(qkv_w, col, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + col));
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+        float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+        if (!q_ready) norm_rope_head(v, sm.nw, d.eps, cs, sn);
+        *reinterpret_cast<__half2*>(&at.qh[w][lane * 4]) = __floats2half2_rn(v[0], v[1]);
+        *reinterpret_cast<__half2*>(&at.qh[w][lane * 4 + 2]) = __floats2half2_rn(v[2], v[3]);
+      } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
+        const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
+        const uint2 raw = ll_in ? ll_poll4(qkv_w, off, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + off));
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+        float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+        if (w == 2) norm_rope_head(v, sm.nw + kHD, d.eps, cs, sn);
+        float* dst = w == 2 ? at.kf : at.vf;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) at.q[w][lane * 4 + e] = v[e];
-        } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
-          const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
-          const uint2 raw = ll_in ? ll_poll4(qkv_w, off, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + off));
-          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-          float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
-          if (w == 2) norm_rope_head(v, sm.nw + kHD, d.eps, cs, sn);
-          float* dst = w == 2 ? at.kf : at.vf;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
-          __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
-          __half* cache = w == 2 ? kc : vc;
-          *reinterpret_cast<uint2*>(cache + ((size_t)h * d.max_len + pos) * kHD + lane * 4) =
-              *reinterpret_cast<uint2*>(o);
-        }
-        consumer_sync(kConsumerThreads);
-        if (!stamped) {
-          stamp(ph, 1);
-          stamped = true;
-        }
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) qreg[g][e] = at.q[g][lane * 4 + e];
-          m[g] = -INFINITY;
-          l[g] = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
-        }
+        for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
+        __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
+        __half* cache = w == 2 ? kc : vc;
+        *reinterpret_cast<uint2*>(cache + ((size_t)h * d.max_len + pos) * kHD + lane * 4) =
+            *reinterpret_cast<uint2*>(o);
       }
-      const int st = r.stage();
-      wait_full(st);
-      const int p0 = j * kAttnChunk;
-      const uint8_t* kt = sm.ring[st];
-      const uint8_t* vt = sm.ring[st] + kStageBytes / 2;
-      // this warp's kPosPerWarp positions; the current position's k/v come
-      // from shared memory (at.kf / at.vf), never from the cache tile
-      float kv[kPosPerWarp][4];
-#pragma unroll
-      for (int i = 0; i < kPosPerWarp; ++i) {
-        const int p = p0 + w * kPosPerWarp + i;
-        if (!q_ready && p == pos) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) kv[i][e] = at.kf[lane * 4 + e];
-        } else {
-          const uint2 kr = *reinterpret_cast<const uint2*>(kt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
-          const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-          kv[i][0] = __low2float(kh[0]);
-          kv[i][1] = __high2float(kh[0]);
-          kv[i][2] = __low2float(kh[1]);
-          kv[i][3] = __high2float(kh[1]);
-        }
+      consumer_sync(kConsumerThreads);
+      if (!stamped) {
+        stamp(ph, 1);
+        stamped = true;
       }
-      // partial dots of the lane's 4 dims; value index v = g * kPosPerWarp + i
-      float part[2 * kPosPerWarp];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+      }
+#pragma unroll 1
+      for (int t = 0; t < nseg; t += 2) {
+        if (t + slot < nseg) {
+          const uint32_t ri = r.it + slot;
+          const int st = ri % kStages;
+          wait_full_at(st, ri / kStages);
+          attend_tile(sm.ring[st], (j0 + t + slot) * kAttnChunk + 16 * wq, kpos, valid, scale, m, l, acc);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cnt(&sm.cempty[st], 2);  // 4 warps per tile, 8 arrivals per stage use
+        }
+        r.it += t + 1 < nseg ? 2 : 1;
+      }
+      stamp_field(6);
+      // merge the 8 warps' states of this segment into one partial
+      if (lane == 0) {
+        at.wm[w][0] = m[0];
+        at.wm[w][1] = m[1];
+        at.wl[w][0] = l[0];
+        at.wl[w][1] = l[1];
+      }
 #pragma unroll
       for (int g = 0; g < 2; ++g)
 #pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i)
-          part[g * kPosPerWarp + i] =
-              qreg[g][0] * kv[i][0] + qreg[g][1] * kv[i][1] + qreg[g][2] * kv[i][2] + qreg[g][3] * kv[i][3];
-      int vidx;
-      const float tot = reduce_scatter<2 * kPosPerWarp>(part, vidx);
-      // the 16 scores (value index g * kPosPerWarp + i) go to shared memory,
-      // so the softmax below is a compact loop rather than unrolled code:
-      // this runs once per layer, on cold instruction cache lines
-      if ((lane & 1) == 0) at.sc[w][vidx] = tot;
-      __syncwarp();
-      const int pw = p0 + w * kPosPerWarp;  // this warp's first position
+        for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
+      consumer_sync(kConsumerThreads);
+      const int na = attn_ctas(U, nct);
+      const int first_owner = owner_of(h * cph, U, na);
+      const int split = cta - first_owner;
+      const int nsplit = owner_of(h * cph + cph - 1, U, na) - first_owner + 1;
+      const uint32_t ep = epoch_base + (uint32_t)ph + 1;
+      // thread (g, t): query head 2h + g, head dim t: merge the 8 warps' states
+      const int g = tid / kHD, t = tid % kHD;
+      float M = -INFINITY;
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        float cmax = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kPosPerWarp; ++i)
-          if (pw + i < valid) cmax = fmaxf(cmax, at.sc[w][g * kPosPerWarp + i] * scale);
-        const float mn = fmaxf(m[g], cmax);
-        if (mn == -INFINITY) continue;
-        const float corr = expf(m[g] - mn);
-        l[g] *= corr;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
-        m[g] = mn;
-      }
-      // one V row per position serves both query heads
+      for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
+      float L = 0.f, A = 0.f;
 #pragma unroll 1
-      for (int i = 0; i < kPosPerWarp && pw + i < valid; ++i) {
-        const int p = pw + i;
-        float vv[4];
-        if (!q_ready && p == pos) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
-        } else {
-          const uint2 vr = *reinterpret_cast<const uint2*>(vt + (w * kPosPerWarp + i) * kHD * 2 + lane * 8);
-          const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-          vv[0] = __low2float(vh[0]);
-          vv[1] = __high2float(vh[0]);
-          vv[2] = __low2float(vh[1]);
-          vv[3] = __high2float(vh[1]);
-        }
-        const float pr0 = expf(at.sc[w][i] * scale - m[0]);
-        const float pr1 = expf(at.sc[w][kPosPerWarp + i] * scale - m[1]);
-        l[0] += pr0;
-        l[1] += pr1;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[0][e] += pr0 * vv[e];
-          acc[1][e] += pr1 * vv[e];
+      for (int i = 0; i < kConsumerWarps; ++i) {
+        const float mi = at.wm[i][g];
+        if (mi != -INFINITY) {
+          const float f = expf(mi - M);
+          L += at.wl[i][g] * f;
+          A += at.wacc[i][g][t] * f;
         }
       }
-      release(st);
-      if (seg_end) {
-        stamp_field(6);
-        // merge the 8 warps' states of this segment into one partial
-        if (lane == 0) {
-          at.wm[w][0] = m[0];
-          at.wm[w][1] = m[1];
-          at.wl[w][0] = l[0];
-          at.wl[w][1] = l[1];
-        }
-#pragma unroll
-        for (int g = 0; g < 2; ++g)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
-        consumer_sync(kConsumerThreads);
-        const int na = attn_ctas(U, nct);
-        const int first_owner = owner_of(h * cph, U, na);
-        const int last_owner = owner_of(h * cph + cph - 1, U, na);
-        const int split = cta - first_owner;
-        const int nsplit = last_owner - first_owner + 1;
-        const uint32_t ep = epoch_base + (uint32_t)ph + 1;
-        // thread (g, t): query head 2h + g, head dim t.  This CTA's partial
-        // as (log-sum-exp, normalised acc): merge the 8 warps' states.
-        const int g = tid / kHD, t = tid % kHD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
-        float L = 0.f, A = 0.f;
-#pragma unroll 1
-        for (int i = 0; i < kConsumerWarps; ++i) {
-          const float mi = at.wm[i][g];
-          if (mi != -INFINITY) {
-            const float f = expf(mi - M);
-            L += at.wl[i][g] * f;
-            A += at.wacc[i][g][t] * f;
-          }
-        }
-        const float lse = M + logf(L), o = A / L;
-        uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out);
-        __half* const out_h = reinterpret_cast<__half*>(d.out);
-        const bool ll_out = d.flags & AICAS_F_LL_OUT;
-        if (nsplit == 1) {  // the whole head is this CTA's: thread (g, t) has its output
-          const int oidx = (h * 2 + g) * kHD + t;
-          if (ll_out) ll_store(out_w + oidx, o, ep & 0xffffu);
-          else out_h[oidx] = __float2half_rn(o);
-          stamp_field(7);
-        } else {
-          // 1) this CTA's partial as 64-bit LL words (no fence, no counter)
-          uint64_t* const hp = &s->part[h][0][0][0];  // [split][g][log-sum-exp, acc[128]]
-          constexpr int kSplitStride = 2 * (kHD + 1);
-          if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
-          ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
-          // 2) every CTA of the head merges its slice of the head's outputs
-          // over all splits (merge_head).  A CTA only waits for partials of
-          // its current head, which every owner stores before it waits on
-          // anything later, so the waits cannot form a cycle.
-          merge_head(d, h, split, nsplit, ep);
-          stamp_field(7);
-        }
+      const float lse = M + logf(L), o = A / L;
+      if (nsplit == 1) {  // the whole head is this CTA's: thread (g, t) has its output
+        const int oidx = (h * 2 + g) * kHD + t;
+        if (d.flags & AICAS_F_LL_OUT) ll_store(reinterpret_cast<uint32_t*>(d.out) + oidx, o, ep & 0xffffu);
+        else reinterpret_cast<__half*>(d.out)[oidx] = __float2half_rn(o);
+      } else {
+        // this CTA's partial as 64-bit LL words (no fence, no counter), then
+        // its slice of the head's merge (merge_head).  A CTA only waits for
+        // partials of its current head, which every owner stores before it
+        // waits on anything later, so the waits cannot form a cycle.
+        uint64_t* const hp = &s->part[h][0][0][0];
+        constexpr int kSplitStride = 2 * (kHD + 1);
+        if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
+        ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
+        merge_head(d, h, split, nsplit, ep);
       }
+      stamp_field(7);
+      u0 += nseg;
     }
   }
-
-
   // Interleaved-MRoPE cos/sin of the step's position, once per launch
   // (every attention phase of the step uses the same table):
   // frequency i takes axis 1 (h) when i % 3 == 1 and i < 3 * section[1],
