@@ -31,6 +31,9 @@ F_BARRIER = 1 << 10
 F_LL_IN = 1 << 11
 F_LL_OUT = 1 << 12
 F_LL_RESID = 1 << 13
+F_CNT_IN = 1 << 14
+F_CNT_OUT = 1 << 15
+F_CNT_RESID = 1 << 16
 
 DEVICE_ERRORS = {
     10: "grid barrier timed out",

@@ -27,9 +27,9 @@ import ctypes
 
 import torch
 
-from _native import (F_KBLOCKED, F_LL_IN, F_LL_OUT, F_LL_RESID, F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED,
-                     MAX_BATCH, PH_ATTN, PH_GATEUP, PH_GEMV, PH_LMHEAD, AicasError, AicasPhase, AicasStepState,
-                     batch_scratch_bytes, check, lib)
+from _native import (F_CNT_IN, F_CNT_OUT, F_CNT_RESID, F_KBLOCKED, F_LL_IN, F_LL_OUT, F_NORM, F_RESID,
+                     F_RESID_EMBED, F_X_EMBED, MAX_BATCH, PH_ATTN, PH_GATEUP, PH_GEMV, PH_LMHEAD, AicasError,
+                     AicasPhase, AicasStepState, batch_scratch_bytes, check, lib)
 from _ops import device_error
 from engine import hf_inv_freq
 from prefill import layer_weights_from_hf, prefill
@@ -83,12 +83,13 @@ class Qwen3VLBatchDecodeEngine:
             kv_shape = (s.num_layers, B, s.num_kv_heads, max_cache_len, s.head_dim)
             self.k_cache = torch.zeros(kv_shape, **f16)
             self.v_cache = torch.zeros(kv_shape, **f16)
-            ll = dict(dtype=torch.int32, device=dev)  # LL vectors [stream][len]
-            self.h = torch.zeros((B, s.hidden), **ll)
-            self.h_mid = torch.zeros((B, s.hidden), **ll)
-            self.qkv = torch.zeros((B, s.qkv_rows), **ll)
-            self.attn = torch.zeros((B, s.q_size), **ll)
-            self.act = torch.zeros((B, s.intermediate), **ll)
+            # qkv: LL words [stream][len] (attention polls only its heads' columns); the
+            # others are counted fp16 vectors in the operand layout [len / 8][8 stream slots][8]
+            self.qkv = torch.zeros((B, s.qkv_rows), dtype=torch.int32, device=dev)
+            self.h = torch.zeros((s.hidden // 8, MAX_BATCH, 8), **f16)
+            self.h_mid = torch.zeros((s.hidden // 8, MAX_BATCH, 8), **f16)
+            self.attn = torch.zeros((s.q_size // 8, MAX_BATCH, 8), **f16)
+            self.act = torch.zeros((s.intermediate // 8, MAX_BATCH, 8), **f16)
             self.out_tokens = torch.full((B, max_steps), -1, dtype=torch.int64, device=dev)
             self.logits_ring = int(logits_ring)
             self.logits = torch.zeros((B, logits_ring, s.vocab), **f16) if logits_ring > 0 else None
@@ -107,10 +108,13 @@ class Qwen3VLBatchDecodeEngine:
 
     # ------------------------------------------------------------------ program
     def _build_program(self):
-        """28 x [QKV, ATTN, O_PROJ, GATE_UP, DOWN] + LM_HEAD over LL vectors,
-        as the batch-1 program (engine.py), with tile-layout weights and
-        per-stream rows.  Every GEMV phase gives every CTA rows (checked), so
-        one buffer per vector can be reused across layers."""
+        """28 x [QKV, ATTN, O_PROJ, GATE_UP, DOWN] + LM_HEAD, as the batch-1
+        program (engine.py), with tile-layout weights and per-stream rows.
+        qkv is an LL vector (each attention CTA polls only its heads'
+        columns); attn, h_mid, act and h are counted vectors (every CTA reads
+        all of them, once, after all CTAs have written them).  Every GEMV
+        phase gives every CTA rows (checked), so one buffer per vector can be
+        reused across layers."""
         s, nct = self.shape, self.num_ctas
         eps = float(s.rms_eps)
         phases = []
@@ -144,10 +148,10 @@ class Qwen3VLBatchDecodeEngine:
                 gemv_like(PH_GEMV, F_NORM | F_X_EMBED | F_LL_OUT, s.qkv_rows, s.hidden, T["qkv"], self.embed,
                           self.qkv, norm_w=L["ln1"])
             else:
-                gemv_like(PH_GEMV, F_NORM | F_LL_IN | F_LL_OUT, s.qkv_rows, s.hidden, T["qkv"], self.h, self.qkv,
+                gemv_like(PH_GEMV, F_NORM | F_CNT_IN | F_LL_OUT, s.qkv_rows, s.hidden, T["qkv"], self.h, self.qkv,
                           norm_w=L["ln1"], x_src=base - 1)
             a = AicasPhase()
-            a.kind, a.flags = PH_ATTN, F_LL_IN | F_LL_OUT
+            a.kind, a.flags = PH_ATTN, F_LL_IN | F_CNT_OUT
             a.kv_heads, a.q_heads, a.max_len = s.num_kv_heads, s.num_heads, self.max_cache_len
             a.k, a.n = s.qkv_rows, s.q_size  # row lengths of the stream's qkv input and attention output
             a.x, a.out, a.x_src = ptr(self.qkv), ptr(self.attn), base
@@ -155,13 +159,13 @@ class Qwen3VLBatchDecodeEngine:
             a.k_cache, a.v_cache = ptr(self.k_cache[li]), ptr(self.v_cache[li])
             a.eps, a.scale = eps, float(s.head_dim ** -0.5)
             phases.append(a)
-            gemv_like(PH_GEMV, F_LL_IN | F_LL_OUT | F_RESID | (F_RESID_EMBED if first else F_LL_RESID), s.hidden,
+            gemv_like(PH_GEMV, F_CNT_IN | F_CNT_OUT | F_RESID | (F_RESID_EMBED if first else F_CNT_RESID), s.hidden,
                       s.q_size, T["o"], self.attn, self.h_mid, resid=self.embed if first else self.h, x_src=base + 1)
-            gemv_like(PH_GATEUP, F_NORM | F_LL_IN | F_LL_OUT, s.intermediate, s.hidden, T["gate_up"], self.h_mid,
+            gemv_like(PH_GATEUP, F_NORM | F_CNT_IN | F_CNT_OUT, s.intermediate, s.hidden, T["gate_up"], self.h_mid,
                       self.act, norm_w=L["ln2"], x_src=base + 2)
-            gemv_like(PH_GEMV, F_LL_IN | F_LL_OUT | F_RESID | F_LL_RESID | F_KBLOCKED, s.hidden, s.intermediate,
+            gemv_like(PH_GEMV, F_CNT_IN | F_CNT_OUT | F_RESID | F_CNT_RESID | F_KBLOCKED, s.hidden, s.intermediate,
                       T["down"], self.act, self.h, resid=self.h_mid, x_src=base + 3)
-        gemv_like(PH_LMHEAD, F_NORM | F_LL_IN, s.vocab, s.hidden, self.lm_tiled, self.h, None,
+        gemv_like(PH_LMHEAD, F_NORM | F_CNT_IN, s.vocab, s.hidden, self.lm_tiled, self.h, None,
                   norm_w=self.final_norm, x_src=5 * s.num_layers - 1)
         arr = (AicasPhase * len(phases))(*phases)
         check(self._lib.aicas_validate_batch_phases(arr, len(phases)), "aicas_validate_batch_phases")

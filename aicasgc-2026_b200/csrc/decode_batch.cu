@@ -346,6 +346,44 @@ __device__ __forceinline__ void ll_store8(uint32_t* p, const float (&y)[8], uint
                : "memory");
 }
 
+// Completion counters of counted vectors (AICAS_F_CNT_*): one release add per
+// CTA and phase; a reader polls with relaxed loads and takes one acquire
+// fence once the count is complete (wrap-safe comparison).
+__device__ __forceinline__ void red_release_add_u32(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool wait_count(const uint32_t* p, uint32_t target, AicasScratch* s) {
+  if ((int32_t)(ld_relaxed_u32(p) - target) >= 0) {
+    fence_acquire_gpu();
+    return true;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if ((int32_t)(ld_relaxed_u32(p) - target) >= 0) {
+      fence_acquire_gpu();
+      return true;
+    }
+    if ((it & 31u) == 0) {
+      if (ld_volatile_int(&s->abort)) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(s, kErrInputTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// Byte offset of values [8 v, 8 v + 8) of stream b in a counted vector (the
+// batched operand layout [len/8][8 stream slots][8]).
+__device__ __forceinline__ size_t cnt_off(int v, int b) { return ((size_t)v * kMaxB + b) * 16; }
+
 // ---------------------------------------------------------------------------
 // Producer, L2 prefetch, MMA issuer
 // ---------------------------------------------------------------------------
@@ -497,6 +535,7 @@ struct Consumer {
   int tid, w, lane, nct, cta, nb;
   uint32_t tmem;
   uint32_t epoch_base;
+  uint32_t cnt_target = 0;  // completion count of a counted vector in this launch: (launches + 1) * grid
   uint32_t gc = 0;   // accumulator groups consumed (epilogue warps)
   uint32_t rit = 0;  // ring tiles passed (GEMV tiles via the MMA warp, attention tiles read in place)
   int ph = 0;
@@ -537,6 +576,10 @@ struct Consumer {
     const int k = d.k, C = k / kChunk;
     const int b = tid & 7, g = tid >> 3;
     const bool act = active(b);
+    if (d.flags & AICAS_F_CNT_IN) {
+      build_x_counted(d);
+      return;
+    }
     const uint32_t ep = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
     const bool ll = d.flags & AICAS_F_LL_IN;
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(d.x) + (size_t)b * k;
@@ -596,6 +639,64 @@ struct Consumer {
       }
     }
     // the MMA reads the operand through the async proxy
+    fence_proxy_async_smem();
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) mbar_arrive(&sm.xready);
+    if (kTrace && tid == 0) trace_put(a, ph, 1, (int64_t)globaltimer_ns());
+  }
+
+  // A counted input: wait until every CTA has written its part, then copy the
+  // vector (already in the operand layout: piece i = 16 bytes of stream i % 8)
+  // into the A operand, applying the RMSNorm prologue (k == 2048) on the way.
+  // Thread tid copies pieces tid, tid + 256, ...: all of stream tid % 8.
+  __device__ __forceinline__ void build_x_counted(const AicasPhase& d) {
+    const int k = d.k;
+    const int b = tid & 7;
+    const bool act = active(b);
+    if (tid == 0) wait_count(&bs->done[d.x_src], cnt_target, s);
+    consumer_sync(kConsumerThreads);
+    const uint4* src = reinterpret_cast<const uint4*>(d.x);
+    uint4* dst = reinterpret_cast<uint4*>(sm.xa);
+    if (d.flags & AICAS_F_NORM) {  // k == 2048: 8 pieces per thread
+      uint4 raw[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        raw[i] = act ? ldcg_u4(src + tid + kConsumerThreads * i) : make_uint4(0, 0, 0, 0);
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hp[q]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+      if (lane < 8) sm.ssq[w][lane] = ss;
+      consumer_sync(kConsumerThreads);
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kConsumerWarps; ++i) tot += sm.ssq[i][b];
+      const float inv = rsqrtf(tot / (float)k + d.eps);
+      const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = (tid + kConsumerThreads * i) >> 3;  // column group
+        const uint4 wr = __ldg(reinterpret_cast<const uint4*>(nw + 8 * v));
+        __half2* hp = reinterpret_cast<__half2*>(&raw[i]);
+        const __half2* wp = reinterpret_cast<const __half2*>(&wr);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hp[q]);
+          const float2 wf = __half22float2(wp[q]);
+          hp[q] = __floats2half2_rn(wf.x * r16(f.x * inv), wf.y * r16(f.y * inv));
+        }
+        dst[tid + kConsumerThreads * i] = act ? raw[i] : make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      const int pieces = k;  // 8 streams x k values x 2 bytes / 16
+      for (int i = tid; i < pieces; i += kConsumerThreads) dst[i] = act ? ldcg_u4(src + i) : make_uint4(0, 0, 0, 0);
+    }
     fence_proxy_async_smem();
     consumer_sync(kConsumerThreads);
     if (tid == 0) mbar_arrive(&sm.xready);
@@ -699,7 +800,15 @@ struct Consumer {
 #pragma unroll
           for (int j = 0; j < 8; ++j) rv[j] = 0.f;
           if (flags & AICAS_F_RESID) {
-            if (flags & AICAS_F_LL_RESID) {  // complete before this phase: data only
+            if (flags & AICAS_F_CNT_RESID) {  // counted, complete before this phase
+              const uint4 r = ldcg_u4(reinterpret_cast<const uint8_t*>(d.resid) + cnt_off(row0 / 8, b));
+              const __half2* hp = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+              for (int h2 = 0; h2 < 4; ++h2) {
+                rv[2 * h2] = __low2float(hp[h2]);
+                rv[2 * h2 + 1] = __high2float(hp[h2]);
+              }
+            } else if (flags & AICAS_F_LL_RESID) {  // complete before this phase: data only
               const uint32_t* rw = reinterpret_cast<const uint32_t*>(d.resid) + (size_t)b * n + row0;
               const uint4 r0 = ll_load4w(rw), r1 = ll_load4w(rw + 4);
               const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
@@ -738,6 +847,12 @@ struct Consumer {
               best_v = y[j];
               best_i = row0 + j;
             }
+        } else if (flags & AICAS_F_CNT_OUT) {
+          __half2 hv[4];
+#pragma unroll
+          for (int h2 = 0; h2 < 4; ++h2) hv[h2] = __floats2half2_rn(y[2 * h2], y[2 * h2 + 1]);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(d.out) + cnt_off(row0 / 8, b)) =
+              *reinterpret_cast<const uint4*>(hv);
         } else {
           ll_store8(out + (size_t)b * n + row0, y, ep16);
         }
@@ -1074,8 +1189,7 @@ struct Consumer {
         }
         const float lse = M + logf(L), o = A / L;
         if (nsplit == 1) {  // the whole group is this CTA's
-          uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
-          ll_store(out_w + (h * 2 + g) * kHD + t, o, ep & 0xffffu);
+          store_attn(d, b, (h * 2 + g) * kHD + t, o, ep);
         } else {  // this CTA's partial as 64-bit LL words; merged below
           uint64_t* const hp = &bs->part[b * d.kv_heads + h][cta - first_owner][0][0];
           if (t == 0) ll64_store(hp + g * (kHD + 1), lse, ep);
@@ -1114,7 +1228,6 @@ struct Consumer {
   // fixed xor-shuffle tree combines the lanes' (max, sum, acc) triples.
   __device__ __noinline__ void merge_group(const AicasPhase& d, int b, int h, int split, int nsplit, uint32_t ep) {
     uint64_t* const hp = &bs->part[b * d.kv_heads + h][0][0][0];
-    uint32_t* const out_w = reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n;
     constexpr int kSplitStride = 2 * (kHD + 1);
     const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
     const int npairs = q1 - q0;
@@ -1193,7 +1306,16 @@ struct Consumer {
         mx = mm;
       }
     }
-    if (actv && sub == 0) ll_store(out_w + (h * 2 + gq) * kHD + tq, ac / S, ep & 0xffffu);
+    if (actv && sub == 0) store_attn(d, b, (h * 2 + gq) * kHD + tq, ac / S, ep);
+  }
+
+  // Attention output value q of stream b: a counted vector (operand layout) or LL words.
+  __device__ __forceinline__ void store_attn(const AicasPhase& d, int b, int q, float v, uint32_t ep) {
+    if (d.flags & AICAS_F_CNT_OUT)
+      *reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(d.out) + cnt_off(q / 8, b) + (q % 8) * 2) =
+          __float2half_rn(v);
+    else
+      ll_store(reinterpret_cast<uint32_t*>(d.out) + (size_t)b * d.n + q, v, ep & 0xffffu);
   }
 
   __device__ __forceinline__ void run() {
@@ -1201,6 +1323,8 @@ struct Consumer {
     for (ph = 0; ph < a.n_phases; ++ph) {
       const AicasPhase& d = a.phases[ph];
       consumer_sync(kConsumerThreads);  // every warp is done with the previous phase's shared buffers
+      // every warp has written its part of the previous phase's counted vector
+      if (ph > 0 && tid == 0 && (a.phases[ph - 1].flags & AICAS_F_CNT_OUT)) red_release_add_u32(&bs->done[ph - 1], 1u);
       if (kTrace && tid == 0) trace_put(a, ph, 0, (int64_t)globaltimer_ns());
       if (d.kind == AICAS_PH_ATTN) {
         if (tid < 2 * kHD / 8) {
@@ -1221,10 +1345,12 @@ struct Consumer {
     if (lane == 0) mbar_arrive(&sm.cdone);
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
+      if (a.phases[a.n_phases - 1].flags & AICAS_F_CNT_OUT) red_release_add_u32(&bs->done[a.n_phases - 1], 1u);
       __threadfence();
       if (atomicAdd(&bs->exit_count, 1u) == (uint32_t)nct - 1) {
         bs->exit_count = 0;
         bs->epoch = epoch_base + (uint32_t)a.n_phases + 1;
+        bs->launches = bs->launches + 1u;
         __threadfence();
       }
     }
@@ -1300,6 +1426,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
   c.nb = a.nb;
   c.tmem = tmem;
   c.epoch_base = *reinterpret_cast<volatile uint32_t*>(&a.scratch->epoch);
+  c.cnt_target = (*reinterpret_cast<volatile uint32_t*>(&a.scratch->launches) + 1u) * (uint32_t)gridDim.x;
   c.run();
 }
 
@@ -1350,9 +1477,19 @@ static int setup(int* dev_out) {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+static int count_bits(int v) {
+  int c = 0;
+  for (; v; v &= v - 1) ++c;
+  return c;
+}
+
 static int validate(const AicasPhase& d) {
   constexpr int kUnsupported = AICAS_F_X_ADD | AICAS_F_RESID_ADD | AICAS_F_STORE_X | AICAS_F_BARRIER;
   if (d.flags & kUnsupported) return AICAS_ERR_ARG;
+  if (count_bits(d.flags & (AICAS_F_LL_IN | AICAS_F_CNT_IN | AICAS_F_X_EMBED)) > 1) return AICAS_ERR_ARG;
+  if (count_bits(d.flags & (AICAS_F_LL_OUT | AICAS_F_CNT_OUT)) > 1) return AICAS_ERR_ARG;
+  if (count_bits(d.flags & (AICAS_F_LL_RESID | AICAS_F_CNT_RESID | AICAS_F_RESID_EMBED)) > 1) return AICAS_ERR_ARG;
+  if ((d.flags & (AICAS_F_LL_IN | AICAS_F_CNT_IN)) && d.x_src < 0) return AICAS_ERR_ARG;
   switch (d.kind) {
     case AICAS_PH_GEMV:
     case AICAS_PH_GATEUP:
@@ -1369,14 +1506,15 @@ static int validate(const AicasPhase& d) {
       if ((d.flags & AICAS_F_RESID) && (!d.resid || !aligned16(d.resid))) return AICAS_ERR_ALIGN;
       if ((d.flags & AICAS_F_BIAS) && !d.bias) return AICAS_ERR_ARG;
       if (d.kind != AICAS_PH_LMHEAD) {
-        if (!(d.flags & AICAS_F_LL_OUT) || !d.out || !aligned16(d.out)) return AICAS_ERR_ARG;
+        if (!(d.flags & (AICAS_F_LL_OUT | AICAS_F_CNT_OUT)) || !d.out || !aligned16(d.out)) return AICAS_ERR_ARG;
       }
       return AICAS_OK;
     case AICAS_PH_ATTN:
       if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
       if (d.max_len < 1) return AICAS_ERR_SHAPE;
       if (d.k != (d.q_heads + 2 * d.kv_heads) * kHD || d.n != d.q_heads * kHD) return AICAS_ERR_SHAPE;
-      if ((d.flags & AICAS_F_Q_READY) || !(d.flags & AICAS_F_LL_IN) || !(d.flags & AICAS_F_LL_OUT) || d.x_src < 0)
+      if ((d.flags & AICAS_F_Q_READY) || !(d.flags & AICAS_F_LL_IN) ||
+          !(d.flags & (AICAS_F_LL_OUT | AICAS_F_CNT_OUT)) || d.x_src < 0)
         return AICAS_ERR_ARG;
       if (!d.k_cache || !d.v_cache || !aligned16(d.k_cache) || !aligned16(d.v_cache)) return AICAS_ERR_ALIGN;
       if (!d.x || !d.out || !aligned16(d.x) || !aligned16(d.out)) return AICAS_ERR_ALIGN;
@@ -1397,18 +1535,22 @@ extern "C" {
 AICAS_API size_t aicas_batch_scratch_bytes(void) { return sizeof(AicasBatchScratch); }
 
 AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n) {
-  if (!phases || n < 1) return AICAS_ERR_ARG;
+  if (!phases || n < 1 || n > AICAS_MAX_PHASES) return AICAS_ERR_ARG;
   for (int i = 0; i < n; ++i) {
     const int rc = bat::validate(phases[i]);
     if (rc) return rc;
-    if ((phases[i].flags & AICAS_F_LL_IN) && phases[i].x_src >= i) return AICAS_ERR_ARG;
+    const int f = phases[i].flags;
+    if ((f & (AICAS_F_LL_IN | AICAS_F_CNT_IN)) && phases[i].x_src >= i) return AICAS_ERR_ARG;
+    // an input's kind must match its source's output kind
+    if (f & AICAS_F_CNT_IN && !(phases[phases[i].x_src].flags & AICAS_F_CNT_OUT)) return AICAS_ERR_ARG;
+    if (f & AICAS_F_LL_IN && !(phases[phases[i].x_src].flags & AICAS_F_LL_OUT)) return AICAS_ERR_ARG;
   }
   return AICAS_OK;
 }
 
 static int launch_batch(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,
                         void* scratch, int64_t* trace, cudaStream_t stream) {
-  if (!device_phases || n_phases < 1 || !states || !scratch) return AICAS_ERR_ARG;
+  if (!device_phases || n_phases < 1 || n_phases > AICAS_MAX_PHASES || !states || !scratch) return AICAS_ERR_ARG;
   if (nb < 1 || nb > AICAS_MAX_BATCH) return AICAS_ERR_ARG;
   int dev;
   const int rc = bat::setup(&dev);

@@ -203,8 +203,12 @@ AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, in
  *     advances states[b] (out_tokens, script, EOS) like the batch-1 step.
  * A stream whose state has done_step != 0 is inactive: it is skipped (no KV
  * write, no state change); a launch with no active stream returns at once.
- * Scratch: aicas_batch_scratch_bytes() bytes (sizeof(AicasBatchScratch)),
- * zero-filled once, ordered launches only (as for the batch-1 scratch). */
+ * Activations may also be "counted" vectors (AICAS_F_CNT_*: plain fp16 in the
+ * operand layout [len/8][8 stream slots][8], one completion counter per
+ * phase).  Scratch: aicas_batch_scratch_bytes() bytes (sizeof(AicasBatchScratch)),
+ * zero-filled once, ordered launches only (as for the batch-1 scratch); the
+ * completion counters assume every launch on one scratch block runs the same
+ * phase list (zero the block again before switching to another). */
 AICAS_API size_t aicas_batch_scratch_bytes(void);
 AICAS_API int aicas_validate_batch_phases(const AicasPhase* phases, int n);
 AICAS_API int aicas_decode_batch_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* states, int nb,

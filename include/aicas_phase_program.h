@@ -40,6 +40,14 @@ enum AicasPhaseFlags {
   AICAS_F_LL_IN = 1 << 11,       // x is an LL vector written by phase `x_src` of this launch (see below)
   AICAS_F_LL_OUT = 1 << 12,      // out is an LL vector
   AICAS_F_LL_RESID = 1 << 13,    // resid is an LL vector (complete before this phase starts)
+  // Batched programs only (aicas_decode_batch_f16): "counted" vectors are plain
+  // fp16 in the batched operand layout [len/8][8 stream slots][8] (16 bytes per
+  // 8 values of one stream); the phase that writes one adds 1 to its
+  // per-phase completion counter once per CTA (release), and a reader waits
+  // until all CTAs have counted (acquire), then reads the whole vector once.
+  AICAS_F_CNT_IN = 1 << 14,      // x is a counted vector written by phase x_src of this launch
+  AICAS_F_CNT_OUT = 1 << 15,     // out is a counted vector
+  AICAS_F_CNT_RESID = 1 << 16,   // resid is a counted vector (complete before this phase starts)
 };
 
 // LL ("flag in data") vectors carry inter-phase activations without grid
@@ -131,6 +139,7 @@ typedef struct AicasScratch {
 // ("streams") per launch.  The first eight words are laid out exactly as in
 // AicasScratch (the grid barrier, epoch, error and exit words are shared code).
 #define AICAS_MAX_BATCH 8
+#define AICAS_MAX_PHASES 256
 
 typedef struct AicasBatchScratch {
   uint64_t bar_count;
@@ -140,6 +149,10 @@ typedef struct AicasBatchScratch {
   int32_t abort;
   uint32_t argmax_done;
   uint32_t exit_count;
+  uint32_t launches;                  // launches completed (advanced by the last CTA to exit)
+  uint32_t pad1;
+  uint32_t done[AICAS_MAX_PHASES];    // per phase: CTAs that finished writing its counted vector,
+                                      // (launches + 1) * grid once every CTA has (wraps modulo 2^32)
   float am_val[AICAS_MAX_CTAS][AICAS_MAX_BATCH];   // per-CTA best logit of each stream
   int32_t am_idx[AICAS_MAX_CTAS][AICAS_MAX_BATCH];
   // split-KV partials per (stream, KV head) merge group (64-bit LL words, as above)

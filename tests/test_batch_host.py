@@ -38,7 +38,9 @@ def test_tile_weight_rejects_bad_shapes():
 
 def test_batch_scratch_bytes():
     cta, b, heads, splits, hd = 256, 8, 8, 256, 128
-    assert _native.batch_scratch_bytes() == 32 + cta * b * 4 * 2 + b * heads * splits * 2 * (hd + 1) * 8
+    phases = 256
+    header = 32 + 8 + 4 * phases  # shared words, launch counter, per-phase completion counters
+    assert _native.batch_scratch_bytes() == header + cta * b * 4 * 2 + b * heads * splits * 2 * (hd + 1) * 8
 
 
 def _gemv(**kw):
@@ -83,3 +85,10 @@ def test_batch_validation_rules():
     assert _check(_gemv(), _attn(k=2048)) == 2  # x row length = q + k + v of a stream
     assert _check(_gemv(), _attn(flags=_native.F_LL_IN | _native.F_LL_OUT | _native.F_Q_READY)) == 1
     assert _check(_gemv(), _attn(q_heads=8)) == 2
+    # counted vectors: an input must come from a phase that writes one
+    cnt = _native.F_CNT_OUT
+    assert _check(_gemv(flags=cnt), _gemv(flags=cnt | _native.F_CNT_IN, x_src=0)) == 0
+    assert _check(_gemv(), _gemv(flags=cnt | _native.F_CNT_IN, x_src=0)) == 1  # source writes LL words
+    assert _check(_gemv(flags=cnt), _gemv(flags=_native.F_LL_OUT | _native.F_LL_IN, x_src=0)) == 1
+    assert _check(_gemv(flags=cnt | _native.F_LL_OUT)) == 1  # one output kind
+    assert _check(_gemv(), _attn(flags=_native.F_LL_IN | cnt)) == 0
