@@ -145,6 +145,7 @@ struct __align__(128) Smem {
   uint64_t xready;  // the A operand of the next GEMV phase is in shared memory
   uint64_t cdone;   // all consumer warps are done with TMEM
   uint64_t mdone;   // every MMA the issuer launched has completed
+  uint64_t xfull;   // a counted input has landed in the operand buffer (bulk copies)
   uint32_t ring_it;
   uint32_t tmem_base;
   int32_t last_cta;
@@ -536,6 +537,7 @@ struct Consumer {
   uint32_t tmem;
   uint32_t epoch_base;
   uint32_t cnt_target = 0;  // completion count of a counted vector in this launch: (launches + 1) * grid
+  uint32_t xfull_n = 0;     // completions of sm.xfull so far
   uint32_t gc = 0;   // accumulator groups consumed (epilogue warps)
   uint32_t rit = 0;  // ring tiles passed (GEMV tiles via the MMA warp, attention tiles read in place)
   int ph = 0;
@@ -653,16 +655,29 @@ struct Consumer {
     const int k = d.k;
     const int b = tid & 7;
     const bool act = active(b);
-    if (tid == 0) wait_count(&bs->done[d.x_src], cnt_target, s);
-    consumer_sync(kConsumerThreads);
-    const uint4* src = reinterpret_cast<const uint4*>(d.x);
+    // thread 0: wait for the count, then copy the whole vector (8 streams x k
+    // values, k / 2048 pieces of 32 KB) with bulk async copies; the other
+    // threads wait for the copies to land.  The fence orders the acquired
+    // generic-proxy data before the copies' async-proxy reads.
+    if (tid == 0) {
+      wait_count(&bs->done[d.x_src], cnt_target, s);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      const int pieces = k / kChunk;
+      mbar_arrive_expect_tx(&sm.xfull, pieces * kTileBytes);
+      for (int c = 0; c < pieces; ++c)
+        bulk_g2s(sm.xa + c * kTileBytes, reinterpret_cast<const uint8_t*>(d.x) + (size_t)c * kTileBytes, kTileBytes,
+                 &sm.xfull, l2_evict_last_policy());
+    }
+    mbar_wait_bounded(&sm.xfull, xfull_n & 1u, s, kErrFullTimeout);
+    ++xfull_n;
+    const uint4* src = reinterpret_cast<const uint4*>(sm.xa);
     uint4* dst = reinterpret_cast<uint4*>(sm.xa);
     if (d.flags & AICAS_F_NORM) {  // k == 2048: 8 pieces per thread
       uint4 raw[8];
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        raw[i] = act ? ldcg_u4(src + tid + kConsumerThreads * i) : make_uint4(0, 0, 0, 0);
+        raw[i] = act ? src[tid + kConsumerThreads * i] : make_uint4(0, 0, 0, 0);
         const __half2* hp = reinterpret_cast<const __half2*>(&raw[i]);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -693,9 +708,9 @@ struct Consumer {
         }
         dst[tid + kConsumerThreads * i] = act ? raw[i] : make_uint4(0, 0, 0, 0);
       }
-    } else {
+    } else if (!act) {  // streams that are not running read as zeros
       const int pieces = k;  // 8 streams x k values x 2 bytes / 16
-      for (int i = tid; i < pieces; i += kConsumerThreads) dst[i] = act ? ldcg_u4(src + i) : make_uint4(0, 0, 0, 0);
+      for (int i = tid; i < pieces; i += kConsumerThreads) dst[i] = make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async_smem();
     consumer_sync(kConsumerThreads);
@@ -1390,6 +1405,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
     mbar_init(&sm.xready, 1);
     mbar_init(&sm.cdone, kConsumerWarps);
     mbar_init(&sm.mdone, 1);
+    mbar_init(&sm.xfull, 1);
     sm.ring_it = 0;
     sm.last_cta = 0;
     mbar_fence_init();
