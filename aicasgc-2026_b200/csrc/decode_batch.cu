@@ -761,20 +761,21 @@ struct Consumer {
         const int buf = (gc >> 1) & 1;
         mbar_wait_bounded(&sm.dfull[slot], (gc >> 1) & 1u, s, kErrTmemTimeout);
         tc_fence_after();
-        uint32_t v[2][32];
-        tmem_ld_32x32b_x32(tq + slot * kDSlotCols, v[0]);
-        if (gu) tmem_ld_32x32b_x32(tq + slot * kDSlotCols + kDCols, v[1]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.dempty[slot]);
-#pragma unroll
-        for (int p2 = 0; p2 < 2; ++p2) {
-          if (p2 == 1 && !gu) break;
+        // one part (gate, then up) at a time: 32 accumulator registers live
+#pragma unroll 1
+        for (int p2 = 0; p2 < (gu ? 2 : 1); ++p2) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tq + slot * kDSlotCols + p2 * kDCols, v);
+          tmem_wait_ld();
+          if (p2 == (gu ? 1 : 0)) {  // the slot's last read: release it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.dempty[slot]);
+          }
           float part[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {  // the diagonal block's column of stream j
-            const uint32_t x0 = v[p2][j], x1 = v[p2][8 + j], x2 = v[p2][16 + j], x3 = v[p2][24 + j];
+            const uint32_t x0 = v[j], x1 = v[8 + j], x2 = v[16 + j], x3 = v[24 + j];
             part[j] = __uint_as_float(sub == 0 ? x0 : sub == 1 ? x1 : sub == 2 ? x2 : x3);
           }
 #pragma unroll
