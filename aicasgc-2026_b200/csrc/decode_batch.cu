@@ -9,40 +9,47 @@
 //
 //   warp 0      producer: the CTA's weight / KV tiles, phase after phase, into
 //               a 3-stage shared-memory ring (cp.async.bulk, L2 evict_first).
-//   warps 1..8  consumers: per GEMV phase, poll the input rows of every active
-//               stream (LL flag-in-data words), apply the RMSNorm prologue
-//               with HF's fp16 rounding points and write the A operand
-//               (streams x k, fp16) into shared memory; then two of them (the
-//               warps whose TMEM lane quarter holds accumulator rows 0..31)
-//               run the epilogues.  Attention: the split-KV units of all
-//               streams, as in the batch-1 kernel.
+//   warps 1..8  consumers.  GEMV phases: build the streams' operand in shared
+//               memory (a counted input lands there by bulk copies; the
+//               layer-0 embedding rows and LL inputs are loaded or polled),
+//               with the RMSNorm prologue at HF's fp16 rounding points; then
+//               two sets of 4 warps (one warp per TMEM lane quarter each) run
+//               the epilogues of alternate row groups.  Attention: the
+//               split-KV units of all streams, tiles taken in pairs.
 //   warp 9      L2 prefetch cursor, kL2Ahead tiles ahead of the ring.
-//   warp 10     MMA issuer and TMEM owner: per 32 KB weight tile (8 rows x
-//               2048 columns) 128 x tcgen05.mma.kind::f16 with M = 64 (the A
-//               operand's 8 stream rows, repeated: its 8-row groups share one
-//               address), N = 8 (the tile's weight rows), K = 16, accumulating
-//               fp32 in a 16-column TMEM slot (gate_up: gate in columns 0..7,
-//               up in 8..15; down_proj: the 3 K-chunks of a row group into
-//               the same columns).  One tcgen05.commit frees the ring stage
-//               when the tile's MMAs are done, another marks the slot full.
+//   warp 10     MMA issuer and TMEM owner (below).
 //
-// Weight tile layout (aicas_tile_weight_f16): the 8 x 2048 block is stored
-// as [256 column groups][8 rows][8 columns], the K-major no-swizzle canonical
-// layout of the tcgen05 shared-memory descriptor (8-row x 16-byte core
-// matrices, K-adjacent core matrices 128 bytes apart), so one bulk copy lands
-// a tile ready for the tensor core.  The A operand uses the same layout with
-// the 8 streams as rows.
+// Weight tile layout (aicas_tile_weight_f16): an 8-row x 2048-column block
+// (32 KB) is stored as [256 column groups][8 rows][8 columns], the K-major
+// no-swizzle canonical layout of the tcgen05 shared-memory descriptor (8-row x
+// 16-byte core matrices), so one bulk copy lands a tile ready for the tensor
+// core.  The streams' operand has the same layout with the 8 streams as rows.
 //
-// Accumulator layout (M = 64, cta_group::1): row i of D sits in TMEM lane
-// (i % 16) + 32 (i / 16); rows 0..7 are the streams, so a warp of lane
-// quarter 0 reads stream b's 8 (or 16) sums in lane b with one tcgen05.ld.
+// Block-pair MMA: the tile is read as a 128 x 128 operand A whose row
+// (block j, weight row r) is columns 128 j .. 128 j + 127 of row r (8-row
+// core-matrix groups 2 KB apart), and the streams' chunk as B with rows
+// (block j', stream s).  8 tcgen05.mma.kind::f16 (M = 128, N = 128, K = 16)
+// per tile accumulate fp32 D[(j, r)][(j', s)] in TMEM; the epilogue keeps the
+// 16 diagonal blocks j == j': the warp of lane quarter q reads its 4 blocks'
+// 32 columns (one tcgen05.ld.32x32b.x32 per part), sums its blocks with
+// shuffles, and the set's leader warp adds the 4 quarters in a fixed order
+// and applies bias / residual / SiLU / rounding (gate_up: gate and up in the
+// two halves of a 256-column slot; down_proj: its 3 K chunks accumulate in
+// the same columns).  A tcgen05.commit frees the ring stage when a tile's
+// MMAs are done, another marks the slot full.
+//
+// Activations: qkv is an LL vector (each attention CTA polls only its heads'
+// columns); attn, h_mid, act and h are counted vectors (AICAS_F_CNT_*): plain
+// fp16 in the operand layout, one release add per CTA and phase on a
+// completion counter, one acquire wait and a bulk copy per reader.
 //
 // Attention: units (stream, KV head, 64-slot chunk) over all active streams,
-// split contiguously over the CTAs; each (stream, head) merge group is
-// combined from its CTAs' (log-sum-exp, acc) partials in a fixed split order,
-// exactly as in the batch-1 kernel.  Every wait is bounded
-// (aicas_device.cuh); after a failed wait the kernel keeps walking the same
-// program without waiting and ends with the error recorded.
+// split contiguously over the CTAs.  A segment's tiles go in pairs (warps 0..3
+// and 4..7, 16 positions per warp); each CTA first stores the (log-sum-exp,
+// acc) partials of all its segments, then merges its slice of every group it
+// shares, in a fixed split order.  Every wait is bounded (aicas_device.cuh);
+// after a failed wait the kernel keeps walking the same program without
+// waiting and ends with the error recorded.
 //
 // Reference behaviour per stream (file:line in the reference checkout) is
 // that of the batch-1 step: decode_gemv_kernel_fused.cuh:99-185 and
@@ -128,7 +135,7 @@ struct AttnSmem {
 
 struct __align__(128) Smem {
   uint8_t ring[kStages][kTileBytes];
-  uint8_t xa[kMaxC * kTileBytes];  // A operand: [k/8 column groups][8 streams][8] fp16
+  uint8_t xa[kMaxC * kTileBytes];  // the streams' operand (MMA B): [k/8 column groups][8 streams][8] fp16
   AttnSmem at;
   float rope_c[kMaxB][kHD / 2], rope_s[kMaxB][kHD / 2];
   float ssq[kConsumerWarps][kMaxB];
@@ -142,7 +149,7 @@ struct __align__(128) Smem {
   uint64_t cempty[kStages];
   uint64_t dfull[kDSlots];
   uint64_t dempty[kDSlots];
-  uint64_t xready;  // the A operand of the next GEMV phase is in shared memory
+  uint64_t xready;  // the streams' operand of the next GEMV phase is in shared memory
   uint64_t cdone;   // all consumer warps are done with TMEM
   uint64_t mdone;   // every MMA the issuer launched has completed
   uint64_t xfull;   // a counted input has landed in the operand buffer (bulk copies)
@@ -449,7 +456,7 @@ __device__ __forceinline__ void run_l2_prefetcher(const BatchArgs& a, Smem& sm, 
 }
 
 // MMA issuer (lane 0 of the last warp; the whole warp owns the TMEM
-// allocation).  GEMV tiles: wait for the phase's A operand (once per phase),
+// allocation).  GEMV tiles: wait for the phase's streams' operand (once per phase),
 // a free accumulator slot (first tile of a row group) and the landed tile,
 // issue the tile's 128 MMAs, commit the stage (and the slot at the group's
 // last tile).  Attention tiles: pass the consumers' in-place release on to
@@ -569,7 +576,7 @@ struct Consumer {
     }
   }
 
-  // The A operand of a GEMV phase: thread (b = tid % 8, g = tid / 8) takes
+  // The streams' operand of a GEMV phase: thread (b = tid % 8, g = tid / 8) takes
   // column groups v = g + 32 i of stream b (8 columns each), so the 8 lanes
   // of a lane octet write one contiguous 128-byte core-matrix row set.
   // RMSNorm (F_NORM, k == 2048) with HF's rounding points
@@ -649,7 +656,7 @@ struct Consumer {
 
   // A counted input: wait until every CTA has written its part, then copy the
   // vector (already in the operand layout: piece i = 16 bytes of stream i % 8)
-  // into the A operand, applying the RMSNorm prologue (k == 2048) on the way.
+  // into the streams' operand, applying the RMSNorm prologue (k == 2048) on the way.
   // Thread tid copies pieces tid, tid + 256, ...: all of stream tid % 8.
   __device__ __forceinline__ void build_x_counted(const AicasPhase& d) {
     const int k = d.k;
@@ -877,7 +884,7 @@ struct Consumer {
     if (lm) finish_argmax(best_v, best_i);
   }
 
-  // Per stream: the best (value, row) of the two epilogue warps, then of all
+  // Per stream: the best (value, row) of the two sets' leader warps, then of all
   // CTAs (the last CTA to arrive reduces, one warp per stream, and advances
   // the stream's step state exactly like the batch-1 kernel).
   __device__ __forceinline__ void finish_argmax(float bv, int bi) {
@@ -1569,7 +1576,7 @@ static int launch_batch(const AicasPhase* device_phases, int n_phases, AicasStep
                         void* scratch, int64_t* trace, cudaStream_t stream) {
   if (!device_phases || n_phases < 1 || n_phases > AICAS_MAX_PHASES || !states || !scratch) return AICAS_ERR_ARG;
   if (nb < 1 || nb > AICAS_MAX_BATCH) return AICAS_ERR_ARG;
-  int dev;
+  int dev = 0;
   const int rc = bat::setup(&dev);
   if (rc) return rc;
   bat::BatchArgs a;
