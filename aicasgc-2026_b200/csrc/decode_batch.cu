@@ -1249,7 +1249,7 @@ struct Consumer {
   // each output by a group of tpo lanes (a power of two <= 16), lane `sub` of
   // the group polling splits sub, sub + tpo, ... kMergePer at a time, then a
   // fixed xor-shuffle tree combines the lanes' (max, sum, acc) triples.
-  __device__ __noinline__ void merge_group(const AicasPhase& d, int b, int h, int split, int nsplit, uint32_t ep) {
+  __device__ __forceinline__ void merge_group(const AicasPhase& d, int b, int h, int split, int nsplit, uint32_t ep) {
     uint64_t* const hp = &bs->part[b * d.kv_heads + h][0][0][0];
     constexpr int kSplitStride = 2 * (kHD + 1);
     const int q0 = split * 2 * kHD / nsplit, q1 = (split + 1) * 2 * kHD / nsplit;
