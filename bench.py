@@ -203,9 +203,9 @@ def job_throughput(steps: int, world: int, ms: float) -> float:
 # --------------------------------------------------------------------------- GPU
 # DRAM bytes per algorithmic byte of decode_program_kernel, from one
 # `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
-# summarised under profiles/): (1.043547e9 + 10.083584e6) / 1043908608.  The
+# summarised under profiles/): (1.043518e9 + 10.825984e6) / 1043908608.  The
 # per-layer shapes equal the headline model's, so the ratio carries over.
-DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0093131
+DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0099955
 
 def run_ours(args, rank: int, world: int):
     import torch
@@ -230,21 +230,10 @@ def run_ours(args, rank: int, world: int):
                               max_steps=PREFIX + NEW + 8)
     pos3, _ = vision_grid_positions(PREFIX)
     prompt = synthetic_prompt(PREFIX, seed=1234 + rank)
-    # time to first token of the prefix (not part of the decode metric): the
-    # one-pass prefill (prefill.py) after a warm-up, and the one-token-per-
-    # launch prefill through the decode kernel that the bench then uses
-    for _ in range(2):
-        eng.prefill_prompt(prompt, pos3)
-    torch.cuda.synchronize(dev)
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record()
-    for _ in range(3):
-        eng.prefill_prompt(prompt, pos3)
-    p1.record()
-    torch.cuda.synchronize(dev)
-    ttft_gemm_ms = p0.elapsed_time(p1) / 3
-    # prefill: one forced step per prefix token (not timed in the metric)
+    # prefill: one forced step per prefix token (not timed in the metric; its
+    # time is the decode-kernel time to first token reported below)
     eng.load_script(prompt, pos3)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record()
     eng.launch(PREFIX)
     p1.record()
@@ -308,6 +297,19 @@ def run_ours(args, rank: int, world: int):
     if args.trace and rank == 0:
         write_trace_summary(eng, start_state, args.trace)
 
+    # time to first token of the prefix with the one-pass prefill (prefill.py),
+    # after a warm-up; measured last, so the launches before the timed region
+    # are the same as without it (it rewrites the prefix's cache slots)
+    for _ in range(2):
+        eng.prefill_prompt(prompt, pos3)
+    torch.cuda.synchronize(dev)
+    p0.record()
+    for _ in range(3):
+        eng.prefill_prompt(prompt, pos3)
+    p1.record()
+    torch.cuda.synchronize(dev)
+    ttft_gemm_ms = p0.elapsed_time(p1) / 3
+
     # ---- max over ranks
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], world)
     value = job_throughput(args.steps, world, ms)
@@ -327,7 +329,7 @@ def run_ours(args, rank: int, world: int):
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_req / NEW,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 4-layer "
-                                       "launch (1.0435 GB + 10.1 MB vs 1.0439 GB algorithmic), scaled to this "
+                                       "launch (1.0435 GB + 10.8 MB vs 1.0439 GB algorithmic), scaled to this "
                                        "launch by algorithmic bytes",
                      "kernel": "decode_program_kernel (one launch per token)",
                      "algorithmic_bytes_per_launch": bytes_req / NEW},
