@@ -205,7 +205,7 @@ def job_throughput(steps: int, world: int, ms: float) -> float:
 # `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
 # summarised under profiles/): (1.043518e9 + 10.825984e6) / 1043908608.  The
 # per-layer shapes equal the headline model's, so the ratio carries over.
-DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0099955
+DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0099964
 
 def run_ours(args, rank: int, world: int):
     import torch
