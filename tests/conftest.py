@@ -3,7 +3,6 @@
 Tests marked `gpu` need a CUDA device (B200) and the built
 `libaicas_decode.so`; everything else runs on the CPU.
 """
-import os
 import sys
 from pathlib import Path
 

@@ -4,7 +4,6 @@ struct layouts match the Python mirrors.  No kernel is launched."""
 import re
 from pathlib import Path
 
-import pytest
 
 import _native
 
