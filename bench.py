@@ -166,14 +166,15 @@ def run_reference(args, rank: int, world: int):
     tps_w, _, _ = cpu_oracle_decode(st, seconds=0.0, min_steps=max(1, args.warmup), max_steps=max(1, args.warmup))
     tps, n, el = cpu_oracle_decode(st, seconds=0.0, min_steps=args.steps, max_steps=args.steps)
     sample = f"{n} decode tokens at cache slot {PREFIX}+ over a synthetic 1024-slot KV prefix (numpy fp32 port)"
-    metric = METRIC
+    metric, config = METRIC, workload_config(world)
     if args.batch > 1:  # the reference decodes one request at a time: its batched rate is its per-token rate
         metric = f"batch-{args.batch} decode tok/s"
+        config = batch_workload_config(args.batch, batch_contexts(args.batch, rank), world)
         sample += "; the reference serves one request per engine, so requests run one after another"
     line = {
         "impl": "reference", "metric": metric, "value": tps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * el / n, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(world),
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference arm: CPU oracle port of the reference's HF decode step; a step here is one token",
@@ -355,6 +356,15 @@ def run_ours(args, rank: int, world: int):
 
 
 BATCH_NEW = 512  # decode steps per stream per bench step (config 5)
+
+
+def batch_workload_config(batch: int, ctx: list, n_gpus: int) -> dict:
+    return {"workload": f"BASELINE config 5 per GPU: Qwen3-VL-2B text decoder, 28 layers fp16, {batch} ragged "
+                        f"requests (contexts {ctx}, U[512, 4096] seeded), {BATCH_NEW} greedy decode steps "
+                        f"per request per bench step, one batched launch per step, CUDA graph",
+            "model": "Qwen3-VL-2B text decoder (random init N(0,0.02))", "batch": batch,
+            "contexts": ctx, "decode_steps_per_request": BATCH_NEW, "parallelism": f"request-dp{n_gpus}",
+            "l2": "inputs larger than L2: 3.44 GB of weights + the requests' KV streamed per step"}
 # DRAM bytes per algorithmic byte of decode_batch_kernel, from one `ncu --set
 # full` capture of the 2-layer batch-8 profiling case (bench.py --batch 8
 # --layers 2; summarised under profiles/): (983.835392e6 + 21.94944e6) /
@@ -468,12 +478,7 @@ def run_batch(args, rank: int, world: int):
         "metric": f"batch-{B} decode tok/s", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": f"BASELINE config 5 per GPU: Qwen3-VL-2B text decoder, 28 layers fp16, {B} ragged "
-                               f"requests (contexts {ctx}, U[512, 4096] seeded), {BATCH_NEW} greedy decode steps "
-                               f"per request per bench step, one batched launch per step, CUDA graph",
-                   "model": "Qwen3-VL-2B text decoder (random init N(0,0.02))", "batch": B,
-                   "contexts": ctx, "decode_steps_per_request": BATCH_NEW, "parallelism": f"request-dp{world}",
-                   "l2": "inputs larger than L2: 3.44 GB of weights + the requests' KV streamed per step"},
+        "config": batch_workload_config(B, ctx, world),
         "us_per_batched_step": 1000.0 * ms / (args.steps * BATCH_NEW),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
