@@ -92,3 +92,38 @@ def test_batch_validation_rules():
     assert _check(_gemv(flags=cnt), _gemv(flags=_native.F_LL_OUT | _native.F_LL_IN, x_src=0)) == 1
     assert _check(_gemv(flags=cnt | _native.F_LL_OUT)) == 1  # one output kind
     assert _check(_gemv(), _attn(flags=_native.F_LL_IN | cnt)) == 0
+
+
+def _operand(buf: np.ndarray, base: int, rows: int, lbo: int, sbo: int) -> np.ndarray:
+    """The [rows x 16] fp16 matrix a K-major no-swizzle shared-memory
+    descriptor (start `base` bytes into `buf`, K-adjacent core matrices `lbo`
+    bytes apart, 8-row groups `sbo` bytes apart) hands the tensor core for one
+    K = 16 step: element (m, k) at base + (m / 8) sbo + (k / 8) lbo + (m % 8) 16 + (k % 8) 2."""
+    m = np.arange(rows)[:, None]
+    k = np.arange(16)[None, :]
+    addr = base + (m // 8) * sbo + (k // 8) * lbo + (m % 8) * 16 + (k % 8) * 2
+    return buf[addr // 2]
+
+
+def test_block_pair_mma_reproduces_the_projection():
+    """Emulates, in numpy, how decode_batch.cu's tensor cores read one weight
+    tile and the streams' operand: 8 K steps of M = 128, N = 128, K = 16 with
+    the tile and the operand described as canonical K-major layouts (LBO =
+    128 B, SBO = 2 KB, 256 bytes per K step), accumulating D[(j, r)][(j', s)];
+    the sum of D's 16 diagonal blocks j == j' must be the tile's 8 rows times
+    the 8 streams (W x^T)."""
+    g = torch.Generator().manual_seed(7)
+    w = torch.randn(8, 2048, generator=g).half()
+    x = torch.randn(8, 2048, generator=g).half()  # 8 streams
+    tile = tile_weight(w).reshape(-1).numpy()      # one 32 KB tile, the kernel's ring stage
+    xa = tile_weight(x).reshape(-1).numpy()        # the streams' operand uses the same layout
+    d = np.zeros((128, 128), dtype=np.float64)
+    for ks in range(8):
+        a = _operand(tile, 256 * ks, 128, 128, 2048).astype(np.float64)
+        b = _operand(xa, 256 * ks, 128, 128, 2048).astype(np.float64)
+        d += a @ b.T
+    out = sum(d[8 * j:8 * j + 8, 8 * j:8 * j + 8] for j in range(16))  # rows r, columns s
+    ref = w.double().numpy() @ x.double().numpy().T
+    np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-9)
+    # the off-diagonal blocks are the products the epilogue discards
+    assert np.abs(d[0:8, 8:16]).max() > 0
