@@ -71,3 +71,18 @@ def test_reference_arm_runs_on_rank0_only(capsys):
     args = argparse.Namespace(steps=1, warmup=1)
     bench.run_reference(args, rank=1, world=2)  # other ranks exit without work
     assert capsys.readouterr().out == ""
+
+
+def test_batch_workload_is_seeded_and_in_range():
+    """Config 5's per-request contexts: drawn from U[512, 4096] with a
+    rank-dependent seed (the same on every run), and both bench arms describe
+    the same workload."""
+    import bench
+
+    c0 = bench.batch_contexts(8, 0)
+    assert c0 == bench.batch_contexts(8, 0)
+    assert c0 != bench.batch_contexts(8, 1)  # each rank decodes its own requests
+    assert len(c0) == 8 and all(512 <= c <= 4096 for c in c0)
+    cfg = bench.batch_workload_config(8, c0, 2)
+    assert cfg["contexts"] == c0 and cfg["batch"] == 8 and cfg["parallelism"] == "request-dp2"
+    assert "config 5" in cfg["workload"] and cfg["decode_steps_per_request"] == bench.BATCH_NEW
