@@ -12,6 +12,10 @@ modeling_qwen3_vl.py:398-403, q/k-norm + interleaved MRoPE :352-386 and
 :427-431, SiLU-gated MLP :553-563, residual adds).  K and V land in the
 engine's cache layout [L, 1, kv_heads, max_len, head_dim] at slots [0, P).
 
+Both engines call it with CUDA tensors only; the CPU branch of `_linear` / `_down`
+exists for the CPU parity test against the oracle's prefill (tests/test_prefill.py),
+not as a fallback of the GPU path.
+
 Weights come in the engine's fused per-layer layout: qkv [4096, 2048] (q
 rows, then k, then v), o [2048, 2048], gate_up [12288, 2048] (gate rows
 first), down either [2048, 6144] or K-blocked [3, 2048, 2048] (block c holds
