@@ -178,6 +178,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Bounded wait for a bulk copy this CTA issued from valid memory: the abort
+// word does not end it (the copy lands in microseconds either way), so the
+// barrier's phases stay in step and no copy is still writing shared memory
+// when the CTA moves on or exits.  False only on the time limit.
+__device__ __forceinline__ bool mbar_wait_copy(uint64_t* bar, uint32_t parity, AicasScratch* s, int err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(s, err);
+      return false;
+    }
+  }
+}
+
 // Bounded wait on the mbarrier at shared address `bar` (see mbar_wait_bounded).
 __device__ __forceinline__ bool mbar_wait_bounded_s(uint32_t bar, uint32_t parity, AicasScratch* s, int err) {
   if (mbar_try_wait_s(bar, parity)) return true;

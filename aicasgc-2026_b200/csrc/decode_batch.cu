@@ -675,7 +675,7 @@ struct Consumer {
         bulk_g2s(sm.xa + c * kTileBytes, reinterpret_cast<const uint8_t*>(d.x) + (size_t)c * kTileBytes, kTileBytes,
                  &sm.xfull, l2_evict_last_policy());
     }
-    mbar_wait_bounded(&sm.xfull, xfull_n & 1u, s, kErrFullTimeout);
+    mbar_wait_copy(&sm.xfull, xfull_n & 1u, s, kErrFullTimeout);
     ++xfull_n;
     const uint4* src = reinterpret_cast<const uint4*>(sm.xa);
     uint4* dst = reinterpret_cast<uint4*>(sm.xa);
