@@ -503,6 +503,9 @@ __device__ __forceinline__ void run_mma(const BatchArgs& a, Smem& sm, AicasScrat
           ++gc;
         }
       } else {
+        // the stage goes back to the producer only once its copy has landed
+        // (after an abort a consumer may release it without having waited)
+        if (!mbar_wait_bounded(&sm.full[st], par, s, kErrFullTimeout)) break;
         if (!mbar_wait_bounded(&sm.cempty[st], (cpar >> st) & 1u, s, kErrEmptyTimeout)) break;
         cpar ^= 1u << st;
         mbar_arrive(&sm.empty[st]);

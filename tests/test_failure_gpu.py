@@ -10,7 +10,8 @@ with an error code in the scratch block, and the context stays usable:
   correctly again;
 * a cache slot outside the cache: the attention phase raises kErrBadInput
   instead of reading or writing past the cache, the engine reports it and
-  resets its device state, and the next request decodes exactly as before.
+  resets its device state, and the next request decodes exactly as before;
+  the batched engine does the same when one of its streams has such a slot.
 """
 import ctypes
 import time
@@ -21,6 +22,7 @@ import torch
 
 from _native import F_LL_IN, F_LL_OUT, PH_GEMV, AicasError, AicasPhase, AicasStepState, check, lib, scratch_bytes
 from _ops import device_error
+from batch_engine import Qwen3VLBatchDecodeEngine
 from engine import Qwen3VLDecodeEngine
 from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state
 
@@ -85,3 +87,23 @@ def test_cache_slot_outside_the_cache_is_reported_not_used(cuda_device):
     assert torch.equal(eng.k_cache, kv[0]) and torch.equal(eng.v_cache, kv[1])
     again = eng.generate(prompt, 8)
     assert torch.equal(again, ref)
+
+
+def test_batched_stream_with_a_slot_outside_the_cache_is_reported_not_used(cuda_device):
+    shape = QWEN3VL_2B.with_layers(2)
+    st = synthetic_state(shape, seed=0)
+    eng = Qwen3VLBatchDecodeEngine(st, shape, max_batch=3, max_cache_len=64, max_steps=128)
+    prompts = [synthetic_prompt(n, seed=sd).numpy() for n, sd in ((20, 9), (7, 10), (33, 11))]
+    ref = eng.generate_batch(prompts, 8)
+    kv1 = (eng.k_cache[:, 1].clone(), eng.v_cache[:, 1].clone())
+    start = torch.tensor([[int(ref[b][0]), len(prompts[b])] + [len(prompts[b])] * 3 for b in range(3)],
+                         dtype=torch.int64)
+    start[1, 1] = eng.max_cache_len  # stream 1: slot == cache length
+    eng.decode_host(start, 1, graph_steps=1)
+    with pytest.raises(AicasError, match="device error 15"):
+        eng.check_error()
+    # nothing was written into stream 1's cache
+    assert torch.equal(eng.k_cache[:, 1], kv1[0]) and torch.equal(eng.v_cache[:, 1], kv1[1])
+    again = eng.generate_batch(prompts, 8)
+    for b in range(3):
+        assert torch.equal(again[b], ref[b]), b
