@@ -430,9 +430,6 @@ __device__ __forceinline__ void run_mover(const ProgramArgs& a, Smem& sm, const 
         tcgen05_commit(&sm.empty[st]);
         ++g;
       } else {
-        // the stage goes back to the producer only once its copy has landed
-        // (after an abort a consumer may release it without having waited)
-        if (!mbar_wait_bounded(&sm.full[st], par, s, kErrFullTimeout)) break;
         if (!mbar_wait_bounded(&sm.cempty[st], (cpar >> st) & 1u, s, kErrEmptyTimeout)) break;
         cpar ^= 1u << st;
         mbar_arrive(&sm.empty[st]);
