@@ -13,17 +13,22 @@ import torch
 from _native import (DEVICE_ERRORS, SCRATCH_ERROR_OFFSET, AicasError, check, lib,
                      scratch_bytes)
 
-_scratch: dict[int, torch.Tensor] = {}
+_scratch: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def scratch_for(device: torch.device) -> torch.Tensor:
-    """The default scratch block of `device` (zero-filled once, reused by
-    every op on that device; ops must be ordered on one stream)."""
+    """The scratch block of `device`'s current stream (zero-filled once,
+    reused by every op issued on that stream).  One block per stream: ops on
+    one stream are ordered, so they never share a block concurrently, and ops
+    on two streams never share one at all.  A device error recorded in a
+    block makes every later op on that stream do nothing until
+    `raise_if_device_error` (which zeroes the block) is called."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _scratch.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    t = _scratch.get(key)
     if t is None:
         t = torch.zeros(scratch_bytes(), dtype=torch.uint8, device=torch.device("cuda", idx))
-        _scratch[idx] = t
+        _scratch[key] = t
     return t
 
 

@@ -1388,6 +1388,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   AicasScratch* s = reinterpret_cast<AicasScratch*>(a.scratch);
+  // A scratch block that still holds a device error from an earlier launch
+  // refuses the launch (nothing is read, written or advanced) until the
+  // caller zeroes it.
+  if (ld_volatile_int(&s->error) != 0) return;
   if (threadIdx.x < kMaxB) {
     const int b = threadIdx.x;
     StreamIn in{};

@@ -57,6 +57,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "aicas_device.cuh"
 #include "aicas_phase_program.h"
 
@@ -475,13 +477,23 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
     int good = 1;
     if (lane == 0) {
       if (r.round() > 0) {
+        const uint32_t prev = (r.round() - 1) & 1u;
         if (kTrace) {
           const uint64_t t0 = globaltimer_ns();
-          good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+          good = mbar_wait_bounded(&sm.empty[st], prev, s, kErrEmptyTimeout);
           slot_wait += globaltimer_ns() - t0;
         } else {
-          good = mbar_wait_bounded(&sm.empty[st], (r.round() - 1) & 1u, s, kErrEmptyTimeout);
+          good = mbar_wait_bounded(&sm.empty[st], prev, s, kErrEmptyTimeout);
         }
+        // The stage's previous copy has landed before the stage is armed
+        // again.  In-place stages (attention, partial chunks) are released by
+        // the consumers' arrivals alone, and after an abort a consumer may
+        // arrive without having waited for the copy; this wait (which ignores
+        // the abort word and normally succeeds at once) keeps a second copy
+        // from being issued into a stage that is still being written, so
+        // every phase of full[st] completes once per copy and the drain
+        // below sees each of them.
+        if (good) good = mbar_wait_copy(&sm.full[st], prev, s, kErrDrainTimeout);
       }
       if (good) {
         mbar_arrive_expect_tx(&sm.full[st], td.pieces * td.bytes);
@@ -1519,6 +1531,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
   // thread reads the same word, so the whole grid returns before any barrier,
   // TMEM allocation or copy)
   if (a.state && *reinterpret_cast<const volatile int64_t*>(&a.state->done_step) != 0) return;
+  // A scratch block that still holds a device error from an earlier launch
+  // refuses the launch: nothing is read, written or advanced until the caller
+  // zeroes the block (an aborted launch leaves its barriers, counters and
+  // vectors in an unknown state).
+  if (ld_volatile_int(&a.scratch->error) != 0) return;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);
@@ -1924,7 +1941,11 @@ AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const 
 // looked up once per device with cudaGetSymbolAddress.
 namespace aicas {
 static __device__ __align__(256) AicasScratch g_noalloc_scratch;
-static AicasScratch* g_noalloc_scratch_ptr[kMaxDevices];
+// Device address of g_noalloc_scratch per device, filled on the first call
+// there.  Atomic: host threads may call concurrently (two threads that both
+// look it up store the same address).  A device reset invalidates it; the
+// library must then be reloaded.
+static std::atomic<AicasScratch*> g_noalloc_scratch_ptr[kMaxDevices];
 }  // namespace aicas
 
 extern "C" AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, const void* k_cache,
@@ -1941,11 +1962,11 @@ extern "C" AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, co
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
-  AicasScratch* scr = g_noalloc_scratch_ptr[dev];
+  AicasScratch* scr = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
   if (!scr) {  // first call on this device: resolve the array's device address
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&scr), g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e);
-    g_noalloc_scratch_ptr[dev] = scr;
+    g_noalloc_scratch_ptr[dev].store(scr, std::memory_order_release);
   }
   // The array keeps the previous call's contents: zero the words a launch
   // expects to start at zero (error, abort and counters).  The epoch base

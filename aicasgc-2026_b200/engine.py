@@ -3,8 +3,12 @@
 One decode step = ONE persistent launch of the phase-program kernel
 (`aicas_decode_program_f16`): 28 x [RMSNorm+QKV, q/k-norm+MRoPE+KV-write+
 split-KV attention, o_proj+residual, RMSNorm+gate_up+SiLU*up,
-down+residual] + final RMSNorm + tied lm_head + argmax, 141 phases separated
-by bounded grid barriers, weights streamed by bulk async copies.
+down+residual] + final RMSNorm + tied lm_head + argmax: 141 phases with no
+grid barrier between them.  Each phase polls the flag-in-data words of the
+vector it consumes (every 32-bit word carries an fp16 value and the epoch of
+the phase that wrote it), so a CTA starts a phase as soon as its own inputs
+are complete; weights are streamed by bulk async copies ahead of the
+consumers, independently of the activations.
 
 The step reads its inputs (token, cache slot, 3-axis rope position) from a
 device-resident step state and advances it itself, so a run of N steps is N
@@ -361,7 +365,8 @@ class Qwen3VLDecodeEngine:
         `prefill`: "decode" runs the prompt through the decode kernel one token
         per launch; "gemm" prefills it in one pass (prefill_prompt)."""
         P = len(torch.as_tensor(prompt).reshape(-1))
-        if P + max_new_tokens - 1 > self.max_steps or P + max_new_tokens > self.max_cache_len:
+        # cache slots [0, P + max_new_tokens - 1): the last token is never fed back
+        if P + max_new_tokens - 1 > self.max_steps or P + max_new_tokens - 1 > self.max_cache_len:
             raise AicasError("request exceeds max_steps / max_cache_len")
         if prefill == "gemm":
             self.prefill_prompt(prompt, pos3, eos_token_id=eos_token_id)

@@ -224,3 +224,38 @@ def vision_grid_positions(prefix_len: int, grid_start: int = 16, grid_h: int = 1
         pos[:, i] = next_text + (i - end)
     rope_delta = next_text - end
     return pos, rope_delta
+
+
+def hf_model(shape: Qwen3VLTextShape, seed: int = 0, state: dict | None = None):
+    """An HF `Qwen3VLForConditionalGeneration` (transformers 5.x) with the
+    text decoder of `shape` and the seeded synthetic weights (`state`, or
+    `synthetic_state(shape, seed)`), tied lm_head, SDPA attention, a minimal
+    vision tower (unused by text prompts), fp32 on the CPU, in eval mode.
+    This is the model the reference's engine runs (`evaluation_wrapper.py:
+    1109-1114` loads the real checkpoint the same way)."""
+    import torch
+    from transformers import Qwen3VLConfig, Qwen3VLForConditionalGeneration
+
+    s = shape
+    cfg = Qwen3VLConfig(
+        text_config=dict(
+            hidden_size=s.hidden, num_attention_heads=s.num_heads, num_key_value_heads=s.num_kv_heads,
+            head_dim=s.head_dim, intermediate_size=s.intermediate, vocab_size=s.vocab,
+            num_hidden_layers=s.num_layers, rms_norm_eps=s.rms_eps,
+            rope_parameters={"rope_type": "default", "rope_theta": s.rope_theta,
+                             "mrope_section": list(s.mrope_section), "mrope_interleaved": True},
+            max_position_embeddings=32768, attention_bias=False, hidden_act="silu",
+        ),
+        vision_config=dict(depth=1, hidden_size=64, intermediate_size=64, num_heads=2,
+                           out_hidden_size=s.hidden, deepstack_visual_indexes=[]),
+        tie_word_embeddings=True,
+    )
+    cfg.text_config._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    model = Qwen3VLForConditionalGeneration(cfg).eval().float()
+    if state is None:
+        state = synthetic_state(s, seed=seed)
+    lm = model.model.language_model
+    lm.load_state_dict({k: v.float() for k, v in state.items()}, strict=True)
+    model.lm_head.weight = lm.embed_tokens.weight  # tied (config tie_word_embeddings)
+    return model

@@ -49,6 +49,17 @@ def measured_peak_gbs():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def headline_request(rank: int = 0):
+    """The request one bench step decodes on `rank`: the
+    1024-token prefix (seeded ids, 16x16 vision grid with 3-axis MRoPE
+    positions).  Returns (prompt [PREFIX] int64, pos3 [3, PREFIX], rope_delta).
+    The GPU parity test checks the same request's tokens and logits."""
+    from qwen3vl_config import synthetic_prompt, vision_grid_positions
+
+    pos3, rope_delta = vision_grid_positions(PREFIX)
+    return synthetic_prompt(PREFIX, seed=1234 + rank), pos3, rope_delta
+
+
 def workload_config(n_gpus: int) -> dict:
     return {
         "workload": "BASELINE config 4: Qwen3-VL-2B text decoder, 28 layers fp16, batch 1, 1024-token prefix "
@@ -213,7 +224,7 @@ def run_ours(args, rank: int, world: int):
     import torch.distributed as dist
 
     from engine import Qwen3VLDecodeEngine
-    from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state, vision_grid_positions
+    from qwen3vl_config import QWEN3VL_2B, synthetic_state
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -229,8 +240,7 @@ def run_ours(args, rank: int, world: int):
     st = synthetic_state(shape, seed=0, dtype=torch.float16)
     eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev,
                               max_steps=PREFIX + NEW + 8)
-    pos3, _ = vision_grid_positions(PREFIX)
-    prompt = synthetic_prompt(PREFIX, seed=1234 + rank)
+    prompt, pos3, _ = headline_request(rank)
     # prefill: one forced step per prefix token (not timed in the metric; its
     # time is the decode-kernel time to first token reported below)
     eng.load_script(prompt, pos3)

@@ -8,8 +8,9 @@
  * device during a launch (bounded waits that gave up, out-of-range token or
  * cache position) are written to the `error` word at the start of the scratch
  * block (see AicasScratch in aicas_phase_program.h); read it after the stream
- * synchronises.  After a device error, zero the scratch block again before the
- * next launch.
+ * synchronises.  A launch whose scratch block still holds a device error does
+ * nothing (no read, write or step-state change): zero the scratch block (and,
+ * for the step programs, the flag-in-data activation vectors) to resume.
  *
  * Scratch: kernels that need workspace (grid barrier, split-KV partials, the
  * cross-CTA argmax) take a `scratch` pointer to aicas_scratch_bytes() bytes of
@@ -150,8 +151,11 @@ AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_ph
  * that overlap on the GPU (different streams, no ordering) race and give
  * wrong results.  Each call zeroes the array's counters before its launch;
  * `status` (device int32, may be null) receives the call's device error
- * code.  Nothing is allocated or freed.  This entry point has no counterpart
- * in the reference. */
+ * code.  Nothing is allocated or freed.  Host threads may call it
+ * concurrently (the address lookup is thread-safe; the launches still race
+ * on the GPU unless ordered).  After a device reset (cudaDeviceReset) the
+ * cached address is stale: reload the library.  This entry point has no
+ * counterpart in the reference. */
 AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                                    const void* cache_position, float scale, void* out,
                                                    int64_t q_heads, int64_t kv_heads, int64_t max_len,

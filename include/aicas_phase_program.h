@@ -5,10 +5,15 @@
 //
 // A decode step is a list of PHASES executed by one persistent launch of
 // `decode_program_kernel` (one CTA per SM).  Every phase is a memory-bound
-// sweep over one weight matrix (or over the KV cache); phases are separated by
-// bounded software grid barriers.  One warp per CTA streams the phase's tiles
-// from HBM into a shared-memory ring with bulk async copies, independently of
-// the grid barriers, so weight streaming never waits on a barrier.
+// sweep over one weight matrix (or over the KV cache).  Phases are ordered by
+// their inputs: a phase that reads the vector of an earlier phase polls its
+// flag-in-data words (AICAS_F_LL_IN, below) or, in the batched kernel, a
+// per-phase completion counter (AICAS_F_CNT_IN); only a phase marked
+// AICAS_F_BARRIER waits at a bounded software grid barrier first (the
+// op-level post-attention MLP uses one).  One warp per CTA streams the
+// phase's tiles from HBM into a shared-memory ring with bulk async copies,
+// independently of the activations, so weight streaming never waits on
+// another CTA.
 #pragma once
 #include <stdint.h>
 

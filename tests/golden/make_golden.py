@@ -44,7 +44,7 @@ REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "aicasgc-2026_b200"))
 
 from qwen3vl_config import (  # noqa: E402
-    QWEN3VL_2B, synthetic_prompt, synthetic_state, vision_grid_positions,
+    QWEN3VL_2B, hf_model, synthetic_prompt, vision_grid_positions,
 )
 
 N_LAYERS = 2
@@ -67,34 +67,7 @@ def summarize(logits_rows: np.ndarray):
 
 
 def build_hf_model(n_layers: int):
-    import torch
-    from transformers import Qwen3VLConfig, Qwen3VLForConditionalGeneration
-
-    s = QWEN3VL_2B
-    cfg = Qwen3VLConfig(
-        text_config=dict(
-            hidden_size=s.hidden, num_attention_heads=s.num_heads,
-            num_key_value_heads=s.num_kv_heads, head_dim=s.head_dim,
-            intermediate_size=s.intermediate, vocab_size=s.vocab,
-            num_hidden_layers=n_layers, rms_norm_eps=s.rms_eps,
-            rope_parameters={"rope_type": "default", "rope_theta": s.rope_theta,
-                             "mrope_section": list(s.mrope_section),
-                             "mrope_interleaved": True},
-            max_position_embeddings=32768, attention_bias=False, hidden_act="silu",
-        ),
-        vision_config=dict(depth=1, hidden_size=64, intermediate_size=64, num_heads=2,
-                           out_hidden_size=s.hidden, deepstack_visual_indexes=[]),
-        tie_word_embeddings=True,
-    )
-    cfg.text_config._attn_implementation = "sdpa"
-    torch.manual_seed(0)
-    model = Qwen3VLForConditionalGeneration(cfg).eval().float()
-    state = synthetic_state(s.with_layers(n_layers), seed=0)
-    lm = model.model.language_model
-    missing, unexpected = lm.load_state_dict(state, strict=True), None
-    del missing, unexpected
-    model.lm_head.weight = lm.embed_tokens.weight  # tied (config tie_word_embeddings)
-    return model
+    return hf_model(QWEN3VL_2B.with_layers(n_layers), seed=0)
 
 
 def main():

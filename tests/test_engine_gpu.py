@@ -9,12 +9,12 @@
   the tolerance (a genuine near-tie that fp32 summation order may break
   either way).
 
-Tolerances.  2 layers: max |d logit| <= 2e-2.  28 layers: max |d| <= 3e-2 and
-mean |d| <= 5e-3 per step.  The 28-layer bound is set by the fp16 model's own
-noise floor: the fp16 oracle run with float64 instead of float32 matmul
-accumulation (same fp16 rounding points) differs from itself by up to 0.018
-max / 0.0028 mean at 28 layers (300-token vision prefix, 8 steps), because
-single-ulp fp16 rounding flips propagate through 28 residual layers.
+Tolerance: max |d logit| <= 2e-2 at every step (the fp16 bound of the
+acceptance rule), at 2 and at 28 layers; 28 layers also bound the mean
+|d logit| per step by 5e-3.  The 28-layer test decodes the benchmarked
+request itself (bench.py's `headline_request`: 1024-token prefix with a
+vision grid, then the first token and 256 decode steps, 257 tokens in all)
+and prints per-step differences and every near-tie exemption it used.
 """
 from pathlib import Path
 
@@ -29,28 +29,33 @@ from qwen3vl_config import QWEN3VL_2B, synthetic_prompt, synthetic_state, vision
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
 LOGIT_ATOL = 2e-2
-LOGIT_ATOL_28L = 3e-2
 LOGIT_MEAN_28L = 5e-3
 
 
 def _teacher_forced_check(eng, oracle, prompt, n_new, pos3=None, rope_delta=0, atol=LOGIT_ATOL, mean_tol=None):
+    """Greedy-decode `n_new` tokens on the GPU, run the oracle teacher-forced
+    on the GPU's tokens, and check every step.  Returns (tokens, logits, per-step
+    max |d|, per-step mean |d|, steps whose token differs from the oracle's
+    argmax only inside a near-tie)."""
     toks = eng.generate(prompt, n_new, pos3=pos3).numpy()
     P = len(prompt)
     gl = np.stack([eng.step_logits(P - 1 + i).float().cpu().numpy() for i in range(n_new)])
     otoks, ol = oracle.greedy(prompt, n_new, pos3_prompt=pos3, rope_delta=rope_delta, forced=toks)
-    diff = np.abs(gl - ol).max(axis=-1)
+    d = np.abs(gl - ol)
+    diff, mean = d.max(axis=-1), d.mean(axis=-1)
     assert diff.max() <= atol, f"max logit diff per step {diff}"
     if mean_tol is not None:
-        mean = np.abs(gl - ol).mean(axis=-1)
         assert mean.max() <= mean_tol, f"mean logit diff per step {mean}"
     srt = np.sort(ol, axis=-1)
     gap = srt[:, -1] - srt[:, -2]
+    exempt = []
     for i in range(n_new):
         if toks[i] != otoks[i]:
             assert gap[i] <= atol, f"step {i}: token {toks[i]} vs oracle {otoks[i]} (gap {gap[i]})"
+            exempt.append((i, int(toks[i]), int(otoks[i]), float(gap[i])))
     # the engine's token is the first max of its own fp16 logits
     np.testing.assert_array_equal(toks, np.argmax(gl, axis=-1))
-    return toks, gl, diff
+    return toks, gl, diff, mean, exempt
 
 
 @pytest.fixture(scope="module")
@@ -143,16 +148,26 @@ def test_engine_gemm_prefill_then_device_decode(cuda_device, state2):
             break
 
 
-def test_engine_full_model_vision_prefix(cuda_device):
-    """BASELINE config 4 shapes: 28 layers, 1024-token prefix with a 16x16
-    vision grid (3-axis MRoPE), then greedy decode (64 steps here)."""
+def test_engine_full_model_benchmarked_request(cuda_device):
+    """BASELINE config 4 as bench.py runs it: 28 layers, the bench's 1024-token
+    prefix (16x16 vision grid, 3-axis MRoPE), then the first token and the 256
+    benchmarked decode steps.  Every step: logits within 2e-2 (max) and 5e-3
+    (mean) of the fp16 oracle run teacher-forced on the GPU's tokens, and the
+    GPU's token equal to the oracle's argmax unless the oracle's own top-2 gap
+    is within the tolerance (each such exemption is printed)."""
+    import bench
+
     st = synthetic_state(QWEN3VL_2B, seed=0, dtype=torch.float16)
-    P, n = 1024, 64
-    pos3, rope_delta = vision_grid_positions(P)
-    prompt = synthetic_prompt(P, seed=1234).numpy()
-    eng = Qwen3VLDecodeEngine(st, QWEN3VL_2B, max_cache_len=P + n, logits_ring=n, max_steps=P + n)
+    prompt, pos3, rope_delta = bench.headline_request(0)
+    P, n = bench.PREFIX, bench.NEW + 1
+    prompt = prompt.numpy()
+    eng = Qwen3VLDecodeEngine(st, QWEN3VL_2B, max_cache_len=P + bench.NEW, logits_ring=n, max_steps=P + n)
     o = Qwen3VLOracle(st, 28, mode="fp16", max_cache_len=P + n, inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
     del st
-    toks, gl, diff = _teacher_forced_check(eng, o, prompt, n, pos3=pos3.numpy(), rope_delta=rope_delta,
-                                           atol=LOGIT_ATOL_28L, mean_tol=LOGIT_MEAN_28L)
-    print("full-model max logit diff", float(diff.max()))
+    toks, gl, diff, mean, exempt = _teacher_forced_check(eng, o, prompt, n, pos3=pos3.numpy(),
+                                                         rope_delta=rope_delta, mean_tol=LOGIT_MEAN_28L)
+    q = np.quantile(diff, [0.5, 0.9, 0.99])
+    print(f"\n28-layer benchmarked request, {n} steps: max |d logit| {diff.max():.4g} (step {int(diff.argmax())}), "
+          f"median {q[0]:.4g}, p90 {q[1]:.4g}, p99 {q[2]:.4g}; mean |d| max {mean.max():.4g}; "
+          f"near-tie exemptions {len(exempt)}: {exempt}")
+    print("per-step max |d|:", " ".join(f"{x:.4f}" for x in diff))

@@ -11,7 +11,9 @@ with an error code in the scratch block, and the context stays usable:
 * a cache slot outside the cache: the attention phase raises kErrBadInput
   instead of reading or writing past the cache, the engine reports it and
   resets its device state, and the next request decodes exactly as before;
-  the batched engine does the same when one of its streams has such a slot.
+  the batched engine does the same when one of its streams has such a slot;
+* a launch on a scratch block that still holds an error (no reset after the
+  abort) is refused on the device: nothing is written and nothing advances.
 """
 import ctypes
 import time
@@ -63,6 +65,16 @@ def test_input_that_never_arrives_ends_the_launch_with_a_timeout(cuda_device):
     # phase 0 ran normally before the wait: every word of its output carries its epoch (1)
     assert np.all((out0.cpu().numpy().view(np.uint32) >> 16) == 1)
 
+    # a C-ABI call on the aborted scratch block, made without zeroing it, is
+    # refused on the device: no output is written and the error stays recorded
+    y0 = torch.full((n,), 7.0, dtype=torch.float16, device=cuda_device)
+    check(L.aicas_gemv_f16(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()), None,
+                           ctypes.c_void_p(y0.data_ptr()), n, k, ctypes.c_void_p(scratch.data_ptr()), stream),
+          "aicas_gemv_f16")
+    torch.cuda.synchronize(cuda_device)
+    assert torch.all(y0 == 7.0)
+    assert device_error(scratch) == K_ERR_INPUT_TIMEOUT
+
     # with the scratch block zeroed again, the library computes correctly
     scratch.zero_()
     import cuda_decode_gemv as cg
@@ -81,6 +93,13 @@ def test_cache_slot_outside_the_cache_is_reported_not_used(cuda_device):
     kv = (eng.k_cache.clone(), eng.v_cache.clone())
     start = torch.tensor([int(ref[0]), eng.max_cache_len, 40, 40, 40], dtype=torch.int64)  # slot == cache length
     eng.decode_host(start, 1, graph_steps=1)
+    # a further step launched without resetting the device state is refused:
+    # the step state, the caches and the recorded error stay as they were
+    st_after = eng.state_dev.clone()
+    eng.launch(2)
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(eng.state_dev, st_after)
+    assert device_error(eng.scratch) == 15
     with pytest.raises(AicasError, match="device error 15"):
         eng.check_error()
     # nothing was written into the cache
