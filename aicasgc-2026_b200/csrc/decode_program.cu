@@ -1456,19 +1456,32 @@ struct Consumer {
         if (d.flags & AICAS_F_LL_OUT) ll_store(reinterpret_cast<uint32_t*>(d.out) + oidx, o, ep & 0xffffu);
         else reinterpret_cast<__half*>(d.out)[oidx] = __float2half_rn(o);
       } else {
-        // this CTA's partial as 64-bit LL words (no fence, no counter), then
-        // its slice of the head's merge (merge_head).  A CTA only waits for
-        // partials of its current head, which every owner stores before it
-        // waits on anything later, so the waits cannot form a cycle.
+        // this CTA's partial as 64-bit LL words (no fence, no counter)
         uint64_t* const hp = &s->part[h][0][0][0];
         constexpr int kSplitStride = 2 * (kHD + 1);
         if (t == 0) ll64_store(hp + split * kSplitStride + g * (kHD + 1), lse, ep);
         ll64_store(hp + split * kSplitStride + g * (kHD + 1) + 1 + t, o, ep);
-        merge_head(d, h, split, nsplit, ep);
       }
-      stamp_field(7);
       u0 += nseg;
     }
+    // Then this CTA's slice of the merge of every head it shares.  The
+    // partials of ALL its segments are stored before it waits for any other
+    // CTA's: merging head h first would hold back this CTA's partial of head
+    // h + 1 until head h's slowest CTA had stored, and at long contexts those
+    // waits chained across the heads (measured at 8192 slots: the slowest CTA
+    // 75 us against a 14 us median).  With every partial stored up front, a
+    // merge waits only for other CTAs' unit work.
+    const int na = attn_ctas(U, nct);
+    const uint32_t ep = epoch_base + (uint32_t)ph + 1;
+    for (int u0 = rg.start; u0 < rg.start + rg.count;) {
+      const int h = u0 / cph, j0 = u0 % cph;
+      const int nseg = min(cph - j0, rg.start + rg.count - u0);
+      const int first_owner = owner_of(h * cph, U, na);
+      const int nsplit = owner_of(h * cph + cph - 1, U, na) - first_owner + 1;
+      if (nsplit > 1) merge_head(d, h, cta - first_owner, nsplit, ep);
+      u0 += nseg;
+    }
+    stamp_field(7);
   }
   // Interleaved-MRoPE cos/sin of the step's position, once per launch
   // (every attention phase of the step uses the same table):
@@ -1804,82 +1817,6 @@ AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, in
   return launch_program(a, stream);
 }
 
-AICAS_API int aicas_gemv_f16(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t k,
-                             void* scratch, cudaStream_t stream) {
-  if (n < 1 || n > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& d = a.inl[0];
-  d.kind = AICAS_PH_GEMV;
-  d.flags = bias ? AICAS_F_BIAS : 0;
-  d.n = (int32_t)n;
-  d.k = (int32_t)k;
-  d.w = w;
-  d.x = x;
-  d.bias = bias;
-  d.out = y;
-  a.n_phases = 1;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
-AICAS_API int aicas_rmsnorm_qkv_f16(const void* x, const void* norm_w, const void* w, const void* bias, void* y,
-                                    int64_t n, int64_t k, float eps, void* scratch, cudaStream_t stream) {
-  if (n < 1 || n > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& d = a.inl[0];
-  d.kind = AICAS_PH_GEMV;
-  d.flags = AICAS_F_NORM | (bias ? AICAS_F_BIAS : 0);
-  d.n = (int32_t)n;
-  d.k = (int32_t)k;
-  d.w = w;
-  d.x = x;
-  d.norm_w = norm_w;
-  d.bias = bias;
-  d.out = y;
-  d.eps = eps;
-  a.n_phases = 1;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
-AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out, const void* norm_w,
-                                      const void* gate_up_w, const void* down_w, const void* bias, void* act_out,
-                                      void* out, int64_t hidden, int64_t inter, float eps, void* scratch,
-                                      cudaStream_t stream) {
-  if (hidden < 1 || inter < 1 || hidden > AICAS_MAX_K || inter > AICAS_MAX_K) return AICAS_ERR_SHAPE;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& g = a.inl[0];
-  g.kind = AICAS_PH_GATEUP;
-  g.flags = AICAS_F_X_ADD | AICAS_F_NORM;
-  g.n = (int32_t)inter;
-  g.k = (int32_t)hidden;
-  g.w = gate_up_w;
-  g.x = residual;
-  g.x2 = attn_out;
-  g.norm_w = norm_w;
-  g.out = act_out;
-  g.eps = eps;
-  AicasPhase& dn = a.inl[1];
-  dn.kind = AICAS_PH_GEMV;
-  dn.flags = AICAS_F_RESID | AICAS_F_RESID_ADD | (bias ? AICAS_F_BIAS : 0);
-  dn.n = (int32_t)hidden;
-  dn.k = (int32_t)inter;
-  dn.w = down_w;
-  dn.x = act_out;
-  dn.resid = residual;
-  dn.resid2 = attn_out;
-  dn.bias = bias;
-  dn.out = out;
-  dn.flags |= AICAS_F_BARRIER;  // act comes from the gate_up phase of this launch
-  dn.rot = 37;  // the down sweep's extra row groups land on other CTAs than gate_up's
-  a.n_phases = 2;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
 AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,
                                             const void* cache_position, float scale, void* out, int64_t q_heads,
                                             int64_t kv_heads, int64_t max_len, void* scratch, cudaStream_t stream) {
@@ -1899,29 +1836,6 @@ AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, 
   d.pos_ptr = cache_position;
   d.out = out;
   d.scale = scale;
-  a.n_phases = 1;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
-AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const void* w, void* logits,
-                                       void* token_out, int64_t vocab, int64_t k, float eps, void* scratch,
-                                       cudaStream_t stream) {
-  if (vocab < 1 || vocab > (1 << 30) || k < 1) return AICAS_ERR_SHAPE;
-  if (!token_out) return AICAS_ERR_ARG;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& d = a.inl[0];
-  d.kind = AICAS_PH_LMHEAD;
-  d.flags = norm_w ? AICAS_F_NORM : 0;
-  d.n = (int32_t)vocab;
-  d.k = (int32_t)k;
-  d.w = w;
-  d.x = x;
-  d.norm_w = norm_w;
-  d.out = logits;
-  d.idx_out = token_out;
-  d.eps = eps;
   a.n_phases = 1;
   a.scratch = reinterpret_cast<AicasScratch*>(scratch);
   return launch_program(a, stream);

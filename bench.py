@@ -206,6 +206,27 @@ def max_over_ranks(vals, world: int):
     return [float(x) for x in t]
 
 
+def gather_ranks(row, world: int):
+    """Every rank's `row` (a list of floats) -> the list of all ranks' rows
+    (rank order), so rank 0 can report each GPU's own work."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v) for v in row], dtype=torch.float64)
+    if world == 1:
+        return [t.tolist()]
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [x.tolist() for x in out]
+
+
+def per_rank_report(rows, tokens_per_rank: int) -> list:
+    """[rank, device index, timed ms, setup s] rows -> per-rank dicts with the
+    rank's own tok/s (each rank's GPU decodes its own requests)."""
+    return [{"rank": int(r[0]), "device": int(r[1]), "ms": r[2], "tok_s": tokens_per_rank / (r[2] / 1000.0),
+             "setup_s": r[3]} for r in rows]
+
+
 def job_throughput(steps: int, world: int, ms: float) -> float:
     """Whole-job tok/s: every rank decodes `steps` requests of NEW tokens in
     `ms` (the max over ranks)."""
@@ -236,6 +257,7 @@ def run_ours(args, rank: int, world: int):
         if world > 1:
             dist.barrier()
 
+    t_setup = time.perf_counter()
     shape = QWEN3VL_2B.with_layers(args.layers)
     st = synthetic_state(shape, seed=0, dtype=torch.float16)
     eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev,
@@ -259,6 +281,8 @@ def run_ours(args, rank: int, world: int):
     def one_request():
         eng.restore(start_state)
         eng.run(NEW, graph_steps)  # 256 decode steps = 8 replays of a 32-launch graph
+
+    setup_s = time.perf_counter() - t_setup  # weights, prefill, graph capture
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -321,7 +345,8 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize(dev)
     ttft_gemm_ms = p0.elapsed_time(p1) / 3
 
-    # ---- max over ranks
+    # ---- max over ranks (and each rank's own figures: its GPU and its work)
+    ranks = per_rank_report(gather_ranks([rank, dev.index, ms, setup_s], world), args.steps * NEW)
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], world)
     value = job_throughput(args.steps, world, ms)
     e2e_value = job_throughput(args.steps, world, e2e_ms)
@@ -347,6 +372,7 @@ def run_ours(args, rank: int, world: int):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 8 * NEW,
                 "tokens_match_device_run": e2e_ok},
         "gpu_launches": args.steps * NEW,
+        "per_rank": ranks,
         "ttft": {"prefix_tokens": PREFIX, "one_pass_prefill_ms": ttft_gemm_ms,
                  "decode_kernel_prefill_ms": ttft_decode_ms,
                  "note": "first token of the 1024-token prefix; outside the decode metric"},
@@ -411,6 +437,7 @@ def run_batch(args, rank: int, world: int):
         if world > 1:
             dist.barrier()
 
+    t_setup = time.perf_counter()
     B = args.batch
     ctx = batch_contexts(B, rank)
     shape = QWEN3VL_2B.with_layers(args.layers)
@@ -435,6 +462,8 @@ def run_batch(args, rank: int, world: int):
     def one_step():
         eng.state_dev.copy_(start_state)
         eng.run(BATCH_NEW, graph_steps)
+
+    setup_s = time.perf_counter() - t_setup
 
     for _ in range(args.warmup):
         one_step()
@@ -476,6 +505,7 @@ def run_batch(args, rank: int, world: int):
     barrier()
     e2e_ok = bool(torch.equal(out_host, toks))
 
+    ranks = per_rank_report(gather_ranks([rank, dev.index, ms, setup_s], world), args.steps * B * BATCH_NEW)
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], world)
     tok_per_step = B * BATCH_NEW
     value = args.steps * tok_per_step * world / (ms / 1000.0)
@@ -501,6 +531,7 @@ def run_batch(args, rank: int, world: int):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 40 * B,
                 "d2h_bytes_per_step": 8 * B * BATCH_NEW, "tokens_match_device_run": e2e_ok},
         "gpu_launches": args.steps * BATCH_NEW,
+        "per_rank": ranks,
         "prefill_ms_all_requests": prefill_ms,
         "clocks": clocks,
     }
@@ -510,6 +541,153 @@ def run_batch(args, rank: int, world: int):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- op benchmarks
+GEMV_SHAPES = [("qkv", 4096, 2048), ("o_proj", 2048, 2048), ("gate_up", 12288, 2048), ("down", 2048, 6144),
+               ("lm_head_argmax", 151936, 2048)]
+ATTN_LENGTHS = [128, 512, 1024, 2048, 4096, 8192]
+OP_COPIES = 28  # distinct weight / KV copies visited round-robin: the working set exceeds L2
+
+
+def _cpu_op_baseline(fn, seconds: float):
+    """Median seconds per call of `fn` on the host (all threads), at least 3
+    calls and about `seconds` of work."""
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(limits=os.cpu_count() or 1):
+        fn()
+        ts = []
+        t_end = time.perf_counter() + seconds
+        while len(ts) < 3 or time.perf_counter() < t_end:
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+            if len(ts) >= 200:
+                break
+    return statistics.median(ts), len(ts)
+
+
+def _time_graph(torch, calls, reps: int, warmup: int, dev):
+    """Capture `calls` (a list of zero-argument launches) in one CUDA graph,
+    replay it `warmup` + `reps` times; returns device us per call (CUDA
+    events on the capturing stream)."""
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for c in calls:  # eager warm-up outside capture
+            c()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for c in calls:
+                c()
+        for _ in range(warmup):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        stream.synchronize()
+    return 1000.0 * e0.elapsed_time(e1) / (reps * len(calls))
+
+
+def run_op(args, rank: int, world: int):
+    """BASELINE configs 2 (decode GEMV shapes) and 3 (decode attention
+    alone): one JSON line per shape / valid length, each op called through
+    the C ABI (the reference-facing entry points), one call per distinct
+    weight or KV copy so the working set exceeds L2, as one CUDA graph."""
+    if rank != 0:
+        return
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import _native
+    from oracle.qwen3vl_oracle import attention_reference, gemv_reference
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L = _native.lib()
+    peak, peak_kind = measured_peak_gbs()
+    cores = os.cpu_count()
+    scratch = torch.zeros(_native.scratch_bytes(), dtype=torch.uint8, device=dev)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    g = torch.Generator(device=dev).manual_seed(7)  # inputs made on the device (17 GB of lm_head copies)
+    lines = []
+
+    def emit(name, shape, us, algo_bytes, cpu_s, cpu_n, cpu_sample, extra):
+        achieved = algo_bytes / (us * 1e-6) / 1e9
+        line = {"metric": f"decode {args.op} op us per call", "op": name, "shape": shape, "value": us,
+                "unit": "us", "higher_is_better": False, "n_gpus": 1, "dtype": "f16 (fp32 accumulate)",
+                "data": "synthetic",
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_kind": peak_kind, "algorithmic_bytes": algo_bytes},
+                "cpu_baseline": {"value": cpu_s * 1e6, "unit": "us", "cores": cores, "kind": "port",
+                                 "sample": f"{cpu_n} calls, {cpu_sample}"},
+                "config": {"workload": ("BASELINE config 2: decode GEMV, fp16 weights N(0,0.02), x N(0,1)"
+                                        if args.op == "gemv" else
+                                        "BASELINE config 3: decode attention, q [1,16,128], K/V [8,L,128] "
+                                        "N(0,1) in an 8192-slot cache, scale 1/sqrt(128)"),
+                           "copies": OP_COPIES, "l2": "one distinct weight / KV copy per call, "
+                                                       f"{OP_COPIES} copies round-robin (working set > L2)"},
+                **extra}
+        lines.append(line)
+        print(json.dumps(line), flush=True)
+
+    if args.op == "gemv":
+        for name, n, k in GEMV_SHAPES:
+            ws = [(torch.randn((n, k), generator=g, device=dev) * 0.02).half() for _ in range(OP_COPIES)]
+            x = torch.randn(k, generator=g, device=dev).half()
+            y = torch.empty(n, dtype=torch.float16, device=dev)
+            tok = torch.empty(1, dtype=torch.int64, device=dev)
+            stream_of = lambda: ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)  # noqa: E731
+            if name == "lm_head_argmax":
+                calls = [lambda w=w: _native.check(L.aicas_lm_head_argmax_f16(
+                    p(x), None, p(w), p(y), p(tok), n, k, 0.0, p(scratch), stream_of()), "lm_head")
+                    for w in ws]
+            else:
+                calls = [lambda w=w: _native.check(L.aicas_gemv_f16(
+                    p(x), p(w), None, p(y), n, k, p(scratch), stream_of()), "gemv") for w in ws]
+            us = _time_graph(torch, calls, reps=args.steps, warmup=args.warmup, dev=dev)
+            w0, x0 = ws[-1].float().cpu().numpy(), x.float().cpu().numpy()
+            ok = bool(np.allclose(y.float().cpu().numpy(), gemv_reference(w0, x0), atol=2e-3, rtol=2e-3))
+            if name == "lm_head_argmax":
+                ok = ok and int(tok.item()) == int(np.argmax(gemv_reference(w0, x0)))
+            cpu_s, cpu_n = _cpu_op_baseline(lambda: gemv_reference(w0, x0), args.cpu_seconds / 5)
+            emit(name, [n, k], us, n * k * 2 + k * 2 + n * 2, cpu_s, cpu_n,
+                 "numpy fp32 W x (the oracle's restatement of F.linear), all host threads",
+                 {"matches_oracle": ok})
+            del ws
+            torch.cuda.empty_cache()
+    else:
+        lmax = 8192
+        scale = 128 ** -0.5
+        q = torch.randn(16 * 128, generator=g, device=dev).half()
+        ks = [torch.randn((8, lmax, 128), generator=g, device=dev).half() for _ in range(OP_COPIES)]
+        vs = [torch.randn((8, lmax, 128), generator=g, device=dev).half() for _ in range(OP_COPIES)]
+        out = torch.empty(16 * 128, dtype=torch.float16, device=dev)
+        for Lv in ATTN_LENGTHS:
+            pos = torch.tensor([Lv - 1], dtype=torch.int64, device=dev)
+            stream_of = lambda: ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)  # noqa: E731
+            calls = [lambda kc=kc, vc=vc: _native.check(L.aicas_decode_attn_splitkv_f16(
+                p(q), p(kc), p(vc), p(pos), scale, p(out), 16, 8, lmax, p(scratch), stream_of()), "attention")
+                for kc, vc in zip(ks, vs)]
+            us = _time_graph(torch, calls, reps=args.steps, warmup=args.warmup, dev=dev)
+            q0 = q.view(16, 128).float().cpu().numpy()
+            k0 = ks[-1][:, :Lv].float().cpu().numpy()
+            v0 = vs[-1][:, :Lv].float().cpu().numpy()
+            ref = attention_reference(q0, k0, v0, Lv, scale)
+            ok = bool(np.abs(out.view(16, 128).float().cpu().numpy() - ref).max() <= 2e-3)
+            cpu_s, cpu_n = _cpu_op_baseline(lambda: attention_reference(q0, k0, v0, Lv, scale),
+                                            args.cpu_seconds / 6)
+            emit(f"attention_L{Lv}", [16, 8, Lv, 128], us, 4096 * Lv + 2 * 16 * 128 * 2, cpu_s, cpu_n,
+                 "numpy fp32 restatement of the reference's _hf_repeat_kv_attention, all host threads",
+                 {"valid_len": Lv, "matches_oracle": ok})
+    if args.op_out:
+        Path(args.op_out).write_text("\n".join(json.dumps(x) for x in lines) + "\n")
 
 
 def write_trace_summary(eng, start_state, path):
@@ -559,10 +737,17 @@ def main():
                          "decode of ragged requests (contexts U[512, 4096], 512 decode steps each)")
     ap.add_argument("--layers", type=int, default=28,
                     help="profiling case only: a smaller model (the headline is 28 layers)")
+    ap.add_argument("--op", choices=["gemv", "attention"], default=None,
+                    help="per-op benchmark instead of the decode step: BASELINE config 2 (the five decode GEMV "
+                         "shapes) or config 3 (decode attention at valid lengths 128..8192); --steps = graph "
+                         "replays of one call per copy")
+    ap.add_argument("--op-out", default="", help="also write the op benchmark's JSON lines to this file")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.impl == "reference":
+    if args.op:
+        run_op(args, rank, world)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     elif args.batch > 1:
         run_batch(args, rank, world)

@@ -32,6 +32,15 @@ Two arithmetic modes:
   (matmul / reduction arithmetic itself stays fp32, as cuBLAS and SDPA do).
   This is the checker for the fp16 CUDA engine.
 
+``accumulate="f64"`` (fp16 mode only) carries out the matmuls, attention and
+norm reductions in float64 before each fp16 rounding point: the fp16 model
+with exact sums.  Any fp32-accumulating implementation (cuBLAS, the CUDA
+engine, numpy's fp32 BLAS) flips an fp16 rounding now and then where its sum
+lands next to a rounding boundary, and at 28 layers those one-ulp flips move
+the logits by up to ~0.02.  Two fp32 implementations compared with each other
+show both sets of flips; against the exact sums only the implementation's own
+remain, which is the comparison the 28-layer GPU parity test makes.
+
 Attention is causal over the static cache prefix `[0, cache_position]`, the
 contract of the reference's kernels (`decode_attention_v4_kernel.cu` reads
 `valid_len = cache_position + 1`).
@@ -52,13 +61,13 @@ def _rnd(x: np.ndarray, mode: str) -> np.ndarray:
     return _r16(x) if mode == "fp16" else x.astype(F32, copy=False)
 
 
-def rms_norm(x: np.ndarray, w: np.ndarray, eps: float, mode: str = "fp16") -> np.ndarray:
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float, mode: str = "fp16", acc=F32) -> np.ndarray:
     """`Qwen3VLTextRMSNorm.forward` (modeling_qwen3_vl.py:398-403) over the
-    last axis: fp32 variance and scale, cast back to the activation dtype,
-    then the weight multiply in the activation dtype."""
-    xf = x.astype(F32)
-    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=F32)
-    n = _rnd(xf * (F32(1.0) / np.sqrt(var + F32(eps))), mode)
+    last axis: fp32 variance and scale (`acc` float64: exact), cast back to
+    the activation dtype, then the weight multiply in the activation dtype."""
+    xf = x.astype(acc)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=acc)
+    n = _rnd(xf * (acc(1.0) / np.sqrt(var + acc(eps))), mode)
     return _rnd(w * n, mode)
 
 
@@ -82,10 +91,13 @@ class Qwen3VLOracle:
     def __init__(self, state: dict, num_layers: int, *, mode: str = "fp32",
                  max_cache_len: int = 2048, num_heads: int = 16, num_kv_heads: int = 8,
                  head_dim: int = 128, eps: float = 1e-6, rope_theta: float = 5e6,
-                 mrope_section=(24, 20, 20), inv_freq=None):
+                 mrope_section=(24, 20, 20), inv_freq=None, accumulate: str = "f32"):
         if mode not in ("fp32", "fp16"):
             raise ValueError(mode)
+        if accumulate not in ("f32", "f64") or (accumulate == "f64" and mode != "fp16"):
+            raise ValueError(f"accumulate={accumulate!r} (float64 sums are an fp16-mode option)")
         self.mode = mode
+        self.acc = np.float64 if accumulate == "f64" else F32
         self.L = num_layers
         self.nh, self.nkv, self.d = num_heads, num_kv_heads, head_dim
         self.eps = F32(eps)
@@ -97,7 +109,8 @@ class Qwen3VLOracle:
             if hasattr(t, "detach"):
                 t = t.detach().float().cpu().numpy()
             a = np.ascontiguousarray(np.asarray(t, dtype=F32))
-            return _r16(a) if mode == "fp16" else a
+            a = _r16(a) if mode == "fp16" else a
+            return a.astype(self.acc) if self.acc is not F32 else a
 
         self.embed = arr("embed_tokens.weight")
         self.final_norm = arr("norm.weight")
@@ -122,7 +135,7 @@ class Qwen3VLOracle:
         self.inv_freq = (F32(1.0) / np.power(F32(rope_theta), expo)).astype(F32)
         if inv_freq is not None:  # e.g. the table HF computes with torch (1-ulp pow differences)
             self.inv_freq = np.asarray(inv_freq, dtype=F32).reshape(-1)
-        self.k_cache = np.zeros((num_layers, num_kv_heads, max_cache_len, head_dim), F32)
+        self.k_cache = np.zeros((num_layers, num_kv_heads, max_cache_len, head_dim), self.acc)
         self.v_cache = np.zeros_like(self.k_cache)
 
     # ---- elementwise helpers -------------------------------------------------
@@ -130,7 +143,7 @@ class Qwen3VLOracle:
         return _rnd(x, self.mode)
 
     def rms_norm(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
-        return rms_norm(x, w, self.eps, self.mode)
+        return rms_norm(x, w, self.eps, self.mode, self.acc)
 
     def mrope_cos_sin(self, pos3: np.ndarray):
         """Interleaved-MRoPE cos/sin for positions `pos3` [3, T] (t, h, w).
@@ -154,7 +167,7 @@ class Qwen3VLOracle:
         return rope(x, cos, sin, self.mode)
 
     def _linear(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
-        return self._round(x @ w.T)
+        return self._round(x.astype(w.dtype, copy=False) @ w.T)
 
     # ---- model ---------------------------------------------------------------
     def forward(self, tokens, pos3, cache_start: int, *, all_logits: bool = False):
@@ -168,7 +181,8 @@ class Qwen3VLOracle:
             raise ValueError("cache overflow")
         cos, sin = self.mrope_cos_sin(pos3)
         h = self.embed[tokens].astype(F32)
-        scale = F32(self.d ** -0.5)
+        acc = self.acc
+        scale = acc(self.d ** -0.5)
         g = self.nh // self.nkv
         for li, lw in enumerate(self.layers):
             x = self.rms_norm(h, lw["ln1"])
@@ -186,17 +200,18 @@ class Qwen3VLOracle:
             causal = np.arange(end)[None, :] <= (cache_start + np.arange(T))[:, None]
             for hq in range(self.nh):
                 kv = hq // g
-                s = (q[:, hq, :] @ K[kv].T) * scale  # [T, end]
-                s = np.where(causal, s, -np.inf).astype(F32)
+                s = (q[:, hq, :].astype(acc) @ K[kv].T) * scale  # [T, end]
+                s = np.where(causal, s, -np.inf).astype(acc)
                 m = s.max(axis=-1, keepdims=True)
-                p = np.exp(s - m).astype(F32)
-                attn[:, hq, :] = (p @ V[kv]) / p.sum(axis=-1, keepdims=True, dtype=F32)
+                p = np.exp(s - m).astype(acc)
+                attn[:, hq, :] = (p @ V[kv]) / p.sum(axis=-1, keepdims=True, dtype=acc)
             attn = self._round(attn).reshape(T, self.nh * self.d)
             h = self._round(h + self._linear(attn, lw["wo"]))
             x = self.rms_norm(h, lw["ln2"])
             gt = self._linear(x, lw["wg"])
             up = self._linear(x, lw["wu"])
-            act = self._round(self._round(gt / (F32(1.0) + np.exp(-gt))) * up)
+            gt_a = gt.astype(acc)
+            act = self._round(self._round(gt_a / (acc(1.0) + np.exp(-gt_a))) * up)
             h = self._round(h + self._linear(act, lw["wd"]))
         hn = self.rms_norm(h if all_logits else h[-1:], self.final_norm)
         logits = self._linear(hn, self.embed)

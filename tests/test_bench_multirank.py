@@ -31,7 +31,10 @@ def _rank_main(rank: int, world: int, port: int, q):
         dist.barrier()
         # rank r "took" (r + 1) ms on device and 10 (r + 1) ms end to end
         ms, e2e_ms = bench.max_over_ranks([rank + 1.0, 10.0 * (rank + 1)], world)
-        q.put((rank, ms, e2e_ms, bench.job_throughput(3, world, ms)))
+        # each rank's own row (rank, device, its ms, its setup s) reaches every rank in rank order
+        rows = bench.gather_ranks([rank, 4 + rank, rank + 1.0, 0.5], world)
+        per = bench.per_rank_report(rows, 3 * bench.NEW)
+        q.put((rank, ms, e2e_ms, bench.job_throughput(3, world, ms), per))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -50,10 +53,12 @@ def test_max_over_ranks_and_job_throughput_world2():
         p.join(120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     got = sorted(q.get(timeout=5) for _ in range(world))
-    for rank, ms, e2e_ms, tps in got:
+    for rank, ms, e2e_ms, tps, per in got:
         assert ms == 2.0 and e2e_ms == 20.0, (rank, ms, e2e_ms)  # the slowest rank sets the job time
         # whole-job throughput: 3 requests x 256 tokens on each of 2 ranks in 2 ms
         assert tps == pytest.approx(3 * bench.NEW * 2 / 0.002)
+        assert [r["rank"] for r in per] == [0, 1] and [r["device"] for r in per] == [4, 5]
+        assert per[1]["tok_s"] == pytest.approx(3 * bench.NEW / 0.002)  # rank 1's own rate
 
 
 def test_single_rank_needs_no_process_group():
