@@ -114,6 +114,11 @@ SIGNATURES = {
     "aicas_decode_batch_f16": (_I, [_P, _I, _P, _I, _P, _P]),
     "aicas_decode_batch_trace_f16": (_I, [_P, _I, _P, _I, _P, _P, _P]),
     "aicas_tile_weight_f16": (_I, [_P, _P, _I64, _I64, _P]),
+    "aicas_prefill_add_rmsnorm_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P]),
+    "aicas_prefill_qk_norm_rope_kv_f16": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                               _I64, _F, _P]),
+    "aicas_prefill_silu_mul_f16": (_I, [_P, _P, _I64, _I64, _P]),
+    "aicas_prefill_attention_f16": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
 }
 
 _lock = threading.Lock()

@@ -12,10 +12,10 @@
 //               RMSNorm prologue with HF's fp16 rounding points, then reduce
 //               each tile row against it with exact fp16 products and fp32
 //               accumulation (one row per warp, four accumulation chains).
-//   warp 9      L2 prefetch (AICAS_L2_WARP): walks the same tile schedule up
-//               to kL2Ahead tiles ahead of the producer and prefetches them
-//               into L2, so HBM keeps working while the ring is full.
-//   warp 10     TMEM mover: copies every landed GEMV tile from its ring stage
+//   (warp 9     optional L2 prefetch, AICAS_L2_WARP=1: walks the same tile
+//               schedule up to kL2Ahead tiles ahead of the producer and
+//               prefetches them into L2; off by default, see below.)
+//   last warp   TMEM mover: copies every landed GEMV tile from its ring stage
 //               into an 8-slot ring in tensor memory (tcgen05.cp) and frees
 //               the stage; consumers read their tile row from TMEM
 //               (tcgen05.ld), so up to kStages + 8 tiles wait ahead of them.
@@ -66,12 +66,15 @@ namespace aicas {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-// AICAS_L2_WARP: 1 (default) an extra warp runs an L2 prefetch cursor ahead
-// of the ring (one bulk prefetch per tile, lines marked evict_last; the ring
-// loads mark weights and KV tiles evict_first); 2 the same with per-line
-// prefetches; 0 no prefetch warp.
+// AICAS_L2_WARP: 1 an extra warp runs an L2 prefetch cursor ahead of the
+// ring (one bulk prefetch per tile, lines marked evict_last; the ring loads
+// mark weights and KV tiles evict_first); 2 the same with per-line
+// prefetches; 0 (default) no prefetch warp.  Once the norm weights stopped
+// blocking each phase's input poll, the run-ahead cost more than it gave:
+// same-box A/B on the 28-layer step, 996 -> 989 and 990 -> 979 us per token
+// without it.
 #ifndef AICAS_L2_WARP
-#define AICAS_L2_WARP 1
+#define AICAS_L2_WARP 0
 #endif
 // Warp roles: 0 producer, 1..8 consumers, then the L2 prefetch warp (if
 // enabled), then the TMEM mover (last warp).
@@ -627,24 +630,15 @@ struct Consumer {
     return rv;
   }
 
-  // Work for phase `d` that depends on nothing the previous phase writes:
-  // norm weights -> shared memory, first residual rows -> registers.  Runs
-  // between this CTA's barrier arrival and its wait.
+  // Work for phase `d` that depends on nothing the previous phase writes: the
+  // residual rows of the first epilogue batch -> registers (loads issued here,
+  // first used in the epilogue).  Runs between this CTA's barrier arrival and
+  // its wait.  Nothing here blocks on a load: a synchronous load before the
+  // input poll would sit on the critical path of the hand-off (the norm
+  // weights of a phase are loaded into registers by build_x, before its poll;
+  // measured on B200 with the 28-layer step: 1019 -> 983 us per token).
   __device__ __forceinline__ void prefetch(const AicasPhase& d) {
-    if (d.kind == AICAS_PH_ATTN) {
-      if (!(d.flags & AICAS_F_Q_READY) && tid < 2 * kHD / 8) {
-        const __half* src = reinterpret_cast<const __half*>(tid < kHD / 8 ? d.norm_w : d.norm_w2);
-        const int v = tid % (kHD / 8);
-        *reinterpret_cast<uint4*>(&sm.nw[(tid / (kHD / 8)) * kHD + v * 8]) =
-            __ldg(reinterpret_cast<const uint4*>(src) + v);
-      }
-      return;
-    }
-    if (d.flags & AICAS_F_NORM) {
-      const __half* nw = reinterpret_cast<const __half*>(d.norm_w);
-      for (int v = tid; v < d.k / 8; v += kConsumerThreads)
-        *reinterpret_cast<uint4*>(&sm.nw[v * 8]) = __ldg(reinterpret_cast<const uint4*>(nw) + v);
-    }
+    if (d.kind == AICAS_PH_ATTN) return;  // q/k norm weights are loaded into registers by run_attention
     if (d.flags & AICAS_F_RESID) {  // lane l: the row of group l of this CTA (first epilogue batch)
       const Range rg = split_range((d.n + kRows - 1) / kRows, nct, cta, d.rot);
       const int row = (rg.start + lane) * kRows + rwt;
@@ -683,6 +677,14 @@ struct Consumer {
       cols[i] = (v < C * kVec && col < k) ? col : -1;
     }
     uint4 raw[NV];
+    uint4 nwr[NV];
+    const bool norm1 = C == 1 && (flags & AICAS_F_NORM);
+    if (norm1) {  // issued before the poll, used after it: the load latency hides behind the wait
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        nwr[i] = cols[i] >= 0 ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(d.norm_w) + cols[i]))
+                              : make_uint4(0, 0, 0, 0);
+    }
     if (ll) {
       ll_poll8_n<NV>(xw, cols, x_epoch, s, raw);
     } else {
@@ -712,11 +714,31 @@ struct Consumer {
           ss += f.x * f.x + f.y * f.y;
         }
       }
-      *reinterpret_cast<uint4*>(&xbuf[cols[i]]) = raw[i];
+      if (!norm1) *reinterpret_cast<uint4*>(&xbuf[cols[i]]) = raw[i];
     }
-    if (C == 1 && (flags & AICAS_F_NORM)) {
+    if (norm1) {
+      // RMSNorm of the thread's own slice (HF rounding points), then the
+      // normalised vector goes to shared memory for every warp
       ss = warp_sum(ss);
       if (lane == 0) sm.ssq[w] = ss;
+      consumer_sync(kConsumerThreads);
+      ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kConsumerWarps; ++i) ss += sm.ssq[i];
+      const float inv = rsqrtf(ss / (float)k + d.eps);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (cols[i] < 0) continue;
+        __half2* hp = reinterpret_cast<__half2*>(&raw[i]);
+        const __half2* wp = reinterpret_cast<const __half2*>(&nwr[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hp[q]);
+          const float2 g = __half22float2(wp[q]);
+          hp[q] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
+        }
+        *reinterpret_cast<uint4*>(&xbuf[cols[i]]) = raw[i];
+      }
     }
     consumer_sync(kConsumerThreads);
     if constexpr (C == 1) {
@@ -724,29 +746,6 @@ struct Consumer {
       for (int j = 0; j < kVec; ++j) {
         const int col = colv(j);
         x0[j] = col < k ? *reinterpret_cast<const uint4*>(&sm.xs[col]) : make_uint4(0, 0, 0, 0);
-      }
-      if (flags & AICAS_F_NORM) {
-        ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) ss += sm.ssq[i];
-      }
-    }
-    if (C == 1 && (flags & AICAS_F_NORM)) {
-      const float inv = rsqrtf(ss / (float)k + d.eps);
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        const int col = colv(j);
-        if (col < k) {
-          const uint4 wr = *reinterpret_cast<const uint4*>(&sm.nw[col]);
-          __half2* hp = reinterpret_cast<__half2*>(&x0[j]);
-          const __half2* wp = reinterpret_cast<const __half2*>(&wr);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __half22float2(hp[q]);
-            const float2 g = __half22float2(wp[q]);
-            hp[q] = __floats2half2_rn(g.x * r16(f.x * inv), g.y * r16(f.y * inv));
-          }
-        }
       }
     }
     if ((flags & AICAS_F_STORE_X) && cta == 0 && w == 0 && d.x_out) {
@@ -1111,7 +1110,7 @@ struct Consumer {
   // One 128-dim head per warp (lane l holds dims 4l..4l+3): per-head RMSNorm
   // (modeling_qwen3_vl.py:398-403) and rotary embedding (:124-128, :427-431).
   // rotate_half's partner of dim d is d +- 64, held by lane l ^ 16.
-  __device__ __forceinline__ void norm_rope_head(float (&v)[4], const __half* nw, float eps, const float (&cs)[4],
+  __device__ __forceinline__ void norm_rope_head(float (&v)[4], uint2 nw, float eps, const float (&cs)[4],
                                  const float (&sn)[4]) {
     float ss = 0.f;
 #pragma unroll
@@ -1119,7 +1118,10 @@ struct Consumer {
     const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
     float xn[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) xn[e] = r16(__half2float(nw[lane * 4 + e]) * r16(v[e] * inv));
+    const __half2* nh = reinterpret_cast<const __half2*>(&nw);
+    const float nwf[4] = {__low2float(nh[0]), __high2float(nh[0]), __low2float(nh[1]), __high2float(nh[1])};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) xn[e] = r16(nwf[e] * r16(v[e] * inv));
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
@@ -1365,6 +1367,11 @@ struct Consumer {
     const int jpos = pos / kAttnChunk;
     const int kpos = q_ready ? -1 : pos;  // the slot whose k / v come from shared memory
     const int slot = w >> 2, wq = w & 3;
+    // warps 0, 1: q_norm weights of their query head; warp 2: k_norm (dims 4 lane .. 4 lane + 3),
+    // issued here and first used after the q/k/v poll
+    uint2 nwv = make_uint2(0, 0);
+    if (!q_ready && w < 3)
+      nwv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(w < 2 ? d.norm_w : d.norm_w2)) + lane);
     bool stamped = false;
     float m[2], l[2], acc[2][4];
     for (int u0 = rg.start; u0 < rg.start + rg.count;) {
@@ -1376,7 +1383,7 @@ struct Consumer {
         const uint2 raw = ll_in ? ll_poll4(qkv_w, col, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + col));
         const __half2* hp = reinterpret_cast<const __half2*>(&raw);
         float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
-        if (!q_ready) norm_rope_head(v, sm.nw, d.eps, cs, sn);
+        if (!q_ready) norm_rope_head(v, nwv, d.eps, cs, sn);
         *reinterpret_cast<__half2*>(&at.qh[w][lane * 4]) = __floats2half2_rn(v[0], v[1]);
         *reinterpret_cast<__half2*>(&at.qh[w][lane * 4 + 2]) = __floats2half2_rn(v[2], v[3]);
       } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
@@ -1384,7 +1391,7 @@ struct Consumer {
         const uint2 raw = ll_in ? ll_poll4(qkv_w, off, x_epoch, s) : __ldcg(reinterpret_cast<const uint2*>(qkv + off));
         const __half2* hp = reinterpret_cast<const __half2*>(&raw);
         float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
-        if (w == 2) norm_rope_head(v, sm.nw + kHD, d.eps, cs, sn);
+        if (w == 2) norm_rope_head(v, nwv, d.eps, cs, sn);
         float* dst = w == 2 ? at.kf : at.vf;
 #pragma unroll
         for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
@@ -1509,9 +1516,11 @@ struct Consumer {
       consumer_sync(kConsumerThreads);
       const bool barrier = ph > 0 && (d.flags & AICAS_F_BARRIER);
       if (barrier && tid == 0) grid_arrive(s);
-      prefetch(d);
-      if (barrier && tid == 0) grid_wait(s, bar_base + (uint64_t)(++bar_k) * nct);
-      consumer_sync(kConsumerThreads);  // prefetched norm weights visible; barrier passed
+      prefetch(d);  // registers only: nothing to publish through shared memory
+      if (barrier) {
+        if (tid == 0) grid_wait(s, bar_base + (uint64_t)(++bar_k) * nct);
+        consumer_sync(kConsumerThreads);  // every consumer thread is past the grid barrier
+      }
       stamp(ph, 0);
       if (d.kind == AICAS_PH_ATTN) run_attention(d);
       else run_matvec(d);

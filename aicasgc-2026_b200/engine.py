@@ -94,6 +94,8 @@ class Qwen3VLDecodeEngine:
                                          0).contiguous(),
                     # K-blocked [k/2048][n][2048]: every 8-row tile is one contiguous 32 KB copy
                     "down": kblock(W(p + "mlp.down_proj.weight")),
+                    # row-major copy for the prompt prefill's GEMM
+                    "down_rm": W(p + "mlp.down_proj.weight"),
                 })
             # StaticCache-layout KV: [layers][1, KVH, Lmax, 128]
             kv_shape = (s.num_layers, 1, s.num_kv_heads, max_cache_len, s.head_dim)

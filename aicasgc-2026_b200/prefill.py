@@ -12,9 +12,11 @@ modeling_qwen3_vl.py:398-403, q/k-norm + interleaved MRoPE :352-386 and
 :427-431, SiLU-gated MLP :553-563, residual adds).  K and V land in the
 engine's cache layout [L, 1, kv_heads, max_len, head_dim] at slots [0, P).
 
-Both engines call it with CUDA tensors only; the CPU branch of `_linear` / `_down`
-exists for the CPU parity test against the oracle's prefill (tests/test_prefill.py),
-not as a fallback of the GPU path.
+Both engines call it with CUDA tensors, which run `prefill_native` (the
+library's prefill kernels, csrc/prefill_kernels.cu, between fp16 GEMMs); the
+torch restatement `_prefill` runs only for CPU tensors, for the CPU parity
+test against the oracle's prefill (tests/test_prefill.py), never as a
+fallback of the GPU path.
 
 Weights come in the engine's fused per-layer layout: qkv [4096, 2048] (q
 rows, then k, then v), o [2048, 2048], gate_up [12288, 2048] (gate rows
@@ -80,16 +82,90 @@ def prefill(tokens: torch.Tensor, pos3: torch.Tensor, embed: torch.Tensor, final
             head_dim: int, eps: float, inv_freq: torch.Tensor, mrope_section) -> torch.Tensor:
     """Prefill `tokens` [P] (positions `pos3` [3, P]) into slots [0, P) of
     k_cache/v_cache [L, 1, KVH, Lmax, D]; returns the fp16-valued fp32 logits
-    of the last prompt token [vocab]."""
+    of the last prompt token [vocab].  CUDA tensors take the native path
+    (prefill_native: the library's prefill kernels plus fp16 GEMMs); CPU
+    tensors the torch restatement below (the CPU parity test's path)."""
     # fp16 GEMMs accumulate in fp32 (no reduced-precision split-K reductions)
     flag = torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction
     torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
     try:
-        return _prefill(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, num_heads=num_heads,
-                        num_kv_heads=num_kv_heads, head_dim=head_dim, eps=eps, inv_freq=inv_freq,
-                        mrope_section=mrope_section)
+        fn = prefill_native if embed.is_cuda else _prefill
+        return fn(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, num_heads=num_heads,
+                  num_kv_heads=num_kv_heads, head_dim=head_dim, eps=eps, inv_freq=inv_freq,
+                  mrope_section=mrope_section)
     finally:
         torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = flag
+
+
+def _row_major_down(lw: dict) -> torch.Tensor:
+    """down_proj as [hidden, inter] row-major (the decode engine keeps it
+    K-blocked [k/2048][n][2048] and adds the row-major copy for the prefill)."""
+    w = lw.get("down_rm", lw["down"])
+    if w.dim() == 3:
+        raise ValueError("prefill needs the row-major down_proj ('down_rm')")
+    return w
+
+
+def prefill_native(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, *, num_heads, num_kv_heads, head_dim,
+                   eps, inv_freq, mrope_section):
+    """The prompt in one pass on the GPU, per layer:
+    aicas_prefill_add_rmsnorm_f16 (residual add of the previous layer's down
+    output fused with this layer's input norm), the QKV GEMM,
+    aicas_prefill_qk_norm_rope_kv_f16 (q/k norm + interleaved MRoPE, K/V into
+    the cache), aicas_prefill_attention_f16 (causal flash attention on the
+    tensor cores), the o_proj GEMM, add + post-attention norm, the gate_up
+    GEMM, aicas_prefill_silu_mul_f16 and the down GEMM.  The GEMMs are plain
+    fp16 x fp16 -> fp16 with fp32 accumulation (torch.matmul = cuBLAS), at
+    the roofline the bench reports (prefill is ~96% GEMM FLOPs)."""
+    import ctypes
+
+    from _native import check, lib
+
+    L = lib()
+    dev = embed.device
+    tokens = tokens.to(dev).reshape(-1)
+    P = tokens.numel()
+    pos3 = pos3.to(device=dev, dtype=torch.int64).reshape(3, P).contiguous()
+    inv = inv_freq.to(device=dev, dtype=torch.float32).contiguous()
+    hid = embed.shape[1]
+    qs = num_heads * head_dim
+    max_len = k_cache.shape[-2]
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    f16 = dict(dtype=torch.float16, device=dev)
+    h = embed[tokens].contiguous()
+    x = torch.empty((P, hid), **f16)
+    q = torch.empty((P, qs), **f16)
+    attn = torch.empty((P, qs), **f16)
+    act = None
+    delta = None
+    for li, lw in enumerate(layers):
+        check(L.aicas_prefill_add_rmsnorm_f16(p(h), None if delta is None else p(delta), p(lw["ln1"]), p(h), p(x),
+                                              P, hid, float(eps), stream), "aicas_prefill_add_rmsnorm_f16")
+        qkv = x @ lw["qkv"].t()
+        kc, vc = k_cache[li], v_cache[li]  # [1, KVH, Lmax, D]: written in place
+        if not (kc.is_contiguous() and vc.is_contiguous()):
+            raise ValueError("prefill writes the cache in place: each layer's K/V must be contiguous")
+        check(L.aicas_prefill_qk_norm_rope_kv_f16(p(qkv), p(lw["qn"]), p(lw["kn"]), p(pos3), p(inv),
+                                                  int(mrope_section[1]), int(mrope_section[2]), p(q), p(kc), p(vc),
+                                                  P, 0, max_len, num_heads, num_kv_heads, float(eps), stream),
+              "aicas_prefill_qk_norm_rope_kv_f16")
+        check(L.aicas_prefill_attention_f16(p(q), p(kc), p(vc), p(attn), P, 0, num_heads, num_kv_heads, max_len,
+                                            float(head_dim ** -0.5), stream), "aicas_prefill_attention_f16")
+        o = attn @ lw["o"].t()
+        check(L.aicas_prefill_add_rmsnorm_f16(p(h), p(o), p(lw["ln2"]), p(h), p(x), P, hid, float(eps), stream),
+              "aicas_prefill_add_rmsnorm_f16")
+        gu = x @ lw["gate_up"].t()
+        inter = gu.shape[1] // 2
+        if act is None:
+            act = torch.empty((P, inter), **f16)
+        check(L.aicas_prefill_silu_mul_f16(p(gu), p(act), P, inter, stream), "aicas_prefill_silu_mul_f16")
+        delta = act @ _row_major_down(lw).t()
+    # last token: residual add + final norm + tied lm_head
+    xl = torch.empty((1, hid), **f16)
+    check(L.aicas_prefill_add_rmsnorm_f16(p(h[-1:]), p(delta[-1:]), p(final_norm), None, p(xl), 1, hid, float(eps),
+                                          stream), "aicas_prefill_add_rmsnorm_f16")
+    return (xl @ embed.t())[0].to(torch.float32)
 
 
 def _prefill(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, *, num_heads, num_kv_heads, head_dim, eps,

@@ -41,12 +41,34 @@ UNIT = "tok/s"
 FALLBACK_HBM_GBS = 6650.0
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
 def measured_peak_gbs():
     p = REPO / "MEASURED_PEAKS.json"
     try:
         return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_peak_tflops():
+    """Dense 16-bit tensor-core peak (the driver's cuBLAS bf16 burst figure;
+    fp16 runs at the same rate)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def prefill_flops(shape, P: int) -> float:
+    """Dense FLOPs of a P-token prefill: the projection GEMMs of every layer,
+    causal attention (Q K^T and P V over the keys each query sees) and the
+    LM head of the last token."""
+    proj = shape.hidden * (shape.qkv_rows + shape.q_size) + shape.hidden * 3 * shape.intermediate
+    attn = 2 * 2 * shape.num_heads * shape.head_dim * (P * (P + 1) // 2)
+    return float(shape.num_layers * (2 * P * proj + attn) + 2 * shape.vocab * shape.hidden)
 
 
 def headline_request(rank: int = 0):
@@ -193,6 +215,12 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def host_threads(world: int) -> int:
+    """Host threads one rank uses for its setup work (weight generation): its
+    share of the cores, so N ranks on one box do not oversubscribe them."""
+    return max(1, (os.cpu_count() or 1) // max(1, world))
+
+
 def max_over_ranks(vals, world: int):
     """Per-rank timings -> their maximum over all ranks (every rank gets it).
     Under torchrun each rank decodes its own request on its own GPU; the job
@@ -259,7 +287,7 @@ def run_ours(args, rank: int, world: int):
 
     t_setup = time.perf_counter()
     shape = QWEN3VL_2B.with_layers(args.layers)
-    st = synthetic_state(shape, seed=0, dtype=torch.float16)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16, threads=host_threads(world))
     eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev,
                               max_steps=PREFIX + NEW + 8)
     prompt, pos3, _ = headline_request(rank)
@@ -344,6 +372,8 @@ def run_ours(args, rank: int, world: int):
     p1.record()
     torch.cuda.synchronize(dev)
     ttft_gemm_ms = p0.elapsed_time(p1) / 3
+    pf_flops = prefill_flops(shape, PREFIX)
+    tpeak, tpeak_kind = measured_peak_tflops()
 
     # ---- max over ranks (and each rank's own figures: its GPU and its work)
     ranks = per_rank_report(gather_ranks([rank, dev.index, ms, setup_s], world), args.steps * NEW)
@@ -375,7 +405,12 @@ def run_ours(args, rank: int, world: int):
         "per_rank": ranks,
         "ttft": {"prefix_tokens": PREFIX, "one_pass_prefill_ms": ttft_gemm_ms,
                  "decode_kernel_prefill_ms": ttft_decode_ms,
-                 "note": "first token of the 1024-token prefix; outside the decode metric"},
+                 "roofline": {"bound": "tensor", "flops": pf_flops,
+                              "achieved_tflops": pf_flops / (ttft_gemm_ms * 1e-3) / 1e12, "peak": tpeak,
+                              "peak_kind": tpeak_kind, "unit": "TFLOP/s",
+                              "frac": pf_flops / (ttft_gemm_ms * 1e-3) / 1e12 / tpeak},
+                 "note": "first token of the 1024-token prefix (prefill_native: hand-written prefill kernels "
+                         "between cuBLAS fp16 GEMMs); outside the decode metric"},
         "clocks": clocks,
     }
     if args.layers != QWEN3VL_2B.num_layers:
@@ -441,7 +476,7 @@ def run_batch(args, rank: int, world: int):
     B = args.batch
     ctx = batch_contexts(B, rank)
     shape = QWEN3VL_2B.with_layers(args.layers)
-    st = synthetic_state(shape, seed=0, dtype=torch.float16)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16, threads=host_threads(world))
     lmax = max(ctx) + BATCH_NEW + 8
     eng = Qwen3VLBatchDecodeEngine(st, shape, max_batch=B, max_cache_len=lmax, device=dev, max_steps=lmax)
     firsts, pos_next = [], []

@@ -233,6 +233,44 @@ AICAS_API int aicas_decode_batch_trace_f16(const AicasPhase* device_phases, int 
  * (dst must not overlap w; n % 8 == 0, k % 2048 == 0). */
 AICAS_API int aicas_tile_weight_f16(const void* w, void* dst, int64_t n, int64_t k, aicas_stream_t stream);
 
+/* ---- one-pass prompt prefill (the kernels between the prefill's GEMMs) ---
+ *
+ * The reference prefills a prompt with HF's forward over all prompt tokens
+ * (evaluation_wrapper.py:1836-1958; OptimizedDecoderLayer.prefill_forward_no_mask,
+ * optimized_layer.py:471-619).  The projections are dense fp16 GEMMs with fp32
+ * accumulation, run by the caller's GEMM library; these four entry points are
+ * the rest of a prefill layer, with HF's fp16 rounding points, writing K and V
+ * into the decode engine's StaticLayer-layout cache.  Row-major fp16 tensors,
+ * 16-byte aligned. */
+
+/* h_out = r16(h + delta) (delta may be null: h_out = h; h_out may be null or
+ * alias h); x_out = RMSNorm(h_out) * norm_w with HF's rounding points.
+ * [rows, cols], cols % 8 == 0, cols <= 8192. */
+AICAS_API int aicas_prefill_add_rmsnorm_f16(const void* h, const void* delta, const void* norm_w, void* h_out,
+                                            void* x_out, int64_t rows, int64_t cols, float eps,
+                                            aicas_stream_t stream);
+/* qkv [rows, (q_heads + 2 kv_heads) * 128]: per-head RMSNorm of q and k
+ * (q_norm_w / k_norm_w [128]) and interleaved MRoPE from pos3 [3, rows]
+ * (int64 t, h, w positions; inv_freq [64] fp32; sections sec1 / sec2 of the
+ * h and w axes); q to q_out [rows, q_heads, 128], k and v to cache slots
+ * start .. start + rows - 1 of k_cache / v_cache [kv_heads, max_len, 128]. */
+AICAS_API int aicas_prefill_qk_norm_rope_kv_f16(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                                const void* pos3, const void* inv_freq, int sec1, int sec2,
+                                                void* q_out, void* k_cache, void* v_cache, int64_t rows,
+                                                int64_t start, int64_t max_len, int64_t q_heads, int64_t kv_heads,
+                                                float eps, aicas_stream_t stream);
+/* act [rows, inter] = r16(r16(SiLU(gate)) * up) of gate_up [rows, 2 inter]
+ * (gate columns first). */
+AICAS_API int aicas_prefill_silu_mul_f16(const void* gate_up, void* act, int64_t rows, int64_t inter,
+                                         aicas_stream_t stream);
+/* Causal GQA attention of `rows` queries (q [rows, q_heads, 128], query t at
+ * cache slot start + t) over cache slots [0, start + t]:
+ * out [rows, q_heads, 128] fp16.  Flash form on the tensor cores (fp16
+ * operands, fp32 scores, online softmax, fp32 accumulation). */
+AICAS_API int aicas_prefill_attention_f16(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                          int64_t rows, int64_t start, int64_t q_heads, int64_t kv_heads,
+                                          int64_t max_len, float scale, aicas_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
