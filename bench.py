@@ -185,6 +185,37 @@ def _cpu_oracle_decode(state16, seconds, min_steps, max_steps):
     return n / el, n, el
 
 
+def cpu_hf_decode(state16, steps: int, warmup: int):
+    """The reference's own CPU path: HF's Qwen3-VL model in fp32 on the host
+    cores (what `GreedyDecodeEngine` runs with ENABLE_CUDAGRAPH=0,
+    evaluation_wrapper.py:149-315, 513-539), prefilled with the headline
+    request's 1024-token vision-grid prefix into a StaticCache, then `steps`
+    timed single-token steps through HF's forward.  Returns (tok/s, steps, s)."""
+    import torch
+    from transformers.cache_utils import StaticCache
+
+    from qwen3vl_config import QWEN3VL_2B, hf_model
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    m = hf_model(QWEN3VL_2B, state=state16)
+    prompt, pos3, rd = headline_request(0)
+    with torch.no_grad():
+        cache = StaticCache(config=m.config, max_cache_len=PREFIX + warmup + steps + 1)
+        out = m(input_ids=prompt.view(1, PREFIX), position_ids=pos3.view(3, 1, PREFIX), past_key_values=cache,
+                use_cache=True, logits_to_keep=1)
+        tok = int(out.logits[0, -1].argmax())
+        t0, n = 0.0, 0
+        for i in range(warmup + steps):
+            if i == warmup:
+                t0 = time.perf_counter()
+            p = torch.full((3, 1, 1), PREFIX + i + rd, dtype=torch.long)
+            out = m(input_ids=torch.tensor([[tok]]), position_ids=p, past_key_values=cache, use_cache=True)
+            tok = int(out.logits[0, -1].argmax())
+            n += i >= warmup
+        el = time.perf_counter() - t0
+    return n / el, n, el
+
+
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
@@ -196,9 +227,17 @@ def run_reference(args, rank: int, world: int):
     torch.set_num_threads(cores)
     st = synthetic_state(QWEN3VL_2B, seed=0, dtype=torch.float16)
     # warm-up steps then exactly K timed steps; each step = 1 decode token at ctx ~1024
-    tps_w, _, _ = cpu_oracle_decode(st, seconds=0.0, min_steps=max(1, args.warmup), max_steps=max(1, args.warmup))
-    tps, n, el = cpu_oracle_decode(st, seconds=0.0, min_steps=args.steps, max_steps=args.steps)
-    sample = f"{n} decode tokens at cache slot {PREFIX}+ over a synthetic 1024-slot KV prefix (numpy fp32 port)"
+    if args.ref_path == "hf":
+        tps, n, el = cpu_hf_decode(st, args.steps, max(1, args.warmup))
+        sample = (f"{n} decode tokens after the 1024-token vision-grid prefix, HF transformers fp32 forward with a "
+                  f"StaticCache (the reference's CPU path)")
+        kind = "reference"
+    else:
+        tps_w, _, _ = cpu_oracle_decode(st, seconds=0.0, min_steps=max(1, args.warmup),
+                                        max_steps=max(1, args.warmup))
+        tps, n, el = cpu_oracle_decode(st, seconds=0.0, min_steps=args.steps, max_steps=args.steps)
+        sample = f"{n} decode tokens at cache slot {PREFIX}+ over a synthetic 1024-slot KV prefix (numpy fp32 port)"
+        kind = "port"
     metric, config = METRIC, workload_config(world)
     if args.batch > 1:  # the reference decodes one request at a time: its batched rate is its per-token rate
         metric = f"batch-{args.batch} decode tok/s"
@@ -208,9 +247,10 @@ def run_reference(args, rank: int, world: int):
         "impl": "reference", "metric": metric, "value": tps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * el / n, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
-        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "reference arm: CPU oracle port of the reference's HF decode step; a step here is one token",
+        "note": ("reference arm: the reference's HF fp32 decode on the host cores" if kind == "reference" else
+                 "reference arm: CPU oracle port of the reference's HF decode step") + "; a step here is one token",
     }
     print(json.dumps(line), flush=True)
 
@@ -264,9 +304,9 @@ def job_throughput(steps: int, world: int, ms: float) -> float:
 # --------------------------------------------------------------------------- GPU
 # DRAM bytes per algorithmic byte of decode_program_kernel, from one
 # `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
-# summarised under profiles/): (1.043518e9 + 10.825984e6) / 1043908608.  The
+# summarised under profiles/): (1.043186e9 + 9.19424e6) / 1043908608.  The
 # per-layer shapes equal the headline model's, so the ratio carries over.
-DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0099964
+DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0081153
 
 def run_ours(args, rank: int, world: int):
     import torch
@@ -395,7 +435,7 @@ def run_ours(args, rank: int, world: int):
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_req / NEW,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 4-layer "
-                                       "launch (1.0435 GB + 10.8 MB vs 1.0439 GB algorithmic), scaled to this "
+                                       "launch (1.0432 GB + 9.2 MB vs 1.0439 GB algorithmic), scaled to this "
                                        "launch by algorithmic bytes",
                      "kernel": "decode_program_kernel (one launch per token)",
                      "algorithmic_bytes_per_launch": bytes_req / NEW},
@@ -725,6 +765,62 @@ def run_op(args, rank: int, world: int):
         Path(args.op_out).write_text("\n".join(json.dumps(x) for x in lines) + "\n")
 
 
+def run_prefill_op(args, rank: int, world: int):
+    """Time to first token of the headline request's 1024-token prefix (16x16
+    vision grid) through the native one-pass prefill (engine.prefill_prompt ->
+    prefill_native), 28 layers: ms per prefill (CUDA events), its dense-FLOP
+    roofline against the measured 16-bit tensor peak, and the CPU oracle's
+    prefill of the same prompt as the baseline."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    from engine import Qwen3VLDecodeEngine, hf_inv_freq
+    from oracle.qwen3vl_oracle import Qwen3VLOracle
+    from qwen3vl_config import QWEN3VL_2B, synthetic_state
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    shape = QWEN3VL_2B.with_layers(args.layers)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16)
+    eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev, max_steps=PREFIX + NEW + 8)
+    prompt, pos3, _ = headline_request(0)
+    for _ in range(args.warmup):
+        eng.prefill_prompt(prompt, pos3)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        first = eng.prefill_prompt(prompt, pos3)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = prefill_flops(shape, PREFIX)
+    tpeak, tpeak_kind = measured_peak_tflops()
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "prefill time to first token", "value": ms, "unit": "ms", "higher_is_better": False,
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic", "first_token": first,
+            "config": {"workload": f"BASELINE config 4 prefix: {PREFIX}-token prompt (16x16 vision grid, 3-axis "
+                                   f"MRoPE), {shape.num_layers} layers, one-pass native prefill"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": achieved / tpeak, "peak_kind": tpeak_kind, "flops": flops}}
+    if not args.no_cpu_baseline and args.layers == QWEN3VL_2B.num_layers:
+        from threadpoolctl import threadpool_limits
+
+        with threadpool_limits(limits=os.cpu_count() or 1):
+            o = Qwen3VLOracle(st, shape.num_layers, mode="fp32", max_cache_len=PREFIX + 8,
+                              inv_freq=hf_inv_freq(shape).numpy())
+            t0 = time.perf_counter()
+            logits = o.prefill(prompt.numpy(), pos3.numpy())
+            el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 1000 * el, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
+                                "sample": "one prefill of the same prompt, numpy fp32 oracle port, all host threads",
+                                "first_token": int(np.argmax(logits))}
+    print(json.dumps(line), flush=True)
+
+
 def write_trace_summary(eng, start_state, path):
     """One traced decode step at cache slot 1024.  Per phase kind (summed
     over layers, averaged over CTAs): time waiting for inputs, time from
@@ -765,6 +861,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-path", choices=["port", "hf"], default="port",
+                    help="--impl reference: time the numpy oracle port (default) or HF transformers' own fp32 "
+                         "forward (the reference's CPU path; needs transformers)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--trace", default="", help="write a per-phase timeline summary (JSON) to this path")
     ap.add_argument("--batch", type=int, default=1,
@@ -772,15 +871,17 @@ def main():
                          "decode of ragged requests (contexts U[512, 4096], 512 decode steps each)")
     ap.add_argument("--layers", type=int, default=28,
                     help="profiling case only: a smaller model (the headline is 28 layers)")
-    ap.add_argument("--op", choices=["gemv", "attention"], default=None,
+    ap.add_argument("--op", choices=["gemv", "attention", "prefill"], default=None,
                     help="per-op benchmark instead of the decode step: BASELINE config 2 (the five decode GEMV "
-                         "shapes) or config 3 (decode attention at valid lengths 128..8192); --steps = graph "
-                         "replays of one call per copy")
+                         "shapes), config 3 (decode attention at valid lengths 128..8192; --steps = graph "
+                         "replays of one call per copy), or the headline prefix's one-pass prefill (TTFT)")
     ap.add_argument("--op-out", default="", help="also write the op benchmark's JSON lines to this file")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.op:
+    if args.op == "prefill":
+        run_prefill_op(args, rank, world)
+    elif args.op:
         run_op(args, rank, world)
     elif args.impl == "reference":
         run_reference(args, rank, world)
