@@ -17,6 +17,7 @@ LIB_PATH = Path(os.environ.get("AICAS_LIB", str(HERE / "libaicas_decode.so")))
 
 # Phase kinds / flags (include/aicas_phase_program.h)
 PH_GEMV, PH_GATEUP, PH_ATTN, PH_LMHEAD = 1, 2, 3, 4
+PROGRAM_LEAN = 1  # aicas_decode_program_ex_f16 flag: the lean kernel instantiation
 F_NORM = 1 << 0
 F_X_EMBED = 1 << 1
 F_RESID = 1 << 2
@@ -109,6 +110,8 @@ SIGNATURES = {
     "aicas_lm_head_argmax_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P]),
     "aicas_decode_program_f16": (_I, [_P, _I, _P, _P, _P]),
     "aicas_decode_program_trace_f16": (_I, [_P, _I, _P, _P, _P, _P]),
+    "aicas_lean_program_ok": (_I, [ctypes.POINTER(AicasPhase), _I, _I]),
+    "aicas_decode_program_ex_f16": (_I, [_P, _I, _P, _P, _P, _I, _P]),
     "aicas_batch_scratch_bytes": (ctypes.c_size_t, []),
     "aicas_validate_batch_phases": (_I, [ctypes.POINTER(AicasPhase), _I]),
     "aicas_decode_batch_f16": (_I, [_P, _I, _P, _I, _P, _P]),

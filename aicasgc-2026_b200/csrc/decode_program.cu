@@ -76,11 +76,25 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 #ifndef AICAS_L2_WARP
 #define AICAS_L2_WARP 0
 #endif
-// Warp roles: 0 producer, 1..8 consumers, then the L2 prefetch warp (if
-// enabled), then the TMEM mover (last warp).
+// AICAS_KV_STAGES: attention K/V tiles land in their own shared-memory
+// stages (this many, >= 2: the consumers take tiles in pairs), filled by their
+// own producer warp, so a KV tile that waits for its phase's queries never
+// holds a stage of the weight ring; 0 sends them through the weight ring in
+// schedule order (the weight stream then stalls behind every attention
+// phase).
+#ifndef AICAS_KV_STAGES
+#define AICAS_KV_STAGES 2
+#endif
+constexpr int kKvStages = AICAS_KV_STAGES;
+constexpr bool kKvSplit = kKvStages > 0;
+constexpr int kKvRing = kKvSplit ? kKvStages : 1;  // divisor of the K/V stage index (1 when unused)
+static_assert(kKvStages == 0 || kKvStages >= 2, "attention tiles are consumed in pairs");
+// Warp roles: 0 weight producer, 1..8 consumers, then the L2 prefetch warp
+// (if enabled), the TMEM mover, and the KV producer (with AICAS_KV_STAGES).
 constexpr int kL2Warp = 1 + kConsumerWarps;
 constexpr int kMoverWarp = 1 + kConsumerWarps + (AICAS_L2_WARP ? 1 : 0);
-constexpr int kThreads = 32 * (kMoverWarp + 1);
+constexpr int kKvWarp = kMoverWarp + 1;
+constexpr int kThreads = 32 * (kMoverWarp + 1 + (kKvSplit ? 1 : 0));
 // Tensor memory: an 8-slot ring of GEMV tiles (64 columns x 128 lanes each).
 constexpr int kTmemSlots = 8;
 constexpr int kTmemCols = 512;
@@ -122,6 +136,7 @@ struct AttnSmem {
 
 struct __align__(128) Smem {
   uint8_t ring[kStages][kStageBytes];
+  uint8_t kv[kKvSplit ? kKvStages : 1][kKvSplit ? kStageBytes : 16];  // attention K/V stages
   __half nw[AICAS_MAX_K];  // norm weights of the running phase (prefetched before its barrier)
   AttnSmem at;
   __half xs[kChunk];            // C == 1 phases: the input vector, shared by the 8 warps
@@ -137,6 +152,8 @@ struct __align__(128) Smem {
   uint64_t cempty[kStages];  // consumers done with a stage they read directly (attention, partial chunks)
   uint64_t tfull[kTmemSlots];   // TMEM slot filled (tcgen05.commit of the mover)
   uint64_t tempty[kTmemSlots];  // TMEM slot read by all 8 consumer warps
+  uint64_t kvfull[kKvSplit ? kKvStages : 1];   // K/V stage landed
+  uint64_t kvempty[kKvSplit ? kKvStages : 1];  // K/V stage read by its 4 consumer warps (2 arrivals each)
   uint64_t cdone;               // all consumer warps finished the program (TMEM may be freed)
   uint32_t ring_it;  // tiles the producer has issued (read by the L2 prefetch warp)
   uint32_t tmem_base;  // TMEM address of the slot ring (written by tcgen05.alloc)
@@ -222,8 +239,20 @@ __device__ __forceinline__ int tiles_per_group(const AicasPhase& d) {
 constexpr int kMaxCmajorGroups = 2;
 // split-KV merge: splits whose partial words one merging lane polls per round
 constexpr int kMergePer = 4;
-__device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
+__host__ __device__ __forceinline__ bool chunk_major(int C, int kind, int groups) {
   return C > 1 && kind != AICAS_PH_GATEUP && groups <= kMaxCmajorGroups;
+}
+
+// A GEMV-type phase the lean kernel runs: whole 2048-column chunks (TMEM
+// path), and either one chunk (row-major tile order) or three in chunk-major
+// order on every CTA of an `nct`-CTA grid.
+__host__ __device__ __forceinline__ bool lean_phase(const AicasPhase& d, int nct) {
+  if (d.kind == AICAS_PH_ATTN) return true;
+  if (d.k % kChunk != 0) return false;
+  const int C = d.k / kChunk;
+  if (C == 1) return true;
+  const int groups = (d.n + kRows - 1) / kRows;
+  return C == 3 && chunk_major(C, d.kind, (groups + nct - 1) / nct);
 }
 
 // ---------------------------------------------------------------------------
@@ -254,12 +283,15 @@ struct TileDesc {
 };
 
 // Walks this CTA's tiles of a program in the exact order the consumers
-// take them.  The producer, the TMEM mover and the L2 prefetch warp each run
-// one cursor.
+// take them.  The producer, the TMEM mover, the L2 prefetch warp and the KV
+// producer each run one cursor; `sel` picks the tiles it yields.
+enum { kAllTiles = 0, kWeightTiles = 1, kKvTiles = 2 };
+constexpr int kRingSel = kKvSplit ? kWeightTiles : kAllTiles;
 struct TileCursor {
   const AicasPhase* P;
   int n_phases;
   int nct, cta;
+  int sel;
   int ph = -1;
   int ti = 0, n = 0;
   // cached per-phase schedule
@@ -290,6 +322,7 @@ struct TileCursor {
       rows_total = kind == AICAS_PH_GATEUP ? 2 * d.n : d.n;
       n = rg.count * T;
     }
+    if (sel != kAllTiles && (sel == kKvTiles) != (kind == AICAS_PH_ATTN)) n = 0;
   }
 
   // Next tile; false when the program is exhausted.
@@ -367,7 +400,7 @@ constexpr int kL2Ahead = AICAS_L2_AHEAD;
 __device__ __forceinline__ void run_l2_prefetcher(const ProgramArgs& a, Smem& sm, const StepIn& in) {
   const int lane = threadIdx.x & 31;
   const AicasPhase* P = a.phases ? a.phases : a.inl;
-  TileCursor pf{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+  TileCursor pf{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x, kRingSel};
   TileDesc td;
   const uint64_t pol_last = l2_evict_last_policy();
   for (uint32_t k = 0; pf.next(in, td); ++k) {
@@ -409,7 +442,7 @@ __device__ __forceinline__ void run_mover(const ProgramArgs& a, Smem& sm, const 
   AicasScratch* s = a.scratch;
   if (lane == 0) {
     const AicasPhase* P = a.phases ? a.phases : a.inl;
-    TileCursor cur{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+    TileCursor cur{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x, kRingSel};
     TileDesc td;
     uint32_t it = 0, g = 0;
     // cempty[st] completes once per in-place use of stage st (not per use):
@@ -466,7 +499,7 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   const uint64_t pol = l2_evict_first_policy();
   Ring r;
   const AicasPhase* P = a.phases ? a.phases : a.inl;
-  TileCursor ld{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x};
+  TileCursor ld{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x, kRingSel};
   uint64_t slot_wait = 0;  // trace only
   int traced_ph = 0;
   TileDesc td;
@@ -529,10 +562,58 @@ __device__ __forceinline__ void run_producer(const ProgramArgs& a, Smem& sm, con
   }
 }
 
+// KV producer (AICAS_KV_STAGES > 0; lane 0 of its own warp): walks the
+// CTA's attention tiles only and lands each one (K half, V half: two bulk
+// copies) in the next K/V stage.  The weight producer never waits for a
+// KV stage, so HBM keeps streaming weights into the ring and TMEM while the
+// consumers wait for an attention phase's queries; the K/V tiles of the next
+// layer land as soon as this layer's are read.  A stage is armed again only
+// after its 8 consumer arrivals AND its previous copy's completion (an
+// aborted consumer may arrive early), and every issued copy lands before
+// the warp exits.
+__device__ __forceinline__ void run_kv_producer(const ProgramArgs& a, Smem& sm, const StepIn& in) {
+  if (!kKvSplit || (threadIdx.x & 31) != 0) return;
+  AicasScratch* s = a.scratch;
+  const uint64_t pol = l2_evict_first_policy();
+  const AicasPhase* P = a.phases ? a.phases : a.inl;
+  TileCursor ld{P, a.n_phases, (int)gridDim.x, (int)blockIdx.x, kKvTiles};
+  TileDesc td;
+  uint32_t it = 0;
+  while (ld.next(in, td)) {
+    const int st = it % kKvRing;
+    const uint32_t round = it / kKvRing;
+    if (round > 0) {
+      const uint32_t prev = (round - 1) & 1u;
+      if (!mbar_wait_bounded(&sm.kvempty[st], prev, s, kErrEmptyTimeout)) break;
+      if (!mbar_wait_copy(&sm.kvfull[st], prev, s, kErrDrainTimeout)) break;
+    }
+    mbar_arrive_expect_tx(&sm.kvfull[st], td.pieces * td.bytes);
+    for (int i = 0; i < td.pieces; ++i)
+      bulk_g2s(sm.kv[st] + i * td.dst_stride, td.src + i * td.src_stride, td.bytes, &sm.kvfull[st], pol);
+    ++it;
+  }
+  const uint32_t first = it > (uint32_t)kKvRing ? it - kKvRing : 0;
+  for (uint32_t k = first; k < it; ++k) {
+    const int st = k % kKvRing;
+    if (!mbar_wait_bounded(&sm.kvfull[st], (k / kKvRing) & 1u, s, kErrDrainTimeout)) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.kvfull[st], (k / kKvRing) & 1u)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Consumers (warps 1..8)
 // ---------------------------------------------------------------------------
-template <bool kTrace>
+// kLean: the instantiation for programs whose every GEMV-type phase streams
+// whole 2048-column chunks through TMEM with k = 2048 (row-major tile order)
+// or k = 6144 (chunk-major, <= 2 row groups per CTA) -- the engine's 28-layer
+// program.  It carries none of the other tile paths: the kernel's executed
+// code is smaller, and on B200 the step is sensitive to instruction-cache
+// misses (same-box A/B on the 28-layer step: 972 -> 955 us per token).
+template <bool kTrace, bool kLean>
 struct Consumer {
   const ProgramArgs& a;
   Smem& sm;
@@ -572,6 +653,16 @@ struct Consumer {
     }
     mbar_wait_bounded(&sm.full[st], round & 1u, s, kErrFullTimeout);
   }
+  uint32_t kv_it = 0;  // K/V tiles consumed so far (AICAS_KV_STAGES)
+  __device__ __forceinline__ void wait_kv(int st, uint32_t round) {
+    if (kTrace && tid == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      mbar_wait_bounded(&sm.kvfull[st], round & 1u, s, kErrFullTimeout);
+      wait_ns += globaltimer_ns() - t0;
+      return;
+    }
+    mbar_wait_bounded(&sm.kvfull[st], round & 1u, s, kErrFullTimeout);
+  }
   __device__ __forceinline__ void wait_full(int st) {
     if (kTrace && tid == 0) {
       const uint64_t t0 = globaltimer_ns();
@@ -594,10 +685,10 @@ struct Consumer {
     if (kTrace && tid == 0) {
       int64_t* t = a.trace + ((size_t)cta * a.n_phases + phase) * kTraceFields;
       t[which] = (int64_t)globaltimer_ns();
-      if (which == 0) it_at_start = r.it;
+      if (which == 0) it_at_start = r.it + kv_it;
       if (which == 2) {
         t[3] = (int64_t)wait_ns;
-        t[5] = (int64_t)(r.it - it_at_start);
+        t[5] = (int64_t)(r.it + kv_it - it_at_start);
         wait_ns = 0;
       }
     }
@@ -878,7 +969,7 @@ struct Consumer {
     unsigned jlast = 0;
 #pragma unroll
     for (int j = 0; j < kVec; ++j) jlast |= (colv(j) < last_len ? 1u : 0u) << j;
-    const bool use_tm = tmem_phase(kind, k);
+    const bool use_tm = kLean || tmem_phase(kind, k);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     __half* logits = nullptr;
@@ -1041,7 +1132,7 @@ struct Consumer {
   __device__ __forceinline__ void run_matvec(const AicasPhase& d) {
     const int C = n_chunks(d);
     if (C == 1) matvec<1>(d);
-    else if (C == 2) matvec<2>(d);
+    else if (!kLean && C == 2) matvec<2>(d);
     else matvec<3>(d);
   }
 
@@ -1117,7 +1208,6 @@ struct Consumer {
     for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
     const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
     float xn[4];
-#pragma unroll
     const __half2* nh = reinterpret_cast<const __half2*>(&nw);
     const float nwf[4] = {__low2float(nh[0]), __high2float(nh[0]), __low2float(nh[1]), __high2float(nh[1])};
 #pragma unroll
@@ -1415,14 +1505,23 @@ struct Consumer {
 #pragma unroll 1
       for (int t = 0; t < nseg; t += 2) {
         if (t + slot < nseg) {
-          const uint32_t ri = r.it + slot;
-          const int st = ri % kStages;
-          wait_full_at(st, ri / kStages);
-          attend_tile(sm.ring[st], (j0 + t + slot) * kAttnChunk + 16 * wq, kpos, valid, scale, m, l, acc);
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cnt(&sm.cempty[st], 2);  // 4 warps per tile, 8 arrivals per stage use
+          if (kKvSplit) {
+            const uint32_t ri = kv_it + slot;
+            const int st = ri % kKvRing;
+            wait_kv(st, ri / kKvRing);
+            attend_tile(sm.kv[st], (j0 + t + slot) * kAttnChunk + 16 * wq, kpos, valid, scale, m, l, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&sm.kvempty[st], 2);  // 4 warps per tile, 8 arrivals per stage use
+          } else {
+            const uint32_t ri = r.it + slot;
+            const int st = ri % kStages;
+            wait_full_at(st, ri / kStages);
+            attend_tile(sm.ring[st], (j0 + t + slot) * kAttnChunk + 16 * wq, kpos, valid, scale, m, l, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&sm.cempty[st], 2);  // 4 warps per tile, 8 arrivals per stage use
+          }
         }
-        r.it += t + 1 < nseg ? 2 : 1;
+        (kKvSplit ? kv_it : r.it) += t + 1 < nseg ? 2 : 1;
       }
       stamp_field(6);
       // merge the 8 warps' states of this segment into one partial
@@ -1523,7 +1622,8 @@ struct Consumer {
       }
       stamp(ph, 0);
       if (d.kind == AICAS_PH_ATTN) run_attention(d);
-      else run_matvec(d);
+      else if (!kLean || lean_phase(d, nct)) run_matvec(d);
+      else if (tid == 0) raise_error(s, kErrBadPhase);  // not a lean program: the launch aborts
       stamp(ph, 2);
     }
     // this warp is done with TMEM: the mover may free it
@@ -1544,8 +1644,8 @@ struct Consumer {
 };
 
 // kTrace: the traced variant records per-phase timestamps (a.trace); the
-// plain one carries none of that code.
-template <bool kTrace>
+// plain one carries none of that code.  kLean: see Consumer.
+template <bool kTrace, bool kLean>
 __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __grid_constant__ ProgramArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1567,6 +1667,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
     for (int i = 0; i < kTmemSlots; ++i) {
       mbar_init(&sm.tfull[i], 1);
       mbar_init(&sm.tempty[i], kConsumerWarps);
+    }
+    for (int i = 0; i < (kKvSplit ? kKvStages : 0); ++i) {
+      mbar_init(&sm.kvfull[i], 1);
+      mbar_init(&sm.kvempty[i], kConsumerWarps);
     }
     mbar_init(&sm.cdone, kConsumerWarps);
     sm.ring_it = 0;
@@ -1593,6 +1697,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
     run_mover(a, sm, in, tmem);
     return;
   }
+  if (kKvSplit && warp == kKvWarp) {
+    run_kv_producer(a, sm, in);
+    return;
+  }
   if (AICAS_L2_WARP && warp == kL2Warp) {
     run_l2_prefetcher(a, sm, in);
     return;
@@ -1601,7 +1709,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_program_kernel(const __gri
     run_producer<kTrace>(a, sm, in);
     return;
   }
-  Consumer<kTrace> c{a, sm, in, a.scratch};
+  Consumer<kTrace, kLean> c{a, sm, in, a.scratch};
   c.tid = threadIdx.x - 32;
   c.w = warp - 1;
   c.lane = threadIdx.x & 31;
@@ -1643,9 +1751,11 @@ static int device_setup(int* dev_out) {
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
   if (!g_attr_done[dev]) {
-    for (int v = 0; v < 2; ++v) {
-      const void* fn = v ? reinterpret_cast<const void*>(decode_program_kernel<true>)
-                         : reinterpret_cast<const void*>(decode_program_kernel<false>);
+    const void* fns[4] = {reinterpret_cast<const void*>(decode_program_kernel<false, false>),
+                          reinterpret_cast<const void*>(decode_program_kernel<true, false>),
+                          reinterpret_cast<const void*>(decode_program_kernel<false, true>),
+                          reinterpret_cast<const void*>(decode_program_kernel<true, true>)};
+    for (const void* fn : fns) {
       cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
       if (e != cudaSuccess) return cuda_fail(e);
       int per_sm = 0;
@@ -1701,7 +1811,7 @@ static int validate_phase(const AicasPhase& d) {
   }
 }
 
-static int launch_program(ProgramArgs& a, cudaStream_t stream) {
+static int launch_program(ProgramArgs& a, cudaStream_t stream, bool lean = false) {
   int dev;
   int rc = device_setup(&dev);
   if (rc) return rc;
@@ -1726,8 +1836,11 @@ static int launch_program(ProgramArgs& a, cudaStream_t stream) {
   attr[0].val.cooperative = g_cooperative;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = a.trace ? cudaLaunchKernelEx(&cfg, decode_program_kernel<true>, a)
-                          : cudaLaunchKernelEx(&cfg, decode_program_kernel<false>, a);
+  cudaError_t e;
+  if (lean) e = a.trace ? cudaLaunchKernelEx(&cfg, decode_program_kernel<true, true>, a)
+                        : cudaLaunchKernelEx(&cfg, decode_program_kernel<false, true>, a);
+  else e = a.trace ? cudaLaunchKernelEx(&cfg, decode_program_kernel<true, false>, a)
+                   : cudaLaunchKernelEx(&cfg, decode_program_kernel<false, false>, a);
   return e == cudaSuccess ? AICAS_OK : cuda_fail(e);
 }
 
@@ -1824,6 +1937,27 @@ AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, in
   a.scratch = reinterpret_cast<AicasScratch*>(scratch);
   a.trace = trace;
   return launch_program(a, stream);
+}
+
+AICAS_API int aicas_lean_program_ok(const AicasPhase* phases, int n_phases, int num_ctas) {
+  if (!phases || n_phases < 1 || num_ctas < 1) return AICAS_ERR_ARG;
+  for (int i = 0; i < n_phases; ++i)
+    if (!lean_phase(phases[i], num_ctas)) return AICAS_ERR_SHAPE;
+  return AICAS_OK;
+}
+
+AICAS_API int aicas_decode_program_ex_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
+                                          void* scratch, int64_t* trace, int flags, cudaStream_t stream) {
+  if (!device_phases || n_phases < 1 || !state) return AICAS_ERR_ARG;
+  if (flags & ~AICAS_PROGRAM_LEAN) return AICAS_ERR_ARG;
+  ProgramArgs a;
+  memset(&a, 0, sizeof(a));
+  a.phases = device_phases;
+  a.n_phases = n_phases;
+  a.state = state;
+  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
+  a.trace = trace;
+  return launch_program(a, stream, (flags & AICAS_PROGRAM_LEAN) != 0);
 }
 
 AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,

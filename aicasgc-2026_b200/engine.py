@@ -34,8 +34,8 @@ import math
 import torch
 
 from _native import (F_KBLOCKED, F_LL_IN, F_LL_OUT, F_LL_RESID, F_NORM, F_RESID, F_RESID_EMBED, F_X_EMBED,
-                     PH_ATTN, PH_GATEUP, PH_GEMV, PH_LMHEAD, AicasError, AicasPhase, AicasStepState, check, lib,
-                     scratch_bytes)
+                     PH_ATTN, PH_GATEUP, PH_GEMV, PH_LMHEAD, PROGRAM_LEAN, AicasError, AicasPhase, AicasStepState,
+                     check, lib, scratch_bytes)
 from _ops import device_error
 from qwen3vl_config import QWEN3VL_2B, Qwen3VLTextShape
 
@@ -184,6 +184,9 @@ class Qwen3VLDecodeEngine:
                   x_src=5 * s.num_layers - 1)
         arr = (AicasPhase * len(phases))(*phases)
         check(self._lib.aicas_validate_phases(arr, len(phases)), "aicas_validate_phases")
+        # the lean kernel (no code for tile paths this program never takes)
+        # when every GEMV phase qualifies: the 28-layer Qwen3-VL program does
+        self.program_flags = PROGRAM_LEAN if self._lib.aicas_lean_program_ok(arr, len(phases), self.num_ctas) == 0 else 0
         raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
         self.program = raw.to(self.device)
         self.n_phases = len(phases)
@@ -235,10 +238,11 @@ class Qwen3VLDecodeEngine:
         """n decode steps, eagerly (no graph)."""
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         for _ in range(n):
-            rc = self._lib.aicas_decode_program_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
-                                                    ctypes.c_void_p(self.state_dev.data_ptr()),
-                                                    ctypes.c_void_p(self.scratch.data_ptr()), stream)
-            check(rc, "aicas_decode_program_f16")
+            rc = self._lib.aicas_decode_program_ex_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
+                                                       ctypes.c_void_p(self.state_dev.data_ptr()),
+                                                       ctypes.c_void_p(self.scratch.data_ptr()), None,
+                                                       self.program_flags, stream)
+            check(rc, "aicas_decode_program_ex_f16")
 
     def launch_traced(self) -> torch.Tensor:
         """One step with per-CTA per-phase %globaltimer stamps; returns the
@@ -247,11 +251,11 @@ class Qwen3VLDecodeEngine:
         issued) after synchronising."""
         trace = torch.zeros((self.num_ctas, self.n_phases, 8), dtype=torch.int64, device=self.device)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
-        rc = self._lib.aicas_decode_program_trace_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
-                                                      ctypes.c_void_p(self.state_dev.data_ptr()),
-                                                      ctypes.c_void_p(self.scratch.data_ptr()),
-                                                      ctypes.c_void_p(trace.data_ptr()), stream)
-        check(rc, "aicas_decode_program_trace_f16")
+        rc = self._lib.aicas_decode_program_ex_f16(ctypes.c_void_p(self.program.data_ptr()), self.n_phases,
+                                                   ctypes.c_void_p(self.state_dev.data_ptr()),
+                                                   ctypes.c_void_p(self.scratch.data_ptr()),
+                                                   ctypes.c_void_p(trace.data_ptr()), self.program_flags, stream)
+        check(rc, "aicas_decode_program_ex_f16")
         torch.cuda.synchronize(self.device)
         return trace.cpu()
 

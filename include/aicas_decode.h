@@ -138,6 +138,25 @@ AICAS_API int aicas_lm_head_argmax_f16(const void* x, const void* norm_w, const 
 AICAS_API int aicas_decode_program_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
                                        void* scratch, aicas_stream_t stream);
 
+/* Whether the lean kernel can run a program: every GEMV-type phase streams
+ * whole 2048-column chunks (k % 2048 == 0) and has either k == 2048, or
+ * k == 6144 with at most 2 row groups of 8 rows per CTA on a grid of
+ * `num_ctas` CTAs (aicas_num_ctas) and is not a GATEUP phase.  The engine's
+ * 28-layer Qwen3-VL program qualifies.  Returns AICAS_OK or AICAS_ERR_SHAPE;
+ * `phases` is the host copy of the program. */
+AICAS_API int aicas_lean_program_ok(const AicasPhase* phases, int n_phases, int num_ctas);
+
+/* aicas_decode_program_f16 with options: `trace` (may be null) as in
+ * aicas_decode_program_trace_f16; `flags` AICAS_PROGRAM_LEAN runs the lean
+ * instantiation of the kernel (no code for the tile paths such programs
+ * never take: a smaller instruction footprint), for programs that passed
+ * aicas_lean_program_ok.  A program that does not qualify is not run past
+ * its first unsuitable phase: the launch aborts with device error 14 (bad
+ * phase) in the scratch block's error word. */
+#define AICAS_PROGRAM_LEAN 1
+AICAS_API int aicas_decode_program_ex_f16(const AicasPhase* device_phases, int n_phases, AicasStepState* state,
+                                          void* scratch, int64_t* trace, int flags, aicas_stream_t stream);
+
 /* Allocation-free variant of aicas_decode_attn_splitkv_f16, for callers that
  * cannot allocate device memory themselves (for example code running inside
  * a framework that owns every allocation, or a plugin that is only handed the

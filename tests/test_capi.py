@@ -64,3 +64,26 @@ def test_host_validation_rejects_bad_phases():
     a.k_cache = a.v_cache = a.x = a.out = 4096
     assert L.aicas_validate_phases((_native.AicasPhase * 1)(a), 1) == 2
     del ctypes
+
+
+def test_lean_program_rule():
+    """aicas_lean_program_ok: whole 2048-column chunks, k == 2048, or k == 6144
+    with <= 2 row groups of 8 per CTA (not GATEUP); attention always passes."""
+    L = _native.lib()
+
+    def ph(kind, n, k):
+        p = _native.AicasPhase()
+        p.kind, p.n, p.k = kind, n, k
+        return p
+
+    def ok(*phases, nct=148):
+        arr = (_native.AicasPhase * len(phases))(*phases)
+        return L.aicas_lean_program_ok(arr, len(phases), nct)
+
+    assert ok(ph(_native.PH_GEMV, 4096, 2048), ph(_native.PH_ATTN, 0, 0), ph(_native.PH_GATEUP, 6144, 2048),
+              ph(_native.PH_GEMV, 2048, 6144), ph(_native.PH_LMHEAD, 151936, 2048)) == 0
+    assert ok(ph(_native.PH_GEMV, 2048, 6144), nct=100) == 2      # 256 groups: 3 per CTA on 100 CTAs
+    assert ok(ph(_native.PH_GEMV, 64, 4096)) == 2                 # two chunks
+    assert ok(ph(_native.PH_GEMV, 64, 1024)) == 2                 # part of a chunk
+    assert ok(ph(_native.PH_GATEUP, 64, 6144)) == 2
+    assert ok(ph(_native.PH_GEMV, 64, 2048), nct=0) == 1

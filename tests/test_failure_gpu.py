@@ -13,7 +13,9 @@ with an error code in the scratch block, and the context stays usable:
   resets its device state, and the next request decodes exactly as before;
   the batched engine does the same when one of its streams has such a slot;
 * a launch on a scratch block that still holds an error (no reset after the
-  abort) is refused on the device: nothing is written and nothing advances.
+  abort) is refused on the device: nothing is written and nothing advances;
+* a program that does not suit the lean kernel, launched with the lean flag,
+  aborts at its first unsuitable phase with kErrBadPhase.
 """
 import ctypes
 import time
@@ -22,7 +24,8 @@ import numpy as np
 import pytest
 import torch
 
-from _native import F_LL_IN, F_LL_OUT, PH_GEMV, AicasError, AicasPhase, AicasStepState, check, lib, scratch_bytes
+from _native import (F_LL_IN, F_LL_OUT, PH_GEMV, PROGRAM_LEAN, AicasError, AicasPhase, AicasStepState, check, lib,
+                     scratch_bytes)
 from _ops import device_error
 from batch_engine import Qwen3VLBatchDecodeEngine
 from engine import Qwen3VLDecodeEngine
@@ -126,3 +129,38 @@ def test_batched_stream_with_a_slot_outside_the_cache_is_reported_not_used(cuda_
     again = eng.generate_batch(prompts, 8)
     for b in range(3):
         assert torch.equal(again[b], ref[b]), b
+
+
+def test_lean_flag_on_a_program_that_does_not_qualify_aborts(cuda_device):
+    L = lib()
+    nct = L.aicas_num_ctas(cuda_device.index)
+    n, k = 256, 1024  # part of a 2048-column chunk: not a lean phase
+    g = torch.Generator().manual_seed(1)
+    w = (torch.randn(n, k, generator=g) * 0.02).half().to(cuda_device)
+    x = torch.randn(k, generator=g).half().to(cuda_device)
+    y = torch.zeros(n, dtype=torch.float16, device=cuda_device)
+    p0 = AicasPhase()
+    p0.kind, p0.n, p0.k = PH_GEMV, n, k
+    p0.w, p0.x, p0.out = w.data_ptr(), x.data_ptr(), y.data_ptr()
+    arr = (AicasPhase * 1)(p0)
+    check(L.aicas_validate_phases(arr, 1), "aicas_validate_phases")
+    assert L.aicas_lean_program_ok(arr, 1, nct) != 0
+    prog = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(cuda_device)
+    state = torch.zeros(ctypes.sizeof(AicasStepState), dtype=torch.uint8, device=cuda_device)
+    scratch = torch.zeros(scratch_bytes(), dtype=torch.uint8, device=cuda_device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+
+    def launch(flags):
+        check(L.aicas_decode_program_ex_f16(ctypes.c_void_p(prog.data_ptr()), 1, ctypes.c_void_p(state.data_ptr()),
+                                            ctypes.c_void_p(scratch.data_ptr()), None, flags, stream),
+              "aicas_decode_program_ex_f16")
+        torch.cuda.synchronize(cuda_device)
+
+    t0 = time.perf_counter()
+    launch(PROGRAM_LEAN)
+    assert time.perf_counter() - t0 < 5.0  # the abort ends every wait at once
+    assert device_error(scratch) == 14
+    scratch.zero_()
+    launch(0)
+    assert device_error(scratch) == 0
+    assert torch.allclose(y.float(), w.float() @ x.float(), atol=2e-2, rtol=1e-2)
