@@ -251,6 +251,7 @@ __host__ __device__ __forceinline__ bool lean_phase(const AicasPhase& d, int nct
   if (d.k % kChunk != 0) return false;
   const int C = d.k / kChunk;
   if (C == 1) return true;
+  if (d.kind == AICAS_PH_LMHEAD) return false;
   const int groups = (d.n + kRows - 1) / kRows;
   return C == 3 && chunk_major(C, d.kind, (groups + nct - 1) / nct);
 }
@@ -957,9 +958,14 @@ struct Consumer {
     uint4 x0[kVec];
     build_x<C>(d, x0);
     stamp(ph, 1);
-    // descriptor fields in registers (the waits below clobber memory)
-    const int n = d.n, k = d.k, flags = d.flags, kind = d.kind;
-    const bool gateup = kind == AICAS_PH_GATEUP;
+    // descriptor fields in registers (the waits below clobber memory).  A
+    // GATEUP phase always has k <= 2048 (host-checked), and the lean kernel
+    // runs the LM head only with k == 2048: for C > 1 those kinds cannot occur,
+    // so this instantiation carries no code for them.
+    const int n = d.n, k = d.k, flags = d.flags;
+    const int kind = C == 1 ? d.kind : (d.kind == AICAS_PH_GATEUP || (kLean && d.kind == AICAS_PH_LMHEAD))
+                                           ? AICAS_PH_GEMV : d.kind;
+    const bool gateup = C == 1 && kind == AICAS_PH_GATEUP;
     __half* const out = reinterpret_cast<__half*>(d.out);
     const __half* const bias = reinterpret_cast<const __half*>(d.bias);
     const Range rg = split_range((n + kRows - 1) / kRows, nct, cta, d.rot);
@@ -1032,7 +1038,7 @@ struct Consumer {
     }                                                                                             \
   } while (0)
     uint4 xh[kVec];  // fp16 input slice of the running chunk (C > 1; C == 1 uses x0)
-    if (chunk_major(C, kind, rg.count)) {
+    if (kLean ? C > 1 : chunk_major(C, kind, rg.count)) {
       float acc[kMaxCmajorGroups][kRowsPerWarp][4];
 #pragma unroll
       for (int g = 0; g < kMaxCmajorGroups; ++g)

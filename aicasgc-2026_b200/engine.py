@@ -350,15 +350,35 @@ class Qwen3VLDecodeEngine:
             first = int(torch.argmax(logits))  # first index of the max, like the device argmax
             if self.logits is not None:
                 self.logits[(P - 1) % self.logits_ring].copy_(logits.to(torch.float16))
+            self.begin_decode(first, P, (pos3[:, -1] + 1).tolist(), eos_token_id)
+        return first
+
+    def begin_decode(self, first: int, P: int, rope, eos_token_id: int | None = None):
+        """Continue a request whose prompt (P tokens) is already in the cache
+        (slots [0, P)), e.g. prefilled by another implementation: `first` is
+        the token its prompt produced (out_tokens[P - 1]); the next step feeds
+        it at cache slot P with rope positions `rope` (3 axes).  With
+        `eos_token_id`, a first token equal to it ends the request at once."""
+        with torch.cuda.device(self.device):
             self.out_tokens.fill_(-1)
-            self.out_tokens[P - 1] = first
+            self.out_tokens[P - 1] = int(first)
             # step == script_len == P: every following step decodes freely
-            self._write_state(first, P, (pos3[:, -1] + 1).tolist(), P, P,
+            self._write_state(int(first), P, [int(r) for r in rope], P, P,
                               -1 if eos_token_id is None else int(eos_token_id))
-            if eos_token_id is not None and first == int(eos_token_id):
+            if eos_token_id is not None and int(first) == int(eos_token_id):
                 self.state_dev.view(torch.int64)[AicasStepState.done_step.offset // 8].fill_(P)
         self.script_len = P
-        return first
+
+    def collect(self, P: int, max_new_tokens: int) -> torch.Tensor:
+        """The request's generated tokens (CPU int64) after its steps ran: the
+        first max_new_tokens from out_tokens[P - 1], cut after a device-side
+        end of sequence (included)."""
+        toks = self.out_tokens[P - 1:P - 1 + max_new_tokens].cpu()
+        self.check_error()
+        done = self.done_step()
+        if done:
+            toks = toks[:done - (P - 1)]
+        return toks
 
     def generate(self, prompt, max_new_tokens: int, pos3=None, graph_steps: int = 32,
                  eos_token_id: int | None = None, prefill: str = "decode") -> torch.Tensor:
@@ -382,12 +402,7 @@ class Qwen3VLDecodeEngine:
         else:
             raise ValueError(f"unknown prefill mode {prefill!r}")
         self.run(max_new_tokens - 1, graph_steps)
-        toks = self.out_tokens[P - 1:P - 1 + max_new_tokens].cpu()
-        self.check_error()
-        done = self.done_step()
-        if done:
-            toks = toks[:done - (P - 1)]
-        return toks
+        return self.collect(P, max_new_tokens)
 
     def check_error(self):
         code = device_error(self.scratch)

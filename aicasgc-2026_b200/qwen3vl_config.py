@@ -55,6 +55,18 @@ class Qwen3VLTextShape:
     def with_layers(self, n: int) -> "Qwen3VLTextShape":
         return Qwen3VLTextShape(**{**self.__dict__, "num_layers": n})
 
+    @staticmethod
+    def from_hf_text_config(cfg) -> "Qwen3VLTextShape":
+        """The shape of an HF Qwen3-VL text config (`config.get_text_config()`)."""
+        rope = getattr(cfg, "rope_parameters", None) or getattr(cfg, "rope_scaling", None) or {}
+        theta = rope.get("rope_theta", getattr(cfg, "rope_theta", 5_000_000.0))
+        return Qwen3VLTextShape(
+            hidden=cfg.hidden_size, num_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads,
+            head_dim=getattr(cfg, "head_dim", cfg.hidden_size // cfg.num_attention_heads),
+            intermediate=cfg.intermediate_size, vocab=cfg.vocab_size, num_layers=cfg.num_hidden_layers,
+            rms_eps=float(cfg.rms_norm_eps), rope_theta=float(theta),
+            mrope_section=tuple(rope.get("mrope_section", (24, 20, 20))))
+
     def weight_bytes_per_step(self) -> int:
         """Algorithmic fp16 weight bytes one decode step must read.
 

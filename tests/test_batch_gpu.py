@@ -156,3 +156,37 @@ def test_batch_full_model_ragged_vs_batch1_engine(cuda_device):
                 assert top2[1] - top2[0] <= 2 * LOGIT_ATOL_28L, (b, i, toks[i], ref[i])
                 break
     print("batch vs batch-1 max logit diff", worst)
+
+
+def test_batch_full_model_two_streams_vs_oracle(cuda_device):
+    """28 layers, two requests in one batched step (one with a vision grid):
+    every stream's logits against the fp16 oracle run on that stream alone,
+    teacher-forced on the stream's own tokens, for 16 steps.  Tolerance: the
+    28-layer fp16 noise floor (3e-2 max, 5e-3 mean per step); a token may
+    differ from the oracle's only at a near tie of the oracle's top two."""
+    st = synthetic_state(QWEN3VL_2B, seed=0, dtype=torch.float16)
+    lengths = [300, 96]  # the vision prompt ends after its 16x16 grid (tokens 16..271)
+    prompts, pos3s, deltas = _requests(lengths, vision=(0,), seed=1200)
+    n = 16
+    Lmax = max(lengths) + n + 8
+    eng = Qwen3VLBatchDecodeEngine(st, QWEN3VL_2B, max_batch=2, max_cache_len=Lmax, logits_ring=n, max_steps=Lmax)
+    outs = eng.generate_batch(prompts, n, pos3s=pos3s)
+    gl = [np.stack([eng.step_logits(b, lengths[b] - 1 + i).float().cpu().numpy() for i in range(n)]) for b in range(2)]
+    del eng
+    torch.cuda.empty_cache()
+    o = Qwen3VLOracle(st, QWEN3VL_2B.num_layers, mode="fp16", max_cache_len=Lmax,
+                      inv_freq=hf_inv_freq(QWEN3VL_2B).numpy())
+    for b in range(2):
+        toks = outs[b].numpy()
+        assert len(toks) == n
+        np.testing.assert_array_equal(toks, np.argmax(gl[b], axis=-1))
+        otoks, ol = o.greedy(prompts[b], n, pos3_prompt=pos3s[b], rope_delta=deltas[b], forced=toks)
+        d = np.abs(gl[b] - ol)
+        print(f"stream {b}: max |d logit| per step {np.round(d.max(axis=-1), 4).tolist()}")
+        assert d.max() <= LOGIT_ATOL_28L, f"stream {b}: {d.max(axis=-1)}"
+        assert d.mean(axis=-1).max() <= 5e-3
+        srt = np.sort(ol, axis=-1)
+        gap = srt[:, -1] - srt[:, -2]
+        for i in range(n):
+            if toks[i] != otoks[i]:
+                assert gap[i] <= 2 * LOGIT_ATOL_28L, f"stream {b} step {i}: {toks[i]} vs {otoks[i]} (gap {gap[i]})"

@@ -86,4 +86,5 @@ def test_lean_program_rule():
     assert ok(ph(_native.PH_GEMV, 64, 4096)) == 2                 # two chunks
     assert ok(ph(_native.PH_GEMV, 64, 1024)) == 2                 # part of a chunk
     assert ok(ph(_native.PH_GATEUP, 64, 6144)) == 2
+    assert ok(ph(_native.PH_LMHEAD, 64, 6144)) == 2               # the LM head: one chunk only
     assert ok(ph(_native.PH_GEMV, 64, 2048), nct=0) == 1
