@@ -57,8 +57,6 @@
 #include <stdint.h>
 #include <string.h>
 
-#include <atomic>
-
 #include "aicas_device.cuh"
 #include "aicas_phase_program.h"
 
@@ -1966,97 +1964,4 @@ AICAS_API int aicas_decode_program_ex_f16(const AicasPhase* device_phases, int n
   return launch_program(a, stream, (flags & AICAS_PROGRAM_LEAN) != 0);
 }
 
-AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,
-                                            const void* cache_position, float scale, void* out, int64_t q_heads,
-                                            int64_t kv_heads, int64_t max_len, void* scratch, cudaStream_t stream) {
-  if (max_len < 1 || max_len > (1 << 30)) return AICAS_ERR_SHAPE;
-  if (!cache_position) return AICAS_ERR_ARG;
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& d = a.inl[0];
-  d.kind = AICAS_PH_ATTN;
-  d.flags = AICAS_F_Q_READY;
-  d.q_heads = (int32_t)q_heads;
-  d.kv_heads = (int32_t)kv_heads;
-  d.max_len = (int32_t)max_len;
-  d.x = q;
-  d.k_cache = const_cast<void*>(k_cache);
-  d.v_cache = const_cast<void*>(v_cache);
-  d.pos_ptr = cache_position;
-  d.out = out;
-  d.scale = scale;
-  a.n_phases = 1;
-  a.scratch = reinterpret_cast<AicasScratch*>(scratch);
-  return launch_program(a, stream);
-}
-
 }  // extern "C"
-
-// ===========================================================================
-// Allocation-free split-KV decode attention
-// ===========================================================================
-// Same computation as aicas_decode_attn_splitkv_f16, but the scratch block
-// (split partials, merge counters, error word) is this library's own device
-// memory, so the caller never allocates it.  The block is one file-scope
-// __device__ array per device (zero at module load, held until the process
-// exits).  Host code must not hand the array's name to a kernel: on the host
-// it is only a stand-in for the device symbol, so its device address is
-// looked up once per device with cudaGetSymbolAddress.
-namespace aicas {
-static __device__ __align__(256) AicasScratch g_noalloc_scratch;
-// Device address of g_noalloc_scratch per device, filled on the first call
-// there.  Atomic: host threads may call concurrently (two threads that both
-// look it up store the same address).  A device reset invalidates it; the
-// library must then be reloaded.
-static std::atomic<AicasScratch*> g_noalloc_scratch_ptr[kMaxDevices];
-}  // namespace aicas
-
-extern "C" AICAS_API int aicas_decode_attn_splitkv_f16_noalloc(const void* q, const void* k_cache,
-                                                               const void* v_cache, const void* cache_position,
-                                                               float scale, void* out, int64_t q_heads,
-                                                               int64_t kv_heads, int64_t max_len, int32_t* status,
-                                                               cudaStream_t stream) {
-  if (max_len < 1 || max_len > (1 << 30)) return AICAS_ERR_SHAPE;
-  if (!q || !k_cache || !v_cache || !cache_position || !out) return AICAS_ERR_ARG;
-  // The fixed scratch holds partials for at most AICAS_MAX_KV_HEADS KV heads
-  // (GQA 2:1, head dim 128) and AICAS_MAX_SPLITS splits (one per CTA).
-  if (kv_heads < 1 || kv_heads > AICAS_MAX_KV_HEADS || q_heads != 2 * kv_heads) return AICAS_ERR_CAPACITY;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e);
-  if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
-  AicasScratch* scr = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!scr) {  // first call on this device: resolve the array's device address
-    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&scr), g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e);
-    g_noalloc_scratch_ptr[dev].store(scr, std::memory_order_release);
-  }
-  // The array keeps the previous call's contents: zero the words a launch
-  // expects to start at zero (error, abort and counters).  The epoch base
-  // keeps counting, so partials left by the previous call never match.
-  e = cudaMemsetAsync(&scr->error, 0, offsetof(AicasScratch, am_val) - offsetof(AicasScratch, error), stream);
-  if (e != cudaSuccess) return cuda_fail(e);
-  ProgramArgs a;
-  memset(&a, 0, sizeof(a));
-  AicasPhase& d = a.inl[0];
-  d.kind = AICAS_PH_ATTN;
-  d.flags = AICAS_F_Q_READY;
-  d.q_heads = (int32_t)q_heads;
-  d.kv_heads = (int32_t)kv_heads;
-  d.max_len = (int32_t)max_len;
-  d.x = q;
-  d.k_cache = const_cast<void*>(k_cache);
-  d.v_cache = const_cast<void*>(v_cache);
-  d.pos_ptr = cache_position;
-  d.out = out;
-  d.scale = scale;
-  a.n_phases = 1;
-  a.scratch = scr;
-  const int rc = launch_program(a, stream);
-  if (rc) return rc;
-  if (status) {  // the call's device-side error code, for callers that cannot read the array
-    e = cudaMemcpyAsync(status, &scr->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
-    if (e != cudaSuccess) return cuda_fail(e);
-  }
-  return AICAS_OK;
-}

@@ -100,8 +100,13 @@ AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out
 /* Decode attention for one query token: out[q_heads,128] =
  * softmax(q K^T * scale) V over cache slots [0, *cache_position] (int64 on
  * the device).  K/V: [kv_heads, max_len, 128] (HF StaticLayer.keys/values of
- * batch 1); q_heads == 2 * kv_heads.  Split-KV over all SMs with a
- * deterministic log-sum-exp merge.  Replaces
+ * batch 1); q_heads == 2 * kv_heads <= 16.  One ordinary launch: up to 64
+ * chunks of cache slots per KV head, each CTA's partial merged by the last CTA
+ * of its head in split order (deterministic).  `scratch` (aicas_scratch_bytes,
+ * zeroed before its first use) holds the partials, one arrival counter per KV
+ * head (back to zero after every call) and the error word: a cache position
+ * outside [0, max_len) records device error 15 and writes nothing, and a
+ * block that holds an error refuses the call.  Replaces
  * `decode_attn_v4_cta_qhead_splitkv_fused` (cuda_decode_attention.py:489-558;
  * kernel cuda_extensions/decode_attention_v4_kernel.cu:647-900). */
 AICAS_API int aicas_decode_attn_splitkv_f16(const void* q, const void* k_cache, const void* v_cache,
