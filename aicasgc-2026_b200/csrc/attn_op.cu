@@ -9,10 +9,10 @@
 // The op moves 4 KB of K/V per cache slot; at 8192 slots that is 33.5 MB, ~5
 // us of HBM time, so the launch must put the whole cache in flight at once:
 //
-//   * grid (splits, kv heads): each CTA takes one contiguous chunk of slots of
-//     one KV head (chunk = the valid length over the splits, rounded up to 64
-//     slots; CTAs past the last chunk return at once), so both query heads of
-//     a KV head read its K/V once;
+//   * grid (16 splits, kv heads): each CTA takes one contiguous chunk of slots
+//     of one KV head (chunk = the valid length over the splits, rounded up to
+//     128 slots; CTAs past the last chunk return at once), so both query heads
+//     of a KV head read its K/V once;
 //   * 8 warps per CTA take 16 slots each in turn (all 16 slots' K and V loads
 //     issued first), as two groups of 8: lane (slot pi = lane / 4, quarter
 //     qc = lane % 4) dots its 32 dims of K (four 16-byte loads, evict-first)
@@ -53,11 +53,21 @@ namespace attn {
 constexpr int kHD = AICAS_HEAD_DIM;
 constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kSlotAlign = 64;          // chunk granularity (cache slots)
-#ifndef AICAS_ATTN_SPLITS
-#define AICAS_ATTN_SPLITS 64
+#ifndef AICAS_ATTN_ALIGN
+#define AICAS_ATTN_ALIGN 128
 #endif
-constexpr int kMaxSplits = AICAS_ATTN_SPLITS;  // splits per KV head (grid x)
+// Chunk granularity (cache slots; 128 = one pass of the 8 warps) and splits per
+// KV head.  Measured on B200 (bench.py --op attention, us per call at L = 128 /
+// 1024 / 4096 / 8192): 64 splits of 64-slot units 7.8 / 10.1 / 21.5 / 24.6;
+// 32 of 64: 7.0 / 8.2 / 14.0 / 18.5; 16 of 128: 4.6 / 7.5 / 10.7 / 14.9;
+// 8 of 128: 4.5 / 7.4 / 13.5 / 21.5.  Each further split adds a partial that
+// the last CTA must read back, so fewer, longer chunks win until the grid
+// stops covering the SMs.
+constexpr int kSlotAlign = AICAS_ATTN_ALIGN;
+#ifndef AICAS_ATTN_SPLITS
+#define AICAS_ATTN_SPLITS 16
+#endif
+constexpr int kMaxSplits = AICAS_ATTN_SPLITS;
 constexpr int kPartFloats = 2 + kHD;    // running max, sum, acc[128]
 static_assert(kMaxSplits <= AICAS_MAX_SPLITS, "partials must fit the scratch block");
 static_assert((size_t)AICAS_MAX_KV_HEADS * kMaxSplits * 2 * kPartFloats * 4 + AICAS_MAX_KV_HEADS * 4 <=
@@ -91,7 +101,10 @@ struct Smem {
   uint32_t last;
 };
 
-__global__ void __launch_bounds__(kThreads) decode_attention_kernel(const __half* __restrict__ q,
+#ifndef AICAS_ATTN_MINB
+#define AICAS_ATTN_MINB 1
+#endif
+__global__ void __launch_bounds__(kThreads, AICAS_ATTN_MINB) decode_attention_kernel(const __half* __restrict__ q,
                                                                     const __half* __restrict__ kc,
                                                                     const __half* __restrict__ vc,
                                                                     const int64_t* __restrict__ pos_ptr, float scale,

@@ -100,7 +100,7 @@ AICAS_API int aicas_post_attn_mlp_f16(const void* residual, const void* attn_out
 /* Decode attention for one query token: out[q_heads,128] =
  * softmax(q K^T * scale) V over cache slots [0, *cache_position] (int64 on
  * the device).  K/V: [kv_heads, max_len, 128] (HF StaticLayer.keys/values of
- * batch 1); q_heads == 2 * kv_heads <= 16.  One ordinary launch: up to 64
+ * batch 1); q_heads == 2 * kv_heads <= 16.  One ordinary launch: up to 16
  * chunks of cache slots per KV head, each CTA's partial merged by the last CTA
  * of its head in split order (deterministic).  `scratch` (aicas_scratch_bytes,
  * zeroed before its first use) holds the partials, one arrival counter per KV
