@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict_
 constexpr int kBQ = 64;   // queries per CTA (4 warps x 16)
 constexpr int kBK = 64;   // keys per block
 constexpr int kAttnThreads = 128;
+constexpr int kAttnSmem = 5 * 64 * 256;  // Q + two K/V stages (80 KB)
 
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -227,9 +228,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __half* _
                                                                const __half* __restrict__ vc, __half* __restrict__ out,
                                                                int P, int start, int hq, int hkv, int max_len,
                                                                float scale) {
-  __shared__ __align__(128) uint8_t smem[3 * 64 * 256];
-  const uint32_t sq = smem_addr(smem), sk = sq + 64 * 256, sv = sk + 64 * 256;
-  const int qb = blockIdx.x, head = blockIdx.y, kvh = head / (hq / hkv);
+  // Q | K, V of key block 2i | K, V of key block 2i + 1: the next block's
+  // copies are in flight while this one is computed
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sq = smem_addr(smem);
+  // the tiles with the most key blocks first (causal: the last query tile)
+  const int qb = gridDim.x - 1 - blockIdx.x, head = blockIdx.y, kvh = head / (hq / hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = qb * kBQ;
   const int qrows = min(kBQ, P - q0);
@@ -249,13 +253,23 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __half* _
   const float sl2 = scale * 1.4426950408889634f;  // scores in log2 units
   const int g = lane >> 2, tig = lane & 3;
   const int qi0 = start + q0 + warp * 16 + g;  // absolute slots of this thread's rows g, g + 8
-  for (int kb = 0; kb < nkb; ++kb) {
+  auto issue = [&](int kb) {
     const int k0 = kb * kBK;
-    __syncthreads();  // previous K/V tiles are no longer read
+    const uint32_t sk = sq + (1 + 2 * (kb & 1)) * 64 * 256, sv = sk + 64 * 256;
     load_tile(sk, kbase + (size_t)k0 * kHD, kHD, min(kBK, kend - k0));
     load_tile(sv, vbase + (size_t)k0 * kHD, kHD, min(kBK, kend - k0));
     asm volatile("cp.async.commit_group;" ::: "memory");
-    cp_async_wait_all();
+  };
+  issue(0);
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int k0 = kb * kBK;
+    const uint32_t sk = sq + (1 + 2 * (kb & 1)) * 64 * 256, sv = sk + 64 * 256;
+    if (kb + 1 < nkb) {
+      issue(kb + 1);  // its buffer was last read in iteration kb - 1 (barrier at that iteration's end)
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      cp_async_wait_all();
+    }
     __syncthreads();
     if (kb == 0) {
 #pragma unroll
@@ -343,6 +357,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __half* _
         mma16816(o[2 * dp + 1], pa, b[2], b[3]);
       }
     }
+    __syncthreads();  // every warp is done with this block's buffer before it is refilled
   }
   // normalise and store rows g, g + 8 of this warp
 #pragma unroll
@@ -416,7 +431,18 @@ AICAS_API int aicas_prefill_attention_f16(const void* q, const void* k_cache, co
   if (!q || !k_cache || !v_cache || !out || !al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out))
     return AICAS_ERR_ALIGN;
   const dim3 grid((unsigned)((rows + kBQ - 1) / kBQ), (unsigned)q_heads);
-  attention_kernel<<<grid, kAttnThreads, 0, stream>>>((const __half*)q, (const __half*)k_cache,
+  // dynamic shared memory above 48 KB needs an opt-in, once per device
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t ea = cudaGetDevice(&dev);
+  if (ea != cudaSuccess) return aicas::record_cuda_error(ea);
+  if (dev < 0 || dev >= 64) return AICAS_ERR_CUDA;
+  if (!attr_done[dev]) {
+    ea = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    if (ea != cudaSuccess) return aicas::record_cuda_error(ea);
+    attr_done[dev] = true;
+  }
+  attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>((const __half*)q, (const __half*)k_cache,
                                                       (const __half*)v_cache, (__half*)out, (int)rows, (int)start,
                                                       (int)q_heads, (int)kv_heads, (int)max_len, scale);
   const cudaError_t e = cudaGetLastError();
