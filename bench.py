@@ -304,9 +304,9 @@ def job_throughput(steps: int, world: int, ms: float) -> float:
 # --------------------------------------------------------------------------- GPU
 # DRAM bytes per algorithmic byte of decode_program_kernel, from one
 # `ncu --set full` capture of the 4-layer profiling case (bench.py --layers 4;
-# summarised under profiles/): (1.043186e9 + 9.19424e6) / 1043908608.  The
+# summarised under profiles/): (1.043188e9 + 6.631424e6) / 1043908608.  The
 # per-layer shapes equal the headline model's, so the ratio carries over.
-DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0081153
+DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0056622
 
 def run_ours(args, rank: int, world: int):
     import torch
@@ -435,7 +435,7 @@ def run_ours(args, rank: int, world: int):
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_req / NEW,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 4-layer "
-                                       "launch (1.0432 GB + 9.2 MB vs 1.0439 GB algorithmic), scaled to this "
+                                       "launch (1.0432 GB + 6.6 MB vs 1.0439 GB algorithmic), scaled to this "
                                        "launch by algorithmic bytes",
                      "kernel": "decode_program_kernel (one launch per token)",
                      "algorithmic_bytes_per_launch": bytes_req / NEW},
