@@ -102,19 +102,29 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const __half* __restrict__ qkv, const __half* __restrict__ qn_w, const __half* __restrict__ kn_w,
     const int64_t* __restrict__ pos3, const float* __restrict__ inv_freq, int sec1, int sec2, __half* __restrict__ q_out,
     __half* __restrict__ k_cache, __half* __restrict__ v_cache, int P, int start, int max_len, int hq, int hkv, float eps) {
+  __shared__ float tcos[kHD / 2], tsin[kHD / 2];
   const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = hq + 2 * hkv;  // qkv row length in heads
+  // the token's 64 rotary frequencies, once per CTA: frequency i takes axis 1
+  // (h) when i % 3 == 1 and i < 3 sec1, axis 2 (w) when i % 3 == 2 and
+  // i < 3 sec2, else axis 0 (t); cos / sin in fp32, rounded to fp16
+  if (threadIdx.x < kHD / 2) {
+    const int i = threadIdx.x;
+    int axis = 0;
+    if (i % 3 == 1 && i < 3 * sec1) axis = 1;
+    else if (i % 3 == 2 && i < 3 * sec2) axis = 2;
+    float sv, cv;
+    sincosf(inv_freq[i] * (float)pos3[(size_t)axis * P + t], &sv, &cv);
+    tcos[i] = r16(cv);
+    tsin[i] = r16(sv);
+  }
+  __syncthreads();
   // this lane's 4 frequencies (dims 4 lane .. 4 lane + 3, frequency d mod 64)
   float cs[4], sn[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const int i = (lane * 4 + e) & 63;
-    int axis = 0;
-    if (i % 3 == 1 && i < 3 * sec1) axis = 1;
-    else if (i % 3 == 2 && i < 3 * sec2) axis = 2;
-    const float ang = inv_freq[i] * (float)pos3[(size_t)axis * P + t];
-    cs[e] = r16(cosf(ang));
-    sn[e] = r16(sinf(ang));
+    cs[e] = tcos[(lane * 4 + e) & 63];
+    sn[e] = tsin[(lane * 4 + e) & 63];
   }
   const size_t slot = (size_t)start + t;
   for (int task = w; task < row; task += 8) {
@@ -123,14 +133,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const __half2* hp = reinterpret_cast<const __half2*>(&raw);
     float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
     if (task < hq + hkv) {
-      const __half* nw = task < hq ? qn_w : kn_w;
+      const uint2 nwr = __ldg(reinterpret_cast<const uint2*>(task < hq ? qn_w : kn_w) + lane);
+      const __half2* nh = reinterpret_cast<const __half2*>(&nwr);
+      const float nwf[4] = {__low2float(nh[0]), __high2float(nh[0]), __low2float(nh[1]), __high2float(nh[1])};
       float ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
       const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
       float xn[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) xn[e] = r16(__half2float(nw[lane * 4 + e]) * r16(v[e] * inv));
+      for (int e = 0; e < 4; ++e) xn[e] = r16(nwf[e] * r16(v[e] * inv));
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
@@ -162,7 +174,8 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict_
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float2 gf = __half22float2(gp[q]), uf = __half22float2(up[q]);
-      const float s0 = r16(gf.x / (1.0f + expf(-gf.x))), s1 = r16(gf.y / (1.0f + expf(-gf.y)));
+      // SiLU in fp32 (the fast exp: its error is far below the fp16 rounding that follows)
+      const float s0 = r16(gf.x / (1.0f + __expf(-gf.x))), s1 = r16(gf.y / (1.0f + __expf(-gf.y)));
       op[q] = __floats2half2_rn(s0 * uf.x, s1 * uf.y);
     }
     reinterpret_cast<uint4*>(act + r * inter)[c] = o;
