@@ -478,9 +478,9 @@ def batch_workload_config(batch: int, ctx: list, n_gpus: int) -> dict:
             "l2": "inputs larger than L2: 3.44 GB of weights + the requests' KV streamed per step"}
 # DRAM bytes per algorithmic byte of decode_batch_kernel, from one `ncu --set
 # full` capture of the 2-layer batch-8 profiling case (bench.py --batch 8
-# --layers 2; summarised under profiles/): (983.835392e6 + 21.94944e6) /
-# 981263360 (reads 0.3 % above the algorithmic bytes, the rest writes).
-BATCH_DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0249897
+# --layers 2; summarised under profiles/): (983.693568e6 + 15.259648e6) /
+# 981263360 (reads 0.2 % above the algorithmic bytes, the rest writes).
+BATCH_DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0180276
 BATCH_CTX = (512, 4096)  # per-stream context lengths, uniform, seeded
 
 
@@ -599,7 +599,7 @@ def run_batch(args, rank: int, world: int):
                      "peak_kind": peak_kind,
                      "traffic": BATCH_DRAM_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_step / BATCH_NEW,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 2-layer batch-8 "
-                                       "launch (983.8 MB + 21.9 MB vs 981.3 MB algorithmic), scaled to this "
+                                       "launch (983.7 MB + 15.3 MB vs 981.3 MB algorithmic), scaled to this "
                                        "launch by algorithmic bytes",
                      "kernel": "decode_batch_kernel (one launch per batched step)",
                      "algorithmic_bytes_per_launch": bytes_step / BATCH_NEW},
