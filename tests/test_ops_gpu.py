@@ -103,6 +103,37 @@ def test_decode_attention_splitkv(cuda_device, L):
     assert np.abs(got - ref).max() <= 2e-3
 
 
+@pytest.mark.parametrize("kvh,lmax,L", [(1, 1000, 1000), (4, 1000, 129), (2, 4100, 4100), (8, 300, 2)])
+def test_decode_attention_other_head_counts_and_cache_sizes(cuda_device, kvh, lmax, L):
+    """The split-KV op with 1, 2, 4 or 8 KV heads (two query heads each) and
+    caches whose length is no multiple of the 128-slot chunk, through the C ABI:
+    against attention_reference, and a second call equal to the first (the
+    merge counters return to zero)."""
+    import ctypes
+
+    import _native
+
+    lib = _native.lib()
+    q = _randn((2 * kvh, 128), 40 + kvh)
+    k = _randn((kvh, lmax, 128), 41 + kvh)
+    v = _randn((kvh, lmax, 128), 42 + kvh)
+    pos = torch.tensor([L - 1], dtype=torch.int64, device="cuda")
+    scratch = torch.zeros(_native.scratch_bytes(), dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        out = torch.full((2 * kvh, 128), float("nan"), dtype=torch.float16, device="cuda")
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _native.check(lib.aicas_decode_attn_splitkv_f16(p(q), p(k), p(v), p(pos), 128 ** -0.5, p(out), 2 * kvh, kvh,
+                                                        lmax, p(scratch),
+                                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                      "aicas_decode_attn_splitkv_f16")
+        outs.append(out)
+    ref = attention_reference(q.float().cpu().numpy(), k[:, :L].float().cpu().numpy(), v[:, :L].float().cpu().numpy(),
+                              L, 128 ** -0.5)
+    assert np.abs(outs[0].float().cpu().numpy() - ref).max() <= 2e-3
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_decode_attention_rejects_bad_gqa(cuda_device):
     import cuda_decode_attention as ca
 
