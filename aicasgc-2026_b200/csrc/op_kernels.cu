@@ -130,7 +130,6 @@ __global__ void __launch_bounds__(kThreads) gemv_op_kernel(const Args a) {
   __shared__ int bi_s[kWarps];
   // a scratch block that still holds a device error refuses the launch
   if (a.scratch && ld_volatile_int(&a.scratch->error) != 0) return;
-  stage_x(a, xs, red);
   constexpr int R = (C == 1 || kMode == kGateUp) ? 2 : 1;
   constexpr int P = kMode == kGateUp ? 1 : R;  // output rows per pass
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -139,15 +138,16 @@ __global__ void __launch_bounds__(kThreads) gemv_op_kernel(const Args a) {
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
   const int stride = gridDim.x * kWarps * P;
-  for (int base = (blockIdx.x * kWarps + warp) * P; base < n; base += stride) {
-    int rows[R];
-    bool ok[R];
+  int rows[R];
+  bool ok[R];
+  uint4 wv[R][C][kVec];
+  // this warp's rows of a pass and their weight loads (no dependence on x)
+  auto load_pass = [&](int base) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       rows[r] = kMode == kGateUp ? base + r * n : base + r;
       ok[r] = kMode == kGateUp ? true : rows[r] < n;
     }
-    uint4 wv[R][C][kVec];
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -157,6 +157,17 @@ __global__ void __launch_bounds__(kThreads) gemv_op_kernel(const Args a) {
           const int col = c * kChunk + j * 256 + lane * 8;
           wv[r][c][j] = (ok[r] && col < k) ? ld_stream(a.w + (size_t)rows[r] * k + col, pol) : make_uint4(0, 0, 0, 0);
         }
+  };
+  // the lm_head pass loop is long: its first pass's weights are requested
+  // before the input is staged, so the two round trips overlap (measured
+  // slower for the short loops of the other projections, whose loads the
+  // compiler then holds in registers all at once)
+  constexpr bool kEarly = kMode == kArgmax;
+  const int first = (blockIdx.x * kWarps + warp) * P;
+  if (kEarly && first < n) load_pass(first);
+  stage_x(a, xs, red);
+  for (int base = first; base < n; base += stride) {
+    if (!kEarly || base != first) load_pass(base);
     float s[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -237,6 +248,68 @@ __global__ void __launch_bounds__(kThreads) gemv_op_kernel(const Args a) {
   *a.idx_out = bi;
 }
 
+// Plain GEMV with k > 2048 (C chunks): the chunks of a row go to C warps of
+// the CTA (warp w: row slot w / C, chunk w % C; warps beyond (8 / C) C idle),
+// so each warp has all 8 of its 16-byte loads per lane in flight at once
+// (one warp holding all C chunks of a row keeps only part of them in flight:
+// 10.9 us for down_proj [2048 x 6144]).  The C partial sums meet in shared
+// memory and the row is finished in chunk order.
+template <int C>
+__global__ void __launch_bounds__(kThreads) gemv_ksplit_kernel(const Args a) {
+  extern __shared__ __align__(16) __half xs[];
+  __shared__ float red[kWarps];
+  __shared__ float part[kWarps];
+  if (a.scratch && ld_volatile_int(&a.scratch->error) != 0) return;
+  constexpr int RS = kWarps / C;  // rows per CTA pass
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = warp / C, c = warp % C;
+  const bool active = slot < RS;
+  const int n = a.n, k = a.k;
+  const uint64_t pol = l2_evict_first_policy();
+  uint4 wv[kVec];
+  auto load_row = [&](int row) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int col = c * kChunk + j * 256 + lane * 8;
+      wv[j] = (active && row < n && col < k) ? ld_stream(a.w + (size_t)row * k + col, pol) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  // the first pass's weights are requested before the input is staged
+  load_row(blockIdx.x * RS + slot);
+  stage_x(a, xs, red);
+  for (int base = blockIdx.x * RS; base < n; base += gridDim.x * RS) {  // the same trip count for the whole CTA
+    const int row = base + slot;
+    if (base != (int)blockIdx.x * RS) load_row(row);
+    float sum = 0.f;
+    if (active && row < n) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int col = c * kChunk + j * 256 + lane * 8;
+        const uint4 xv = col < k ? *reinterpret_cast<const uint4*>(xs + col) : make_uint4(0, 0, 0, 0);
+        acc[j & 3] = dot8_f16(wv[j], xv, acc[j & 3]);
+      }
+      sum = warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    }
+    if (lane == 0) part[warp] = sum;
+    __syncthreads();
+    if (active && c == 0 && lane == 0 && row < n) {
+      float acc = part[warp];
+#pragma unroll
+      for (int cc = 1; cc < C; ++cc) acc += part[warp + cc];
+      if (a.flags & kBias) acc += __half2float(a.bias[row]);
+      float y = r16(acc);
+      if (a.flags & kResid) {
+        float rv = __half2float(a.resid[row]);
+        if (a.flags & kResidAdd) rv = r16(rv + __half2float(a.resid2[row]));
+        y = r16(rv + y);
+      }
+      a.out[row] = __float2half_rn(y);
+    }
+    __syncthreads();
+  }
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 static int sm_count() {
@@ -281,6 +354,16 @@ static int run(Args a, int mode, cudaStream_t stream) {
   if (mode == kArgmax && (!a.idx_out || !a.scratch)) return AICAS_ERR_ARG;
   const int C = (a.k + kChunk - 1) / kChunk;
   if (mode == kGateUp && C != 1) return AICAS_ERR_SHAPE;
+  if (mode == kPlain && C > 1) {  // k > 2048: chunks split over warps
+    const int rs = kWarps / C;
+    long grid = (a.n + rs - 1) / rs;
+    const long cap = (long)sm_count() * 8;
+    if (grid > cap) grid = cap;
+    if (C == 2) gemv_ksplit_kernel<2><<<(int)grid, kThreads, (size_t)a.k * 2, stream>>>(a);
+    else gemv_ksplit_kernel<3><<<(int)grid, kThreads, (size_t)a.k * 2, stream>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AICAS_OK : record_cuda_error(e);
+  }
   const int per_pass = (mode == kGateUp) ? 1 : (C == 1 ? 2 : 1);
   const long passes = (a.n + per_pass - 1) / per_pass;
   long grid = (passes + kWarps - 1) / kWarps;
