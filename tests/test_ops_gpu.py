@@ -31,7 +31,7 @@ def _randn(shape, seed, scale=1.0, dev="cuda"):
 
 
 @pytest.mark.parametrize("n,k", [(4096, 2048), (2048, 2048), (12288, 2048), (2048, 6144), (1000, 8),
-                                 (5, 4104), (151936, 2048)])
+                                 (5, 4104), (151936, 2048), (301, 4096), (77, 2056), (3, 6144)])
 def test_gemv_matches_oracle(cuda_device, n, k):
     import cuda_decode_gemv as cg
 
