@@ -17,9 +17,14 @@ rejects batch > 1, evaluation_wrapper.py:110-111) and its attention kernel
 reads only `cache_position[0]` (cuda_extensions/decode_attention_v4_kernel.cu:
 647-900); per stream, every step computes what the batch-1 step computes.
 
-KV layout: per layer `keys/values [max_batch, num_kv_heads, max_cache_len,
-128]` fp16, HF `StaticLayer` of batch max_batch
-(transformers/cache_utils.py:247-354).
+KV layout: `k_cache` / `v_cache` [layers, max_batch, num_kv_heads,
+max_cache_len, 128] fp16 storage (the shape of HF `StaticLayer`s of batch
+max_batch, transformers/cache_utils.py:247-354), each (layer, stream, head)
+slice in the KV tile layout: slot p, dim d at element (p // 8) * 1024 +
+(d // 8) * 64 + (p % 8) * 8 + d % 8, so a 64-slot chunk lands in shared
+memory as a tensor-core operand with one bulk copy.  `kv_tiles` views the
+storage as [.., slot groups, dim blocks, 8 slots, 8 dims], `kv_hf_layout`
+returns a copy in HF's [.., slots, dims] order.
 """
 from __future__ import annotations
 
@@ -36,6 +41,25 @@ from prefill import layer_weights_from_hf, prefill
 from qwen3vl_config import QWEN3VL_2B, Qwen3VLTextShape
 
 _DONE = AicasStepState.done_step.offset // 8
+
+
+def kv_tiles(cache: torch.Tensor) -> torch.Tensor:
+    """View of a [L, B, KVH, Lmax, D] KV tile layout cache as [L, B, KVH,
+    Lmax / 8, D / 8, 8 slots, 8 dims]."""
+    L, B, H, M, D = cache.shape
+    return cache.view(L, B, H, M // 8, D // 8, 8, 8)
+
+
+def kv_hf_layout(cache: torch.Tensor) -> torch.Tensor:
+    """A copy of a KV tile layout cache in HF's [L, B, KVH, Lmax, D] order."""
+    return kv_tiles(cache).permute(0, 1, 2, 3, 5, 4, 6).reshape(cache.shape)
+
+
+def kv_store_tiles(cache: torch.Tensor, b: int, src: torch.Tensor):
+    """Write `src` [L, KVH, P8, D] (HF order, P8 a multiple of 8) into slots
+    [0, P8) of stream b of a KV tile layout cache."""
+    L, H, P8, D = src.shape
+    kv_tiles(cache)[:, b, :, :P8 // 8] = src.view(L, H, P8 // 8, 8, D // 8, 8).permute(0, 1, 2, 4, 3, 5)
 
 
 def tile_weight(w: torch.Tensor) -> torch.Tensor:
@@ -210,10 +234,17 @@ class Qwen3VLBatchDecodeEngine:
         pos3 = torch.as_tensor(pos3, dtype=torch.int64).reshape(3, P).cpu()
         s, dev = self.shape, self.device
         with torch.cuda.device(dev):
-            logits = prefill(tokens.to(dev), pos3.to(dev), self.embed, self.final_norm, self.layers,
-                             self.k_cache[:, b:b + 1], self.v_cache[:, b:b + 1], num_heads=s.num_heads,
-                             num_kv_heads=s.num_kv_heads, head_dim=s.head_dim, eps=float(s.rms_eps),
-                             inv_freq=self._inv_freq.to(dev), mrope_section=s.mrope_section)
+            # the prefill writes HF-ordered slots [0, P); they go into the
+            # stream's slice in the KV tile layout (whole 8-slot groups)
+            P8 = (P + 7) // 8 * 8
+            kt = torch.zeros((s.num_layers, 1, s.num_kv_heads, P8, s.head_dim), dtype=torch.float16, device=dev)
+            vt = torch.zeros_like(kt)
+            logits = prefill(tokens.to(dev), pos3.to(dev), self.embed, self.final_norm, self.layers, kt, vt,
+                             num_heads=s.num_heads, num_kv_heads=s.num_kv_heads, head_dim=s.head_dim,
+                             eps=float(s.rms_eps), inv_freq=self._inv_freq.to(dev), mrope_section=s.mrope_section)
+            kv_store_tiles(self.k_cache, b, kt[:, 0])
+            kv_store_tiles(self.v_cache, b, vt[:, 0])
+            del kt, vt
             first = int(torch.argmax(logits))
             if self.logits is not None:
                 self.logits[b, (P - 1) % self.logits_ring].copy_(logits.to(torch.float16))

@@ -269,6 +269,10 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32_u4(uint32_t taddr, uint4 (&w)
       : "r"(taddr)
       : "memory");
 }
+// 32 lanes x 2 columns: a = column col, b = column col + 1 of this thread's lane.
+__device__ __forceinline__ void tmem_ld_32x32b_x2(uint32_t taddr, uint32_t& a, uint32_t& b) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(taddr) : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Software grid barrier over `nct` co-resident CTAs, split into arrive and

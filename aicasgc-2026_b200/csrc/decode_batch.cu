@@ -15,7 +15,8 @@
 //               with the RMSNorm prologue at HF's fp16 rounding points; then
 //               two sets of 4 warps (one warp per TMEM lane quarter each) run
 //               the epilogues of alternate row groups.  Attention: the
-//               split-KV units of all streams, tiles taken in pairs.
+//               split-KV units of all streams, tiles taken in pairs, on
+//               the tensor cores.
 //   warp 9      L2 prefetch cursor, kL2Ahead tiles ahead of the ring.
 //   warp 10     MMA issuer and TMEM owner (below).
 //
@@ -43,10 +44,22 @@
 // fp16 in the operand layout, one release add per CTA and phase on a
 // completion counter, one acquire wait and a bulk copy per reader.
 //
+// KV cache: per (stream, KV head) slice of max_len slots, in the KV tile
+// layout: slot p, dim d at element (p / 8) * 1024 + (d / 8) * 64 + (p % 8) * 8
+// + d % 8 (8-slot groups of 2 KB; within a group, 16 core matrices of 8 slots
+// x 8 dims).  A 64-slot chunk is 16 contiguous KB, so one bulk copy per K / V
+// lands it as a tcgen05 operand: K-major for S = K Q^T (LBO 128, SBO 2048)
+// and MN-major for O = V^T P^T (LBO 2048, SBO 128).
+//
 // Attention: units (stream, KV head, 64-slot chunk) over all active streams,
 // split contiguously over the CTAs.  A segment's tiles go in pairs (warps 0..3
-// and 4..7, 16 positions per warp); each CTA first stores the (log-sum-exp,
-// acc) partials of all its segments, then merges its slice of every group it
+// and 4..7, one warp per TMEM lane quarter each): per tile one elected thread
+// issues S = K Q^T (M = 128, N = 16: the 2 query heads of the KV head, zero
+// rows after them) into TMEM; the quarter-0/1 warps read the 64 scores, take
+// the tile maximum, and write the fp16 probabilities as the B operand of
+// O = V^T P^T (M = 128 head dims); each warp folds its 32 dims of O into the
+// running (max, sum, acc).  Each CTA first stores the (log-sum-exp, acc)
+// partials of all its segments, then merges its slice of every group it
 // shares, in a fixed split order.  Every wait is bounded (aicas_device.cuh);
 // after a failed wait the kernel keeps walking the same program without
 // waiting and ends with the error recorded.
@@ -107,6 +120,23 @@ constexpr int kL2Ahead = 8;
 // instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0), both
 // K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// attention: S = K Q^T (M = 128, N = 16, both K-major) and O = V^T P^T (A
+// MN-major: bit 15)
+constexpr uint32_t kIdescQK = (1u << 4) | ((uint32_t)(16 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescQK | (1u << 15);
+// attention operands in the streams' operand buffer (idle during an attention
+// phase): the queries [16 rows x 128 dims] at 0, each warp set's
+// probabilities [16 rows x 64 slots] at kAttnPOff + set * 2048
+constexpr int kAttnPOff = 4096;
+constexpr int kAttnOpBytes = kAttnPOff + 2 * 2048;
+// TMEM columns of warp set `set` during an attention phase (the GEMV
+// accumulators are idle then): S at 64 set, O at 64 set + 32
+constexpr int kAttnTmemStride = 64;
+
+// Byte offset of slot r, 8-dim block blk of a tile in the KV tile layout.
+__host__ __device__ __forceinline__ uint32_t kvt_off(int r, int blk) {
+  return (uint32_t)((r >> 3) * 2048 + blk * 128 + (r & 7) * 16);
+}
 
 static_assert(kAttnChunk * kHD * 2 * 2 == kTileBytes, "attention tile must fill one stage");
 static_assert(offsetof(AicasBatchScratch, bar_count) == offsetof(AicasScratch, bar_count) &&
@@ -125,12 +155,12 @@ struct StreamIn {
 
 struct AttnSmem {
   float kf[kHD], vf[kHD];
-  float wm[kConsumerWarps][2];
-  float wl[kConsumerWarps][2];
-  float wacc[kConsumerWarps][2][kHD];
-  __align__(16) __half qh[2][kHD];  // the segment's queries as fp16 (their values are fp16-rounded)
-  float2 sc[kConsumerWarps][16];     // per warp: the probabilities (both heads) of its 16 positions
-  __half nw[2 * kHD];  // q_norm, k_norm weights of the running phase
+  float wm[2][2];  // per warp set: running max, sum (per query head); acc per head dim
+  float wl[2][2];
+  float wacc[2][2][kHD];
+  float tmax[2][2][2];  // per warp set, TMEM lane quarter 0 / 1, head: the tile's maximum score
+  float tsum[2][2][2];  // ... and its sum of fp16 probabilities
+  __half nw[2 * kHD];   // q_norm, k_norm weights of the running phase
 };
 
 struct __align__(128) Smem {
@@ -153,6 +183,7 @@ struct __align__(128) Smem {
   uint64_t cdone;   // all consumer warps are done with TMEM
   uint64_t mdone;   // every MMA the issuer launched has completed
   uint64_t xfull;   // a counted input has landed in the operand buffer (bulk copies)
+  uint64_t amma[2];  // per warp set: its attention MMAs (S, then O) have completed
   uint32_t ring_it;
   uint32_t tmem_base;
   int32_t last_cta;
@@ -303,7 +334,7 @@ struct Cursor {
       const size_t off = (((size_t)b * d.kv_heads + h) * d.max_len + p0) * kHD * 2;
       td.src = reinterpret_cast<const uint8_t*>(d.k_cache) + off;
       td.src_stride = reinterpret_cast<const uint8_t*>(d.v_cache) - reinterpret_cast<const uint8_t*>(d.k_cache);
-      td.bytes = min(kAttnChunk, valid - p0) * kHD * 2;
+      td.bytes = ((min(kAttnChunk, valid - p0) + 7) & ~7) * kHD * 2;  // whole 8-slot groups
       td.pieces = 2;
       td.mma = false;
       td.c = td.part = 0;
@@ -550,6 +581,7 @@ struct Consumer {
   uint32_t xfull_n = 0;     // completions of sm.xfull so far
   uint32_t gc = 0;   // accumulator groups consumed (epilogue warps)
   uint32_t rit = 0;  // ring tiles passed (GEMV tiles via the MMA warp, attention tiles read in place)
+  uint32_t acnt = 0;  // completed attention MMA groups of this warp's set (sm.amma parity)
   int ph = 0;
 
   __device__ __forceinline__ bool active(int b) const { return b < nb && sm.sin[b].active; }
@@ -983,104 +1015,122 @@ struct Consumer {
     }
   }
 
-  // One warp's 16 positions p0 .. p0 + 15 of a 64-slot K/V tile (ring stage
-  // `tile`): online-softmax update of (m, l, acc) for both query heads.
-  // Scores: lane (pi, qc) dots positions p0 + pi and p0 + 8 + pi over dims
-  // qc*32 .. qc*32+31 (exact fp16 products, fp32 sums; K rows read in an
-  // order rotated by pi, free of bank conflicts); two shuffles finish each.
-  // P V: lane l accumulates dims 4l .. 4l+3; the probabilities pass through
-  // the warp's shared-memory row.  Slot `pos` (this step's k / v) comes from
-  // at.kf / at.vf: the tile may have been loaded before it was written.
-  __device__ __forceinline__ void attend_tile(const uint8_t* tile, int p0, int pos, int valid, float scale, int pi,
-                                              int qc, float (&m)[2], float (&l)[2], float (&acc)[2][4]) {
+  // Named barrier of warp set `set` (consumer warps 4 set .. 4 set + 3).
+  __device__ __forceinline__ static void set_sync(int set) {
+    asm volatile("bar.sync %0, 128;" ::"r"(2 + set) : "memory");
+  }
+
+  // One 64-slot K/V tile (ring stage st, KV tile layout) for warp set `set`
+  // on the tensor cores; q = this warp's TMEM lane quarter, n = valid slots
+  // of the tile, prow = this step's slot in the tile (-1: none).
+  //   1. This step's k / v row (it may have been written after the tile was
+  //      copied) and zeros for V rows [n, 16 ceil(n / 16)) go into the
+  //      staged tile, so the last O = V^T P^T step reads no stale slot.
+  //   2. S = K Q^T: 8 MMAs of M = 128 (TMEM lanes 0..63: the tile's slots;
+  //      lanes 64..127 read the V half behind the K tile and are ignored),
+  //      N = 16 (query heads 2h, 2h + 1, then zero rows), fp32 in TMEM.
+  //   3. Lane quarters 0 and 1 (slot = TMEM lane) mask slots >= n, scale,
+  //      take the tile maximum per head, and write P = exp(s - m) as fp16 in
+  //      the B operand of step 4 (the sum uses the rounded values).
+  //   4. O = V^T P^T: ceil(n / 16) MMAs of M = 128 (head dims), K = 16 slots.
+  //   5. Each warp reads its 32 dims of O and folds them into (m, l, acc).
+  // The elected thread (lane 0 of the set's first warp) issues the MMAs; a
+  // commit on sm.amma[set] marks each group done (waited by every thread
+  // of the set, ignoring the abort word: no MMA is still reading the stage
+  // or writing TMEM when the set moves on).
+  __device__ __forceinline__ void attend_tile_tc(int set, int q, int st, int n, int prow, float scale,
+                                                 float (&m)[2], float (&l)[2], float (&acc)[2]) {
     AttnSmem& at = sm.at;
-    const int row0 = p0 % kAttnChunk;  // the warp's first row in the tile
-    float sg[2][2];
+    uint8_t* const tile = sm.ring[st];
+    const int tl = (w & 3) * 32 + lane;  // thread of the set
+    const int n16 = (n + 15) & ~15;
+    if (prow >= 0 || n < n16) {
+      if (prow >= 0 && tl < 32) {  // 16 lanes K, 16 lanes V: 8 dims each
+        const int kv = tl >> 4, blk = tl & 15;
+        const float* src = (kv == 0 ? at.kf : at.vf) + blk * 8;
+        uint4 pk;
+        __half2* ph = reinterpret_cast<__half2*>(&pk);
 #pragma unroll
-    for (int a2 = 0; a2 < 2; ++a2) {
-      sg[a2][0] = sg[a2][1] = 0.f;
-      const int prow = row0 + 8 * a2 + pi;
-      if (p0 + 8 * a2 + pi == pos) {
+        for (int e = 0; e < 4; ++e) ph[e] = __floats2half2_rn(src[2 * e], src[2 * e + 1]);
+        *reinterpret_cast<uint4*>(tile + kv * (kTileBytes / 2) + kvt_off(prow, blk)) = pk;
+      }
+      for (int i = tl; i < (n16 - n) * 16; i += 128)
+        *reinterpret_cast<uint4*>(tile + kTileBytes / 2 + kvt_off(n + i / 16, i % 16)) = make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();
+    }
+    set_sync(set);
+    const bool leader = tl == 0;
+    const uint32_t t_s = smem_addr(tile), q_s = smem_addr(sm.xa), p_s = q_s + kAttnPOff + set * 2048;
+    const uint32_t dS = tmem + set * kAttnTmemStride, dO = dS + 32;
+    if (leader) {
+      tc_fence_after();
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int qo = qc * 32 + 8 * ((jj + pi) & 3);
-          uint4 kv;
-          __half2* kh = reinterpret_cast<__half2*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) kh[e] = __floats2half2_rn(at.kf[qo + 2 * e], at.kf[qo + 2 * e + 1]);
-          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
-          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
-        }
-      } else {
-        const uint8_t* krow = tile + prow * (kHD * 2) + qc * 64;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int jr = (jj + pi) & 3;
-          const uint4 kv = *reinterpret_cast<const uint4*>(krow + 16 * jr);
-          const int qo = qc * 32 + 8 * jr;
-          sg[a2][0] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[0][qo]), sg[a2][0]);
-          sg[a2][1] = dot8_f16(kv, *reinterpret_cast<const uint4*>(&at.qh[1][qo]), sg[a2][1]);
-        }
+      for (int ks = 0; ks < kHD / kMmaK; ++ks)
+        umma_f16(dS, smem_desc_kmajor(t_s + 256 * ks, 128, 2048), smem_desc_kmajor(q_s + 256 * ks, 128, 2048),
+                 kIdescQK, ks > 0 ? 1u : 0u);
+      tcgen05_commit(&sm.amma[set]);
+    }
+    mbar_wait_copy(&sm.amma[set], acnt & 1u, s, kErrTmemTimeout);
+    ++acnt;
+    tc_fence_after();
+    float x0 = -INFINITY, x1 = -INFINITY;
+    const int r = 32 * q + lane;  // the slot of this lane (quarters 0, 1)
+    if (q < 2) {
+      uint32_t s0, s1;
+      tmem_ld_32x32b_x2(dS + ((uint32_t)(32 * q) << 16), s0, s1);
+      tmem_wait_ld();
+      if (r < n) {
+        x0 = __uint_as_float(s0) * scale;
+        x1 = __uint_as_float(s1) * scale;
+      }
+      const float t0 = warp_max(x0), t1 = warp_max(x1);
+      if (lane == 0) {
+        at.tmax[set][q][0] = t0;
+        at.tmax[set][q][1] = t1;
       }
     }
-    float pr[2][2];
+    set_sync(set);
+    float mn[2];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) mn[g] = fmaxf(m[g], fmaxf(at.tmax[set][0][g], at.tmax[set][1][g]));
+    if (q < 2) {
+      const __half p0 = __float2half_rn(x0 == -INFINITY ? 0.f : expf(x0 - mn[0]));
+      const __half p1 = __float2half_rn(x1 == -INFINITY ? 0.f : expf(x1 - mn[1]));
+      // B operand [16 rows x 64 slots], K-major: row g, slot r at (r / 8) 128 + g 16 + (r % 8) 2
+      uint8_t* pb = sm.xa + kAttnPOff + set * 2048 + (r >> 3) * 128 + (r & 7) * 2;
+      *reinterpret_cast<__half*>(pb) = p0;
+      *reinterpret_cast<__half*>(pb + 16) = p1;
+      const float s0 = warp_sum(__half2float(p0)), s1 = warp_sum(__half2float(p1));
+      if (lane == 0) {
+        at.tsum[set][q][0] = s0;
+        at.tsum[set][q][1] = s1;
+      }
+      fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    set_sync(set);
+    if (leader) {
+      tc_fence_after();
+      for (int ks = 0; ks < n16 / kMmaK; ++ks)
+        umma_f16(dO, smem_desc_kmajor(t_s + kTileBytes / 2 + 4096 * ks, 2048, 128),
+                 smem_desc_kmajor(p_s + 256 * ks, 128, 1024), kIdescPV, ks > 0 ? 1u : 0u);
+      tcgen05_commit(&sm.amma[set]);
+    }
+    mbar_wait_copy(&sm.amma[set], acnt & 1u, s, kErrTmemTimeout);
+    ++acnt;
+    tc_fence_after();
+    uint32_t o0, o1;
+    tmem_ld_32x32b_x2(dO + ((uint32_t)(32 * q) << 16), o0, o1);
+    tmem_wait_ld();
+    const float ov[2] = {__uint_as_float(o0), __uint_as_float(o1)};
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
-      float x[2];
-#pragma unroll
-      for (int a2 = 0; a2 < 2; ++a2) {
-        float v = sg[a2][g];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        x[a2] = p0 + 8 * a2 + pi < valid ? v * scale : -INFINITY;
-      }
-      float cm = fmaxf(x[0], x[1]);  // the warp's 16 positions: pairs, then lanes differing in bits 2..4
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-      const float mn = fmaxf(m[g], cm);
-      pr[0][g] = pr[1][g] = 0.f;
-      if (mn == -INFINITY) continue;  // (warp-uniform) no valid position yet
-#pragma unroll
-      for (int a2 = 0; a2 < 2; ++a2) pr[a2][g] = x[a2] == -INFINITY ? 0.f : expf(x[a2] - mn);
-      float ps = pr[0][g] + pr[1][g];
-      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-      const float corr = expf(m[g] - mn);
-      l[g] = l[g] * corr + ps;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
-      m[g] = mn;
+      const float corr = m[g] == -INFINITY ? 0.f : expf(m[g] - mn[g]);
+      l[g] = l[g] * corr + (at.tsum[set][0][g] + at.tsum[set][1][g]);
+      acc[g] = acc[g] * corr + ov[g];
+      m[g] = mn[g];
     }
-    if (qc == 0) {
-      at.sc[w][pi] = make_float2(pr[0][0], pr[0][1]);
-      at.sc[w][8 + pi] = make_float2(pr[1][0], pr[1][1]);
-    }
-    __syncwarp();
-    const uint8_t* vt = tile + kTileBytes / 2;
-#pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
-      if (p0 + i >= valid) break;
-      const float2 pp = at.sc[w][i];
-      float vv[4];
-      if (p0 + i == pos) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) vv[e] = at.vf[lane * 4 + e];
-      } else {
-        const uint2 vr = *reinterpret_cast<const uint2*>(vt + (row0 + i) * kHD * 2 + lane * 8);
-        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-        vv[0] = __low2float(vh[0]);
-        vv[1] = __high2float(vh[0]);
-        vv[2] = __low2float(vh[1]);
-        vv[3] = __high2float(vh[1]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        acc[0][e] += pp.x * vv[e];
-        acc[1][e] += pp.y * vv[e];
-      }
-    }
+    tc_fence_before();
   }
 
   __device__ __forceinline__ void run_attention(const AicasPhase& d) {
@@ -1096,6 +1146,13 @@ struct Consumer {
     const int na = attn_ctas(U, nct);
     const Range rg = cta < na ? split_range(U, na, cta, 0) : Range{0, 0};
     if (kTrace && tid == 0) trace_put(a, ph, 5, rg.count);
+    // the MMA operands' zero rows: queries and both sets' probabilities
+    // (the streams' operand buffer is idle until the next GEMV phase)
+    for (int i = tid; i < kAttnOpBytes / 16; i += kConsumerThreads)
+      reinterpret_cast<uint4*>(sm.xa)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+    tc_fence_before();  // the previous phase's TMEM reads come before these MMAs
+    consumer_sync(kConsumerThreads);
     uint64_t tile_wait = 0, seg_ns = 0;
     const uint32_t* qkv_w = reinterpret_cast<const uint32_t*>(d.x);
     const uint32_t x_epoch = (epoch_base + (uint32_t)d.x_src + 1) & 0xffffu;
@@ -1104,13 +1161,11 @@ struct Consumer {
     const int qsz = d.q_heads * kHD, kvsz = d.kv_heads * kHD;
     const float scale = d.scale;
     const uint32_t ep = epoch_base + (uint32_t)ph + 1;
-    float m[2], l[2], acc[2][4];
-    // Tiles of a segment go in pairs: warps 0..3 take the first, warps 4..7
-    // the second (slot = w / 4); warp wq = w % 4 of a slot owns the tile's
-    // positions 16 wq .. 16 wq + 15.  Score lanes: (pi = lane / 4, dim quarter
-    // qc = lane % 4) handle positions 16 wq + pi and 16 wq + 8 + pi.
-    const int slot = w >> 2, wq = w & 3;
-    const int pi = lane >> 2, qc = lane & 3;
+    // Tiles of a segment go in pairs: warps 0..3 (set 0) take the first,
+    // warps 4..7 (set 1) the second; a set's state is (m, l) per query head,
+    // uniform over the set, and acc of head dim 32 q + lane per head.
+    float m[2], l[2], acc[2];
+    const int set = w >> 2, q = (w + 1) & 3;
     bool first_seg = true;
     for (int u0 = rg.start; u0 < rg.start + rg.count;) {
       const int b = au.stream_of(u0);
@@ -1136,8 +1191,12 @@ struct Consumer {
           const __half2* hp = reinterpret_cast<const __half2*>(&raw);
           float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
           norm_rope_head(v, at.nw, d.eps, cs, sn);
-          *reinterpret_cast<__half2*>(&at.qh[w][lane * 4]) = __floats2half2_rn(v[0], v[1]);
-          *reinterpret_cast<__half2*>(&at.qh[w][lane * 4 + 2]) = __floats2half2_rn(v[2], v[3]);
+          // row w of the queries operand [16 rows x 128 dims], K-major:
+          // dims 4 lane .. 4 lane + 3 at (dim / 8) 128 + w 16 + (dim % 8) 2
+          __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
+          *reinterpret_cast<uint2*>(sm.xa + (lane >> 1) * 128 + w * 16 + (lane & 1) * 8) =
+              *reinterpret_cast<uint2*>(o);
+          fence_proxy_async_smem();
         } else if (has_pos && w < 4) {  // this step's k (warp 2) / v (warp 3) of head h
           const int off = qsz + (w == 2 ? 0 : kvsz) + h * kHD + lane * 4;
           const uint2 raw = ll_poll4(xw, off, x_epoch, s);
@@ -1148,8 +1207,9 @@ struct Consumer {
 #pragma unroll
           for (int e = 0; e < 4; ++e) dst[lane * 4 + e] = v[e];
           __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
-          __half* cache = w == 2 ? kc : vc;
-          *reinterpret_cast<uint2*>(cache + (head_off + pos) * kHD + lane * 4) = *reinterpret_cast<uint2*>(o);
+          __half* cache = w == 2 ? kc : vc;  // KV tile layout
+          *reinterpret_cast<uint2*>(cache + head_off * kHD + (pos >> 3) * 1024 + (lane >> 1) * 64 + (pos & 7) * 8 +
+                                    (lane & 1) * 4) = *reinterpret_cast<uint2*>(o);
         }
       }
       consumer_sync(kConsumerThreads);
@@ -1162,13 +1222,12 @@ struct Consumer {
       for (int g = 0; g < 2; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+        acc[g] = 0.f;
       }
 #pragma unroll 1
       for (int t = 0; t < nseg; t += 2) {
-        if (t + slot < nseg) {
-          const uint32_t ri = rit + slot;
+        if (t + set < nseg) {
+          const uint32_t ri = rit + set;
           const int st = ri % kStages;
           if (kTrace && tid == 0) {
             const uint64_t w0 = globaltimer_ns();
@@ -1177,23 +1236,23 @@ struct Consumer {
           } else {
             mbar_wait_bounded(&sm.full[st], (ri / kStages) & 1u, s, kErrFullTimeout);
           }
-          attend_tile(sm.ring[st], (j0 + t + slot) * kAttnChunk + 16 * wq, pos, valid, scale, pi, qc, m, l, acc);
+          const int p0 = (j0 + t + set) * kAttnChunk;
+          attend_tile_tc(set, q, st, min(kAttnChunk, valid - p0), pos - p0 < kAttnChunk ? pos - p0 : -1, scale, m,
+                         l, acc);
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.cempty[st]);
         }
         rit += t + 1 < nseg ? 2 : 1;
       }
-      // segment end: merge the 8 warps' states into this CTA's partial
-      if (lane == 0) {
-        at.wm[w][0] = m[0];
-        at.wm[w][1] = m[1];
-        at.wl[w][0] = l[0];
-        at.wl[w][1] = l[1];
+      // segment end: merge the 2 sets' states into this CTA's partial
+      if ((w & 3) == 0 && lane == 0) {
+        at.wm[set][0] = m[0];
+        at.wm[set][1] = m[1];
+        at.wl[set][0] = l[0];
+        at.wl[set][1] = l[1];
       }
 #pragma unroll
-      for (int g = 0; g < 2; ++g)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) at.wacc[w][g][lane * 4 + e] = acc[g][e];
+      for (int g = 0; g < 2; ++g) at.wacc[set][g][32 * q + lane] = acc[g];
       consumer_sync(kConsumerThreads);
       {
         const int gfirst = select_i(au.pre, b) + h * cph;
@@ -1202,10 +1261,10 @@ struct Consumer {
         const int g = tid / kHD, t = tid % kHD;
         float M = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) M = fmaxf(M, at.wm[i][g]);
+        for (int i = 0; i < 2; ++i) M = fmaxf(M, at.wm[i][g]);
         float L = 0.f, A = 0.f;
-#pragma unroll 1
-        for (int i = 0; i < kConsumerWarps; ++i) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
           const float mi = at.wm[i][g];
           if (mi != -INFINITY) {
             const float f = expf(mi - M);
@@ -1421,6 +1480,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_kernel(const __grid_
     mbar_init(&sm.cdone, kConsumerWarps);
     mbar_init(&sm.mdone, 1);
     mbar_init(&sm.xfull, 1);
+    mbar_init(&sm.amma[0], 1);
+    mbar_init(&sm.amma[1], 1);
     sm.ring_it = 0;
     sm.last_cta = 0;
     mbar_fence_init();
@@ -1542,7 +1603,7 @@ static int validate(const AicasPhase& d) {
       return AICAS_OK;
     case AICAS_PH_ATTN:
       if (d.kv_heads < 1 || d.kv_heads > AICAS_MAX_KV_HEADS || d.q_heads != 2 * d.kv_heads) return AICAS_ERR_SHAPE;
-      if (d.max_len < 1) return AICAS_ERR_SHAPE;
+      if (d.max_len < 8 || d.max_len % 8 != 0) return AICAS_ERR_SHAPE;  // whole 8-slot groups
       if (d.k != (d.q_heads + 2 * d.kv_heads) * kHD || d.n != d.q_heads * kHD) return AICAS_ERR_SHAPE;
       if ((d.flags & AICAS_F_Q_READY) || !(d.flags & AICAS_F_LL_IN) ||
           !(d.flags & (AICAS_F_LL_OUT | AICAS_F_CNT_OUT)) || d.x_src < 0)

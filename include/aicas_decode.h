@@ -225,8 +225,11 @@ AICAS_API int aicas_decode_program_trace_f16(const AicasPhase* device_phases, in
  *     aicas_tile_weight_f16 converts a row-major [n, k] matrix;
  *   - attention: x is [nb][q_heads*128 + 2*kv_heads*128] (q, k, v of each
  *     stream; phase field k = that row length), out is [nb][q_heads*128]
- *     (phase field n), K/V caches [nb][kv_heads][max_len][128] (HF StaticLayer
- *     of batch nb), q/k norm + MRoPE + KV write always on (no F_Q_READY);
+ *     (phase field n), K/V caches [nb][kv_heads][max_len * 128] fp16 with
+ *     max_len % 8 == 0, each (stream, head) slice in the KV tile layout:
+ *     slot p, dim d at element (p/8)*1024 + (d/8)*64 + (p%8)*8 + d%8 (the
+ *     size of HF StaticLayer of batch nb, not its order), q/k norm + MRoPE +
+ *     KV write always on (no F_Q_READY);
  *   - the LM head writes stream b's logits to states[b].logits (if set) and
  *     advances states[b] (out_tokens, script, EOS) like the batch-1 step.
  * A stream whose state has done_step != 0 is inactive: it is skipped (no KV

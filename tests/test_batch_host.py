@@ -1,12 +1,12 @@
 """Host side of the batched decode step, on the CPU: the tensor-core tile
-layout of the weights, the batch rules of the C ABI's phase validation and the
-batch scratch size.  No kernel is launched."""
+layout of the weights and of the KV cache, the batch rules of the C ABI's
+phase validation and the batch scratch size.  No kernel is launched."""
 import numpy as np
 import pytest
 import torch
 
 import _native
-from batch_engine import tile_weight
+from batch_engine import kv_hf_layout, kv_store_tiles, kv_tiles, tile_weight
 
 
 def test_tile_weight_layout():
@@ -34,6 +34,30 @@ def test_tile_weight_rejects_bad_shapes():
         tile_weight(torch.zeros(12, 2048))
     with pytest.raises(_native.AicasError):
         tile_weight(torch.zeros(16, 1000))
+
+
+def test_kv_tile_layout():
+    """Slot p, dim d of a (layer, stream, head) slice sits at element
+    (p // 8) * 1024 + (d // 8) * 64 + (p % 8) * 8 + d % 8 of the slice: the
+    offsets the batched kernel's bulk copies, MMA descriptors and this
+    step's k / v write use."""
+    g = torch.Generator().manual_seed(3)
+    L, B, H, M, D = 2, 3, 2, 64, 128
+    cache = torch.zeros((L, B, H, M, D), dtype=torch.float16)
+    P = 21  # a prompt that ends inside an 8-slot group
+    P8 = 24
+    src = torch.zeros((L, H, P8, D), dtype=torch.float16)
+    src[:, :, :P] = torch.randn((L, H, P, D), generator=g).half()
+    kv_store_tiles(cache, 1, src)
+    flat = cache.view(L, B, H, M * D)
+    for (l, h, p, d) in [(0, 0, 0, 0), (1, 1, 20, 127), (0, 1, 7, 8), (1, 0, 9, 63), (0, 0, 16, 65)]:
+        off = (p // 8) * 1024 + (d // 8) * 64 + (p % 8) * 8 + d % 8
+        assert flat[l, 1, h, off] == src[l, h, p, d], (l, h, p, d)
+    hf = kv_hf_layout(cache)
+    assert torch.equal(hf[:, 1, :, :P8], src)
+    assert not hf[:, 1, :, P8:].any() and not hf[:, 0].any() and not hf[:, 2].any()
+    # a 64-slot chunk is one contiguous 16 KB piece of its slice
+    assert kv_tiles(cache)[0, 1, 0, :8].reshape(-1).data_ptr() == cache[0, 1, 0].data_ptr()
 
 
 def test_batch_scratch_bytes():
