@@ -44,8 +44,13 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* __restri
   const size_t base = (size_t)blockIdx.x * cols;
   const int nv = cols / 8;
   constexpr int kMaxV = 4;  // uint4 per thread (cols <= 8192)
-  uint4 v[kMaxV];
+  uint4 v[kMaxV], wv[kMaxV];
   float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxV; ++i) {  // the norm weights load while the sum of squares is reduced
+    const int c = threadIdx.x + i * 256;
+    if (c < nv) wv[i] = __ldg(reinterpret_cast<const uint4*>(norm_w) + c);
+  }
 #pragma unroll
   for (int i = 0; i < kMaxV; ++i) {
     const int c = threadIdx.x + i * 256;
@@ -80,9 +85,8 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __half* __restri
   for (int i = 0; i < kMaxV; ++i) {
     const int c = threadIdx.x + i * 256;
     if (c < nv) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(norm_w) + c);
       __half2* hp = reinterpret_cast<__half2*>(&v[i]);
-      const __half2* wp = reinterpret_cast<const __half2*>(&wv);
+      const __half2* wp = reinterpret_cast<const __half2*>(&wv[i]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 f = __half22float2(hp[q]);
@@ -105,6 +109,22 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   __shared__ float tcos[kHD / 2], tsin[kHD / 2];
   const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = hq + 2 * hkv;  // qkv row length in heads
+  const size_t slot = (size_t)start + t;
+  constexpr int kTasks = 4;  // head tasks of a warp whose loads are in flight together
+  uint2 raw[kTasks], nwr[kTasks];
+  // the warp's tasks task0, task0 + 8, ..., task0 + 8 (kTasks - 1): every
+  // load issued before any is used
+  auto load_round = [&](int task0) {
+#pragma unroll
+    for (int j = 0; j < kTasks; ++j) {
+      const int task = task0 + 8 * j;
+      raw[j] = task < row ? *reinterpret_cast<const uint2*>(qkv + ((size_t)t * row + task) * kHD + lane * 4)
+                          : make_uint2(0, 0);
+      nwr[j] = task < hq + hkv ? __ldg(reinterpret_cast<const uint2*>(task < hq ? qn_w : kn_w) + lane)
+                               : make_uint2(0, 0);
+    }
+  };
+  load_round(w);  // in flight while the rotary table is built
   // the token's 64 rotary frequencies, once per CTA: frequency i takes axis 1
   // (h) when i % 3 == 1 and i < 3 sec1, axis 2 (w) when i % 3 == 2 and
   // i < 3 sec2, else axis 0 (t); cos / sin in fp32, rounded to fp16
@@ -126,60 +146,62 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     cs[e] = tcos[(lane * 4 + e) & 63];
     sn[e] = tsin[(lane * 4 + e) & 63];
   }
-  const size_t slot = (size_t)start + t;
-  for (int task = w; task < row; task += 8) {
-    const __half* src = qkv + ((size_t)t * row + task) * kHD + lane * 4;
-    const uint2 raw = *reinterpret_cast<const uint2*>(src);
-    const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-    float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
-    if (task < hq + hkv) {
-      const uint2 nwr = __ldg(reinterpret_cast<const uint2*>(task < hq ? qn_w : kn_w) + lane);
-      const __half2* nh = reinterpret_cast<const __half2*>(&nwr);
-      const float nwf[4] = {__low2float(nh[0]), __high2float(nh[0]), __low2float(nh[1]), __high2float(nh[1])};
-      float ss = 0.f;
+  for (int task0 = w; task0 < row; task0 += 8 * kTasks) {
+    if (task0 != w) load_round(task0);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
-      const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
-      float xn[4];
+    for (int j = 0; j < kTasks; ++j) {
+      const int task = task0 + 8 * j;
+      if (task >= row) break;
+      const __half2* hp = reinterpret_cast<const __half2*>(&raw[j]);
+      float v[4] = {__low2float(hp[0]), __high2float(hp[0]), __low2float(hp[1]), __high2float(hp[1])};
+      if (task < hq + hkv) {
+        const __half2* nh = reinterpret_cast<const __half2*>(&nwr[j]);
+        const float nwf[4] = {__low2float(nh[0]), __high2float(nh[0]), __low2float(nh[1]), __high2float(nh[1])};
+        float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) xn[e] = r16(nwf[e] * r16(v[e] * inv));
+        for (int e = 0; e < 4; ++e) ss += v[e] * v[e];
+        const float inv = rsqrtf(warp_sum(ss) / (float)kHD + eps);
+        float xn[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
-        const float rot = lane < 16 ? -p : p;
-        v[e] = r16(r16(xn[e] * cs[e]) + r16(rot * sn[e]));
+        for (int e = 0; e < 4; ++e) xn[e] = r16(nwf[e] * r16(v[e] * inv));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p = __shfl_xor_sync(0xffffffffu, xn[e], 16);
+          const float rot = lane < 16 ? -p : p;
+          v[e] = r16(r16(xn[e] * cs[e]) + r16(rot * sn[e]));
+        }
       }
+      const __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
+      __half* dst;
+      if (task < hq) dst = q_out + ((size_t)t * hq + task) * kHD;
+      else if (task < hq + hkv) dst = k_cache + ((size_t)(task - hq) * max_len + slot) * kHD;
+      else dst = v_cache + ((size_t)(task - hq - hkv) * max_len + slot) * kHD;
+      *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<const uint2*>(o);
     }
-    const __half2 o[2] = {__floats2half2_rn(v[0], v[1]), __floats2half2_rn(v[2], v[3])};
-    __half* dst;
-    if (task < hq) dst = q_out + ((size_t)t * hq + task) * kHD;
-    else if (task < hq + hkv) dst = k_cache + ((size_t)(task - hq) * max_len + slot) * kHD;
-    else dst = v_cache + ((size_t)(task - hq - hkv) * max_len + slot) * kHD;
-    *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<const uint2*>(o);
   }
 }
 
 // ---------------------------------------------------------------- SiLU * up
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int P,
                                                        int inter) {
-  const int n8 = inter / 8;
-  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < (size_t)P * n8; e += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = e / n8, c = e % n8;
-    const uint4 g = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter) + c);
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter) + c);
-    const __half2* gp = reinterpret_cast<const __half2*>(&g);
-    const __half2* up = reinterpret_cast<const __half2*>(&u);
-    uint4 o;
-    __half2* op = reinterpret_cast<__half2*>(&o);
+  // CTA (x, y): row y, 8-column groups 256 x + thread
+  const int n8 = inter / 8, c = blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t r = blockIdx.y;
+  if (c >= n8) return;
+  const uint4 g = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter) + c);
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter) + c);
+  const __half2* gp = reinterpret_cast<const __half2*>(&g);
+  const __half2* up = reinterpret_cast<const __half2*>(&u);
+  uint4 o;
+  __half2* op = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 gf = __half22float2(gp[q]), uf = __half22float2(up[q]);
-      // SiLU in fp32 (the fast exp: its error is far below the fp16 rounding that follows)
-      const float s0 = r16(gf.x / (1.0f + __expf(-gf.x))), s1 = r16(gf.y / (1.0f + __expf(-gf.y)));
-      op[q] = __floats2half2_rn(s0 * uf.x, s1 * uf.y);
-    }
-    reinterpret_cast<uint4*>(act + r * inter)[c] = o;
+  for (int q = 0; q < 4; ++q) {
+    const float2 gf = __half22float2(gp[q]), uf = __half22float2(up[q]);
+    // SiLU in fp32 (the fast exp: its error is far below the fp16 rounding that follows)
+    const float s0 = r16(gf.x / (1.0f + __expf(-gf.x))), s1 = r16(gf.y / (1.0f + __expf(-gf.y)));
+    op[q] = __floats2half2_rn(s0 * uf.x, s1 * uf.y);
   }
+  reinterpret_cast<uint4*>(act + r * inter)[c] = o;
 }
 
 // ---------------------------------------------------------------- causal flash attention
@@ -429,8 +451,8 @@ AICAS_API int aicas_prefill_silu_mul_f16(const void* gate_up, void* act, int64_t
                                          aicas_stream_t stream) {
   if (rows < 1 || inter < 8 || inter % 8 != 0) return AICAS_ERR_SHAPE;
   if (!gate_up || !act || !al16(gate_up) || !al16(act)) return AICAS_ERR_ALIGN;
-  const long work = rows * (inter / 8);
-  const unsigned grid = (unsigned)((work + 255) / 256 < 148 * 16 ? (work + 255) / 256 : 148 * 16);
+  if (rows > 65535) return AICAS_ERR_SHAPE;  // one grid row per token
+  const dim3 grid((unsigned)((inter / 8 + 255) / 256), (unsigned)rows);
   silu_mul_kernel<<<grid, 256, 0, stream>>>((const __half*)gate_up, (__half*)act, (int)rows, (int)inter);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AICAS_OK : aicas::record_cuda_error(e);

@@ -287,7 +287,7 @@ AICAS_API int aicas_prefill_qk_norm_rope_kv_f16(const void* qkv, const void* q_n
                                                 int64_t start, int64_t max_len, int64_t q_heads, int64_t kv_heads,
                                                 float eps, aicas_stream_t stream);
 /* act [rows, inter] = r16(r16(SiLU(gate)) * up) of gate_up [rows, 2 inter]
- * (gate columns first). */
+ * (gate columns first); rows <= 65535. */
 AICAS_API int aicas_prefill_silu_mul_f16(const void* gate_up, void* act, int64_t rows, int64_t inter,
                                          aicas_stream_t stream);
 /* Causal GQA attention of `rows` queries (q [rows, q_heads, 128], query t at
