@@ -669,8 +669,9 @@ def _time_graph(torch, calls, reps: int, warmup: int, dev):
 
 
 def run_op(args, rank: int, world: int):
-    """BASELINE configs 2 (decode GEMV shapes) and 3 (decode attention
-    alone): one JSON line per shape / valid length, each op called through
+    """BASELINE configs 2 (decode GEMV shapes, fused GEMV entries) and 3
+    (decode attention alone), and the q/k norm + rotary + KV write small op:
+    one JSON line per shape / valid length, each op called through
     the C ABI (the reference-facing entry points), one call per distinct
     weight or KV copy so the working set exceeds L2, as one CUDA graph."""
     if rank != 0:
@@ -704,6 +705,8 @@ def run_op(args, rank: int, world: int):
                                  "sample": f"{cpu_n} calls, {cpu_sample}"},
                 "config": {"workload": ("BASELINE config 2: decode GEMV, fp16 weights N(0,0.02), x N(0,1)"
                                         if args.op == "gemv" else
+                                        "decode small op: q/k RMSNorm + rotary + static-KV write of one token, "
+                                        "16 query / 8 KV heads, 8192-slot cache" if args.op == "small" else
                                         "BASELINE config 3: decode attention, q [1,16,128], K/V [8,L,128] "
                                         "N(0,1) in an 8192-slot cache, scale 1/sqrt(128)"),
                            "copies": OP_COPIES, "l2": "one distinct weight / KV copy per call, "
@@ -737,6 +740,86 @@ def run_op(args, rank: int, world: int):
                  {"matches_oracle": ok})
             del ws
             torch.cuda.empty_cache()
+        # the fused entry points of the drop-in (cuda_decode_gemv.fused_rmsnorm_qkv_half and
+        # fused_post_attn_mlp_softsync_half): RMSNorm + QKV, and add + RMSNorm + gate_up + SiLU*up
+        # + down + residual (two launches)
+        from oracle.qwen3vl_oracle import post_attn_mlp_reference, rms_norm
+
+        hid, inter = 2048, 6144
+        stream_of = lambda: ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)  # noqa: E731
+        x = torch.randn(hid, generator=g, device=dev).half()
+        a2 = torch.randn(hid, generator=g, device=dev).half()
+        nw = (1 + 0.1 * torch.randn(hid, generator=g, device=dev)).half()
+        wq = [(torch.randn((4096, hid), generator=g, device=dev) * 0.02).half() for _ in range(OP_COPIES)]
+        y = torch.empty(4096, dtype=torch.float16, device=dev)
+        calls = [lambda w=w: _native.check(L.aicas_rmsnorm_qkv_f16(
+            p(x), p(nw), p(w), None, p(y), 4096, hid, 1e-6, p(scratch), stream_of()), "rmsnorm_qkv") for w in wq]
+        us = _time_graph(torch, calls, reps=args.steps, warmup=args.warmup, dev=dev)
+        xn = rms_norm(x.float().cpu().numpy(), nw.float().cpu().numpy(), 1e-6)
+        w0 = wq[-1].float().cpu().numpy()
+        ok = bool(np.allclose(y.float().cpu().numpy(), gemv_reference(w0, xn), atol=2e-3, rtol=2e-3))
+        cpu_s, cpu_n = _cpu_op_baseline(lambda: gemv_reference(w0, rms_norm(x.float().cpu().numpy(),
+                                                                            nw.float().cpu().numpy(), 1e-6)),
+                                        args.cpu_seconds / 5)
+        emit("rmsnorm_qkv", [4096, hid], us, 4096 * hid * 2 + 2 * hid * 2 + 4096 * 2, cpu_s, cpu_n,
+             "numpy fp32 RMSNorm then W x (the oracle's restatement), all host threads", {"matches_oracle": ok})
+        del wq
+        torch.cuda.empty_cache()
+        wgu = [(torch.randn((2 * inter, hid), generator=g, device=dev) * 0.02).half() for _ in range(OP_COPIES)]
+        wd = [(torch.randn((hid, inter), generator=g, device=dev) * 0.02).half() for _ in range(OP_COPIES)]
+        act = torch.empty(inter, dtype=torch.float16, device=dev)
+        out = torch.empty(hid, dtype=torch.float16, device=dev)
+        calls = [lambda u=u, dw=dw: _native.check(L.aicas_post_attn_mlp_f16(
+            p(x), p(a2), p(nw), p(u), p(dw), None, p(act), p(out), hid, inter, 1e-6, p(scratch), stream_of()),
+            "post_attn_mlp") for u, dw in zip(wgu, wd)]
+        us = _time_graph(torch, calls, reps=args.steps, warmup=args.warmup, dev=dev)
+        f = lambda t: t.float().cpu().numpy()  # noqa: E731
+        args_ref = (f(x), f(a2), f(nw), f(wgu[-1]), f(wd[-1]))
+        ract, rout = post_attn_mlp_reference(*args_ref)
+        ok = bool(np.allclose(f(act), ract, atol=2e-3, rtol=2e-3)
+                  and np.abs(f(out) - rout).max() <= 4e-3 * max(1.0, float(np.abs(rout).max())))
+        cpu_s, cpu_n = _cpu_op_baseline(lambda: post_attn_mlp_reference(*args_ref), args.cpu_seconds / 5)
+        emit("post_attn_mlp", [2 * inter, hid, hid, inter], us,
+             (2 * inter * hid + hid * inter) * 2 + 4 * hid * 2 + 2 * inter * 2, cpu_s, cpu_n,
+             "numpy fp32 add + RMSNorm + gate_up + SiLU*up + down + residual (the oracle's restatement), "
+             "all host threads", {"matches_oracle": ok, "launches_per_call": 2})
+        del wgu, wd
+        torch.cuda.empty_cache()
+    elif args.op == "small":
+        # cuda_decode_small_ops.fused_q_rope_kv_cache_update: q/k RMSNorm + rotary + the static-KV write of
+        # one token (16 query heads, 8 KV heads) into a distinct 8192-slot cache per call
+        from oracle.qwen3vl_oracle import rms_norm, rope
+
+        lmax = 8192
+        q = torch.randn(16 * 128, generator=g, device=dev).half()
+        kk = torch.randn(8 * 128, generator=g, device=dev).half()
+        vv = torch.randn(8 * 128, generator=g, device=dev).half()
+        qw = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).half()
+        kw = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).half()
+        ang = torch.arange(128, dtype=torch.float32, device=dev) * 0.37
+        cos, sin = torch.cos(ang).half(), torch.sin(ang).half()
+        kcs = [torch.zeros((8, lmax, 128), dtype=torch.float16, device=dev) for _ in range(OP_COPIES)]
+        vcs = [torch.zeros((8, lmax, 128), dtype=torch.float16, device=dev) for _ in range(OP_COPIES)]
+        qo = torch.empty_like(q)
+        pos = torch.tensor([4095], dtype=torch.int64, device=dev)
+        stream_of = lambda: ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)  # noqa: E731
+        calls = [lambda kc=kc, vc=vc: _native.check(L.aicas_qk_norm_mrope_kvwrite_f16(
+            p(q), p(kk), p(vv), p(qw), p(kw), p(cos), p(sin), p(qo), p(kc), p(vc), p(pos), 1e-6, 16, 8, lmax,
+            stream_of()), "q_rope_kv") for kc, vc in zip(kcs, vcs)]
+        us = _time_graph(torch, calls, reps=args.steps, warmup=args.warmup, dev=dev)
+        f = lambda t: t.float().cpu().numpy()  # noqa: E731
+        c, s_ = f(cos).reshape(1, 128), f(sin).reshape(1, 128)
+        ref = lambda: (rope(rms_norm(f(q).reshape(1, 16, 128), f(qw), 1e-6), c, s_),  # noqa: E731
+                       rope(rms_norm(f(kk).reshape(1, 8, 128), f(kw), 1e-6), c, s_))
+        rq, rk = ref()
+        ok = bool(np.abs(f(qo).reshape(1, 16, 128) - rq).max() <= 2e-3
+                  and np.abs(f(kcs[-1][:, 4095]) - rk[0]).max() <= 2e-3
+                  and np.array_equal(f(vcs[-1][:, 4095]), f(vv).reshape(8, 128)))
+        cpu_s, cpu_n = _cpu_op_baseline(ref, args.cpu_seconds / 5)
+        # bytes: q, k, v in; q out; the k / v slot rows written; norm weights and cos / sin
+        emit("q_rope_kv_update", [16, 8, 128], us, (16 * 128 * 2 + 8 * 128 * 2) * 2 + 2 * 128 * 2 * 2, cpu_s,
+             cpu_n, "numpy fp32 q/k RMSNorm + rotary (the oracle's restatement), all host threads",
+             {"matches_oracle": ok, "bound_note": "12 KB per call: launch- and latency-bound, not HBM-bound"})
     else:
         lmax = 8192
         scale = 128 ** -0.5
@@ -871,10 +954,12 @@ def main():
                          "decode of ragged requests (contexts U[512, 4096], 512 decode steps each)")
     ap.add_argument("--layers", type=int, default=28,
                     help="profiling case only: a smaller model (the headline is 28 layers)")
-    ap.add_argument("--op", choices=["gemv", "attention", "prefill"], default=None,
+    ap.add_argument("--op", choices=["gemv", "attention", "small", "prefill"], default=None,
                     help="per-op benchmark instead of the decode step: BASELINE config 2 (the five decode GEMV "
-                         "shapes), config 3 (decode attention at valid lengths 128..8192; --steps = graph "
-                         "replays of one call per copy), or the headline prefix's one-pass prefill (TTFT)")
+                         "shapes and the fused RMSNorm+QKV / post-attention MLP entries), config 3 (decode "
+                         "attention at valid lengths 128..8192; --steps = graph replays of one call per copy), "
+                         "the q/k norm + rotary + KV write small op, or the headline prefix's one-pass prefill "
+                         "(TTFT)")
     ap.add_argument("--op-out", default="", help="also write the op benchmark's JSON lines to this file")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
