@@ -119,9 +119,12 @@ SIGNATURES = {
     "aicas_tile_weight_f16": (_I, [_P, _P, _I64, _I64, _P]),
     "aicas_prefill_add_rmsnorm_f16": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _P]),
     "aicas_prefill_qk_norm_rope_kv_f16": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I64, _I64, _I64, _I64,
-                                               _I64, _F, _P]),
+                                               _I64, _F, _P, _P]),
     "aicas_prefill_silu_mul_f16": (_I, [_P, _P, _I64, _I64, _P]),
-    "aicas_prefill_attention_f16": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
+    "aicas_prefill_attention_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
+    "aicas_prefill_attention_f16": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _P]),
+    "aicas_prefill_attention_tiles_f16": (_I, [_P, _P, _I64, _I64, _I64, _I64, _F, _P]),
+    "aicas_prefill_attention_timeouts": (_I, []),
 }
 
 _lock = threading.Lock()

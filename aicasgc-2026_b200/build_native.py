@@ -15,7 +15,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent
 SOURCES = [HERE / "csrc" / "decode_program.cu", HERE / "csrc" / "decode_batch.cu", HERE / "csrc" / "small_ops.cu",
-           HERE / "csrc" / "op_kernels.cu", HERE / "csrc" / "prefill_kernels.cu", HERE / "csrc" / "attn_op.cu"]
+           HERE / "csrc" / "op_kernels.cu", HERE / "csrc" / "prefill_kernels.cu", HERE / "csrc" / "attn_op.cu",
+           HERE / "csrc" / "prefill_attn_tc.cu"]
 HEADERS = [REPO / "include" / "aicas_decode.h", REPO / "include" / "aicas_phase_program.h",
            HERE / "csrc" / "aicas_device.cuh"]
 OUT = HERE / "libaicas_decode.so"

@@ -112,7 +112,8 @@ def prefill_native(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, *,
     aicas_prefill_add_rmsnorm_f16 (residual add of the previous layer's down
     output fused with this layer's input norm), the QKV GEMM,
     aicas_prefill_qk_norm_rope_kv_f16 (q/k norm + interleaved MRoPE, K/V into
-    the cache), aicas_prefill_attention_f16 (causal flash attention on the
+    the cache and, with q, into the attention's tile workspace),
+    aicas_prefill_attention_tiles_f16 (causal flash attention on the tcgen05
     tensor cores), the o_proj GEMM, add + post-attention norm, the gate_up
     GEMM, aicas_prefill_silu_mul_f16 and the down GEMM.  The GEMMs are plain
     fp16 x fp16 -> fp16 with fp32 accumulation (torch.matmul = cuBLAS), at
@@ -135,8 +136,11 @@ def prefill_native(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, *,
     f16 = dict(dtype=torch.float16, device=dev)
     h = embed[tokens].contiguous()
     x = torch.empty((P, hid), **f16)
-    q = torch.empty((P, qs), **f16)
     attn = torch.empty((P, qs), **f16)
+    # q, k, v of a layer in the attention's tile layout (rows padded to 128:
+    # the padding stays zero)
+    tiles = torch.zeros(int(L.aicas_prefill_attention_workspace_bytes(P, 0, num_heads, num_kv_heads)),
+                        dtype=torch.uint8, device=dev)
     act = None
     delta = None
     for li, lw in enumerate(layers):
@@ -147,11 +151,12 @@ def prefill_native(tokens, pos3, embed, final_norm, layers, k_cache, v_cache, *,
         if not (kc.is_contiguous() and vc.is_contiguous()):
             raise ValueError("prefill writes the cache in place: each layer's K/V must be contiguous")
         check(L.aicas_prefill_qk_norm_rope_kv_f16(p(qkv), p(lw["qn"]), p(lw["kn"]), p(pos3), p(inv),
-                                                  int(mrope_section[1]), int(mrope_section[2]), p(q), p(kc), p(vc),
-                                                  P, 0, max_len, num_heads, num_kv_heads, float(eps), stream),
+                                                  int(mrope_section[1]), int(mrope_section[2]), None, p(kc), p(vc),
+                                                  P, 0, max_len, num_heads, num_kv_heads, float(eps), p(tiles),
+                                                  stream),
               "aicas_prefill_qk_norm_rope_kv_f16")
-        check(L.aicas_prefill_attention_f16(p(q), p(kc), p(vc), p(attn), P, 0, num_heads, num_kv_heads, max_len,
-                                            float(head_dim ** -0.5), stream), "aicas_prefill_attention_f16")
+        check(L.aicas_prefill_attention_tiles_f16(p(tiles), p(attn), P, 0, num_heads, num_kv_heads,
+                                                  float(head_dim ** -0.5), stream), "aicas_prefill_attention_tiles_f16")
         o = attn @ lw["o"].t()
         check(L.aicas_prefill_add_rmsnorm_f16(p(h), p(o), p(lw["ln2"]), p(h), p(x), P, hid, float(eps), stream),
               "aicas_prefill_add_rmsnorm_f16")

@@ -280,23 +280,43 @@ AICAS_API int aicas_prefill_add_rmsnorm_f16(const void* h, const void* delta, co
  * (q_norm_w / k_norm_w [128]) and interleaved MRoPE from pos3 [3, rows]
  * (int64 t, h, w positions; inv_freq [64] fp32; sections sec1 / sec2 of the
  * h and w axes); q to q_out [rows, q_heads, 128], k and v to cache slots
- * start .. start + rows - 1 of k_cache / v_cache [kv_heads, max_len, 128]. */
+ * start .. start + rows - 1 of k_cache / v_cache [kv_heads, max_len, 128].
+ * `tiles` (optional, start == 0 only): also q, k and v into the workspace
+ * of aicas_prefill_attention_tiles_f16 (q_out may then be null). */
 AICAS_API int aicas_prefill_qk_norm_rope_kv_f16(const void* qkv, const void* q_norm_w, const void* k_norm_w,
                                                 const void* pos3, const void* inv_freq, int sec1, int sec2,
                                                 void* q_out, void* k_cache, void* v_cache, int64_t rows,
                                                 int64_t start, int64_t max_len, int64_t q_heads, int64_t kv_heads,
-                                                float eps, aicas_stream_t stream);
+                                                float eps, void* tiles, aicas_stream_t stream);
 /* act [rows, inter] = r16(r16(SiLU(gate)) * up) of gate_up [rows, 2 inter]
  * (gate columns first); rows <= 65535. */
 AICAS_API int aicas_prefill_silu_mul_f16(const void* gate_up, void* act, int64_t rows, int64_t inter,
                                          aicas_stream_t stream);
 /* Causal GQA attention of `rows` queries (q [rows, q_heads, 128], query t at
- * cache slot start + t) over cache slots [0, start + t]:
- * out [rows, q_heads, 128] fp16.  Flash form on the tensor cores (fp16
- * operands, fp32 scores, online softmax, fp32 accumulation). */
+ * cache slot start + t) over cache slots [0, start + t] of k_cache /
+ * v_cache [kv_heads, max_len, 128]: out [rows, q_heads, 128] fp16, query
+ * head h on KV head h / (q_heads / kv_heads); softmax(q k^T scale) v in fp32
+ * with P rounded to fp16 for its product with V.  On the tcgen05 tensor
+ * cores (csrc/prefill_attn_tc.cu): S = Q K^T and O += P V as M = N = 128
+ * MMAs with fp32 accumulators in tensor memory, one CTA per 128-query tile
+ * and head.  `workspace` (16-byte aligned, aicas_prefill_attention_workspace_bytes
+ * bytes, overwritten) first receives q and the slots in the KV tile layout
+ * (per head, row p, dim d at element (p/8)*1024 + (d/8)*64 + (p%8)*8 + d%8;
+ * rows padded to a multiple of 128): two launches on `stream`.
+ * aicas_prefill_attention_tiles_f16 is the attention alone on a workspace
+ * that aicas_prefill_qk_norm_rope_kv_f16 filled (start == 0; its padding
+ * rows zero or finite).  aicas_prefill_attention_timeouts() returns how many
+ * of the kernel's bounded waits gave up in this process (0 unless something
+ * is wrong; synchronises the device). */
+AICAS_API size_t aicas_prefill_attention_workspace_bytes(int64_t rows, int64_t start, int64_t q_heads,
+                                                         int64_t kv_heads);
 AICAS_API int aicas_prefill_attention_f16(const void* q, const void* k_cache, const void* v_cache, void* out,
                                           int64_t rows, int64_t start, int64_t q_heads, int64_t kv_heads,
-                                          int64_t max_len, float scale, aicas_stream_t stream);
+                                          int64_t max_len, float scale, void* workspace, aicas_stream_t stream);
+AICAS_API int aicas_prefill_attention_tiles_f16(const void* tiles, void* out, int64_t rows, int64_t start,
+                                                int64_t q_heads, int64_t kv_heads, float scale,
+                                                aicas_stream_t stream);
+AICAS_API int aicas_prefill_attention_timeouts(void);
 
 #ifdef __cplusplus
 }

@@ -28,32 +28,43 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def _causal_attention_ref(q, k, v, P):
-    """fp32 causal GQA attention: q [P, Hq, D], k/v [Hkv, >= P, D]."""
+def _causal_attention_ref(q, k, v, P, start=0):
+    """fp32 causal GQA attention: q [P, Hq, D] at cache slots start .., k/v
+    [Hkv, >= start + P, D]."""
     hq, hkv = q.shape[1], k.shape[0]
+    L = start + P
     qf = q.float().transpose(0, 1)                                            # [Hq, P, D]
-    kf = k[:, :P].float().repeat_interleave(hq // hkv, 0)                     # [Hq, P, D]
-    vf = v[:, :P].float().repeat_interleave(hq // hkv, 0)
+    kf = k[:, :L].float().repeat_interleave(hq // hkv, 0)                     # [Hq, L, D]
+    vf = v[:, :L].float().repeat_interleave(hq // hkv, 0)
     s = (qf @ kf.transpose(1, 2)) * q.shape[-1] ** -0.5
-    s = s.masked_fill(~torch.ones((P, P), dtype=torch.bool, device=q.device).tril(), float("-inf"))
+    qi = torch.arange(P, device=q.device).view(-1, 1) + start
+    s = s.masked_fill(torch.arange(L, device=q.device).view(1, -1) > qi, float("-inf"))
     return (torch.softmax(s, -1) @ vf).transpose(0, 1)                         # [P, Hq, D]
 
 
-@pytest.mark.parametrize("P", [1, 5, 63, 64, 65, 300, 1024])
-def test_prefill_attention_kernel(cuda_device, P):
+@pytest.mark.parametrize("P,start", [(1, 0), (5, 0), (63, 0), (64, 0), (65, 0), (127, 0), (128, 0), (129, 0),
+                                     (300, 0), (1024, 0), (100, 200), (1, 511), (257, 3)])
+def test_prefill_attention_kernel(cuda_device, P, start):
+    """The tcgen05 attention through its HF-layout entry point: queries at
+    cache slots start .. start + P - 1 over slots [0, start + t] (a
+    workspace full of NaN bit patterns: every byte the kernel reads is
+    written first)."""
     L = _native.lib()
-    g = torch.Generator(device=cuda_device).manual_seed(100 + P)
-    lmax = 1088
+    g = torch.Generator(device=cuda_device).manual_seed(100 + P + start)
+    lmax = start + P + 37
     q = torch.randn((P, 16, 128), generator=g, device=cuda_device).half()
     k = torch.randn((8, lmax, 128), generator=g, device=cuda_device).half()
     v = torch.randn((8, lmax, 128), generator=g, device=cuda_device).half()
     out = torch.full((P, 16, 128), float("nan"), dtype=torch.float16, device=cuda_device)
-    rc = L.aicas_prefill_attention_f16(_p(q), _p(k), _p(v), _p(out), P, 0, 16, 8, lmax, 128 ** -0.5,
+    ws = torch.full((L.aicas_prefill_attention_workspace_bytes(P, start, 16, 8),), 0xFF, dtype=torch.uint8,
+                    device=cuda_device)
+    rc = L.aicas_prefill_attention_f16(_p(q), _p(k), _p(v), _p(out), P, start, 16, 8, lmax, 128 ** -0.5, _p(ws),
                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _native.check(rc, "aicas_prefill_attention_f16")
-    ref = _causal_attention_ref(q, k, v, P)
+    ref = _causal_attention_ref(q, k, v, P, start)
     err = (out.float() - ref).abs().max().item()
     assert err <= 4e-3, err
+    assert L.aicas_prefill_attention_timeouts() == 0
 
 
 def test_prefill_native_matches_oracle_prefill(cuda_device):
