@@ -69,6 +69,7 @@
 // :850-1076, decode_gemv_kernel_matvec.cuh:209-343,
 // decode_attention_v4_kernel.cu:647-900, decode_small_ops_kernel.cu:115-186,
 // evaluation_wrapper.py:952 (argmax, first max wins).
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -1540,14 +1541,16 @@ __global__ void tile_weight_kernel(const uint4* __restrict__ w, uint4* __restric
 // Host side
 // ---------------------------------------------------------------------------
 static constexpr int kMaxDevices = 64;
-static int g_setup_done[kMaxDevices];
-static int g_ctas[kMaxDevices];
+// per-device setup, done once (idempotent; the flag is published after the
+// values it guards)
+static std::atomic<int> g_setup_done[kMaxDevices];
+static std::atomic<int> g_ctas[kMaxDevices];
 
 static int setup(int* dev_out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
-  if (!g_setup_done[dev]) {
+  if (!g_setup_done[dev].load(std::memory_order_acquire)) {
     for (int v = 0; v < 2; ++v) {
       const void* fn = v ? reinterpret_cast<const void*>(decode_batch_kernel<true>)
                          : reinterpret_cast<const void*>(decode_batch_kernel<false>);
@@ -1560,8 +1563,8 @@ static int setup(int* dev_out) {
     }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
-    g_ctas[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
-    g_setup_done[dev] = 1;
+    g_ctas[dev].store(sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS, std::memory_order_relaxed);
+    g_setup_done[dev].store(1, std::memory_order_release);
   }
   *dev_out = dev;
   return AICAS_OK;
@@ -1656,7 +1659,7 @@ static int launch_batch(const AicasPhase* device_phases, int n_phases, AicasStep
   a.scratch = reinterpret_cast<AicasBatchScratch*>(scratch);
   a.trace = trace;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(bat::g_ctas[dev]);
+  cfg.gridDim = dim3(bat::g_ctas[dev].load(std::memory_order_relaxed));
   cfg.blockDim = dim3(bat::kThreads);
   cfg.dynamicSmemBytes = sizeof(bat::Smem);
   cfg.stream = stream;

@@ -51,6 +51,7 @@
 //   q/k norm+rope+KV write cuda_extensions/decode_small_ops_kernel.cu:115-186
 //   lm_head GEMV           cuda_extensions/decode_gemv_kernel_matvec.cuh:209-274
 //   argmax                 evaluation_wrapper.py:952 (torch.argmax, first max wins)
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -1746,15 +1747,17 @@ static int cuda_fail(cudaError_t e) {
 // Shared with the batched kernel's translation unit (hidden symbol).
 int record_cuda_error(cudaError_t e) { return cuda_fail(e); }
 
-static int g_attr_done[kMaxDevices];
-static int g_num_sms[kMaxDevices];
-static int g_cooperative = 1;
+// per-device setup, done once (idempotent: threads racing on a first call
+// both do it; the flag is published after the values it guards)
+static std::atomic<int> g_attr_done[kMaxDevices];
+static std::atomic<int> g_num_sms[kMaxDevices];
+static std::atomic<int> g_cooperative{1};  // aicas_set_cooperative_launch
 
 static int device_setup(int* dev_out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return AICAS_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return AICAS_ERR_CUDA;
-  if (!g_attr_done[dev]) {
+  if (!g_attr_done[dev].load(std::memory_order_acquire)) {
     const void* fns[4] = {reinterpret_cast<const void*>(decode_program_kernel<false, false>),
                           reinterpret_cast<const void*>(decode_program_kernel<true, false>),
                           reinterpret_cast<const void*>(decode_program_kernel<false, true>),
@@ -1769,8 +1772,8 @@ static int device_setup(int* dev_out) {
     }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AICAS_ERR_CUDA;
-    g_num_sms[dev] = sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS;
-    g_attr_done[dev] = 1;
+    g_num_sms[dev].store(sms < AICAS_MAX_CTAS ? sms : AICAS_MAX_CTAS, std::memory_order_relaxed);
+    g_attr_done[dev].store(1, std::memory_order_release);
   }
   *dev_out = dev;
   return AICAS_OK;
@@ -1831,13 +1834,13 @@ static int launch_program(ProgramArgs& a, cudaStream_t stream, bool lean = false
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g_num_sms[dev]);
+  cfg.gridDim = dim3(g_num_sms[dev].load(std::memory_order_relaxed));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(Smem);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = g_cooperative;
+  attr[0].val.cooperative = g_cooperative.load(std::memory_order_relaxed);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e;
@@ -1880,11 +1883,11 @@ AICAS_API int aicas_num_ctas(int device) {
   int dev = 0;
   const int rc = device_setup(&dev);
   if (device != prev) cudaSetDevice(prev);
-  return rc ? -rc : g_num_sms[dev];
+  return rc ? -rc : g_num_sms[dev].load(std::memory_order_relaxed);
 }
 
 AICAS_API int aicas_set_cooperative_launch(int enable) {
-  g_cooperative = enable ? 1 : 0;
+  g_cooperative.store(enable ? 1 : 0, std::memory_order_relaxed);
   return AICAS_OK;
 }
 

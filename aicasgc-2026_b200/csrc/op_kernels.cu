@@ -23,6 +23,7 @@
 //   fused_rmsnorm_qkv_half     cuda_decode_gemv_ops/fused.py:71-105
 //   fused_post_attn_mlp_softsync_half   cuda_decode_gemv_ops/fused.py:261-337
 //   FastLmHead + torch.argmax  evaluation_wrapper.py:1227-1240, :952
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -313,15 +314,15 @@ __global__ void __launch_bounds__(kThreads) gemv_ksplit_kernel(const Args a) {
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 static int sm_count() {
-  static int cached[64];
+  static std::atomic<int> cached[64];  // 0: not read yet (a racing first read stores the same value)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
-    cached[dev] = sms;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (!v) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v < 1) v = 148;
+    cached[dev].store(v, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return v;
 }
 
 template <int C, int M>

@@ -34,6 +34,7 @@
 // reference runs through HF's eager attention (optimized_layer.py:471-619,
 // prefill_forward_no_mask; modeling_qwen3_vl.py eager_attention_forward):
 // softmax(Q K^T * scale + causal mask) V per query head, KV head = head / 2.
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -387,15 +388,15 @@ AICAS_API size_t aicas_prefill_attention_workspace_bytes(int64_t rows, int64_t s
 
 static int attn_launch(const uint8_t* tiles, void* out, int64_t rows, int64_t start, int64_t q_heads,
                        int64_t kv_heads, float scale, aicas_stream_t stream) {
-  static bool attr_done[64] = {};
+  static std::atomic<bool> attr_done[64];  // per device, set once (idempotent)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return aicas::record_cuda_error(e);
   if (dev < 0 || dev >= 64) return AICAS_ERR_CUDA;
-  if (!attr_done[dev]) {
+  if (!attr_done[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return aicas::record_cuda_error(e);
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   const int64_t r128 = round128(rows), l128 = round128(start + rows);
   const dim3 grid((unsigned)(r128 / kBM), (unsigned)q_heads);
