@@ -904,6 +904,130 @@ def run_prefill_op(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_ops_path(args, rank: int, world: int):
+    """The headline request decoded through the drop-in
+    ops instead of the persistent step kernel: per layer the five calls the
+    reference's OptimizedDecoderLayer decode branch makes (fused RMSNorm +
+    QKV, q/k norm + rotary + KV write, split-KV attention, o_proj GEMV, the
+    post-attention MLP), then the fused lm_head + argmax, the next token's
+    embedding row and the rotary cos/sin computed on the device: one CUDA
+    graph per decode step (about 6 launches per layer), 256 steps per bench
+    step.  This is what a caller of the reference's per-op interface gets
+    from these kernels; the headline path runs the same math as one launch
+    per token.  Tokens are compared with the step kernel's for the same
+    request.  One GPU, rank 0."""
+    if rank != 0:
+        return
+    import torch
+
+    import _ops
+    from engine import Qwen3VLDecodeEngine, hf_inv_freq
+    from qwen3vl_config import QWEN3VL_2B, synthetic_state
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = QWEN3VL_2B.with_layers(args.layers)
+    st = synthetic_state(shape, seed=0, dtype=torch.float16, threads=host_threads(world))
+    eng = Qwen3VLDecodeEngine(st, shape, max_cache_len=PREFIX + NEW, device=dev, max_steps=PREFIX + NEW + 8,
+                              logits_ring=PREFIX + NEW)
+    prompt, pos3, _ = headline_request(rank)
+    first = eng.prefill_prompt(prompt, pos3)
+    start_state = eng.snapshot()
+    eng.run(NEW, 32)
+    torch.cuda.synchronize(dev)
+    eng.check_error()
+    ref_toks = eng.out_tokens[PREFIX:PREFIX + NEW].cpu()
+
+    s = shape
+    eps, scale = float(s.rms_eps), s.head_dim ** -0.5
+    qs, ks = s.num_heads * s.head_dim, s.num_kv_heads * s.head_dim
+    f16 = dict(dtype=torch.float16, device=dev)
+    i64 = dict(dtype=torch.int64, device=dev)
+    inv = hf_inv_freq(s).to(device=dev, dtype=torch.float32)
+    half = s.head_dim // 2
+    axis = torch.zeros(half, **i64)  # interleaved MRoPE: frequency i takes axis 1 / 2 / 0
+    for i in range(half):
+        if i % 3 == 1 and i < 3 * s.mrope_section[1]:
+            axis[i] = 1
+        elif i % 3 == 2 and i < 3 * s.mrope_section[2]:
+            axis[i] = 2
+    rope0 = torch.tensor([int(x) + 1 for x in pos3[:, -1]], **i64)
+    tok, pos, rope = torch.tensor([first], **i64), torch.tensor([PREFIX], **i64), rope0.clone()
+    out_tok = torch.zeros(NEW, **i64)
+    qkv, q_rot, attn, o = (torch.empty(n, **f16) for n in (qs + 2 * ks, qs, qs, s.hidden))
+    act = torch.empty(s.intermediate, **f16)
+    hb = [torch.empty(s.hidden, **f16) for _ in range(2)]
+
+    def step():
+        h = torch.index_select(eng.embed, 0, tok).view(-1)
+        ang = inv * torch.index_select(rope, 0, axis).to(torch.float32)
+        emb = torch.cat([ang, ang])
+        cos, sin = emb.cos().to(torch.float16), emb.sin().to(torch.float16)
+        for li, lw in enumerate(eng.layers):
+            _ops.gemv(h, lw["qkv"], norm_w=lw["ln1"], eps=eps, out=qkv)
+            kc, vc = eng.k_cache[li][0], eng.v_cache[li][0]
+            _ops.qk_norm_rope_kvwrite(qkv[:qs], qkv[qs:qs + ks], qkv[qs + ks:], lw["qn"], lw["kn"], cos, sin, kc, vc,
+                                      pos, eps, q_out=q_rot)
+            _ops.decode_attention(q_rot, kc, vc, pos, scale, out=attn)
+            _ops.gemv(attn, lw["o"], out=o)
+            hn = hb[li % 2]
+            _ops.post_attn_mlp(h, o, lw["ln2"], lw["gate_up"], lw["down_rm"], eps=eps, act_out=act, out=hn)
+            h = hn
+        _ops.lm_head_argmax(h, eng.embed, norm_w=eng.final_norm, eps=eps, token_out=tok, want_logits=False)
+        out_tok.index_copy_(0, pos - PREFIX, tok)
+        pos.add_(1)
+        rope.add_(1)
+
+    def reset():
+        eng.restore(start_state)
+        tok.fill_(first)
+        pos.fill_(PREFIX)
+        rope.copy_(rope0)
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        reset()
+        step()  # eager warm-up outside capture
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        reset()
+        for _ in range(NEW):
+            g.replay()
+        stream.synchronize()
+        eng.check_error()
+        toks = out_tok.cpu()
+        same = int((toks == ref_toks).cumprod(0).sum())  # steps equal to the step kernel's, up to the first difference
+        gap = None
+        if same < NEW:  # the step kernel's top-2 logit gap where the two paths first differ
+            top = eng.step_logits(PREFIX + same).float().topk(2).values
+            gap = float(top[0] - top[1])
+        for _ in range(args.warmup):
+            reset()
+            for _ in range(NEW):
+                g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        ms = 0.0
+        for _ in range(args.steps):
+            reset()
+            e0.record(stream)
+            for _ in range(NEW):
+                g.replay()
+            e1.record(stream)
+            stream.synchronize()
+            ms += e0.elapsed_time(e1)
+    us_tok = 1000.0 * ms / (args.steps * NEW)
+    line = {"metric": METRIC, "path": "drop-in ops: the five per-layer op calls of the reference's decoder layer + "
+                                      "lm_head/argmax, one CUDA graph per token",
+            "value": 1e6 / us_tok, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "us_per_token": us_tok, "higher_is_better": True, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "config": workload_config(1), "tokens_equal_to_step_kernel": f"{same} of {NEW}",
+            "top2_gap_at_first_difference": gap}
+    print(json.dumps(line), flush=True)
+
+
 def write_trace_summary(eng, start_state, path):
     """One traced decode step at cache slot 1024.  Per phase kind (summed
     over layers, averaged over CTAs): time waiting for inputs, time from
@@ -961,6 +1085,9 @@ def main():
                          "the q/k norm + rotary + KV write small op, or the headline prefix's one-pass prefill "
                          "(TTFT)")
     ap.add_argument("--op-out", default="", help="also write the op benchmark's JSON lines to this file")
+    ap.add_argument("--path", choices=["step", "ops"], default="step",
+                    help="ops: decode the headline request through the drop-in per-op entry points (one CUDA graph "
+                         "per token) instead of the persistent step kernel; one GPU")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -968,6 +1095,8 @@ def main():
         run_prefill_op(args, rank, world)
     elif args.op:
         run_op(args, rank, world)
+    elif args.path == "ops":
+        run_ops_path(args, rank, world)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     elif args.batch > 1:
