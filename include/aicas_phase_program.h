@@ -9,8 +9,9 @@
 // their inputs: a phase that reads the vector of an earlier phase polls its
 // flag-in-data words (AICAS_F_LL_IN, below) or, in the batched kernel, a
 // per-phase completion counter (AICAS_F_CNT_IN); only a phase marked
-// AICAS_F_BARRIER waits at a bounded software grid barrier first (the
-// op-level post-attention MLP uses one).  One warp per CTA streams the
+// AICAS_F_BARRIER waits at a bounded software grid barrier first (for
+// programs whose vectors are plain fp16; the engines' programs use none).
+// One warp per CTA streams the
 // phase's tiles from HBM into a shared-memory ring with bulk async copies,
 // independently of the activations, so weight streaming never waits on
 // another CTA.
