@@ -151,3 +151,59 @@ def test_block_pair_mma_reproduces_the_projection():
     np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-9)
     # the off-diagonal blocks are the products the epilogue discards
     assert np.abs(d[0:8, 8:16]).max() > 0
+
+
+def _operand_mn(buf: np.ndarray, base: int, cols: int, lbo: int, sbo: int) -> np.ndarray:
+    """The [16 x cols] fp16 matrix (K = 16 rows, MN = cols) an MN-major
+    no-swizzle descriptor hands the tensor core for one K step: core matrices
+    of 8 K-rows x 8 MN-elements (16 bytes per K-row), 8-deep K groups `lbo`
+    bytes apart, 8-wide MN blocks `sbo` bytes apart: element (k, n) at
+    base + (k / 8) lbo + (n / 8) sbo + (k % 8) 16 + (n % 8) 2."""
+    k = np.arange(16)[:, None]
+    n = np.arange(cols)[None, :]
+    addr = base + (k // 8) * lbo + (n // 8) * sbo + (k % 8) * 16 + (n % 8) * 2
+    return buf[addr // 2]
+
+
+def test_attention_mma_operands_over_the_kv_tile_layout():
+    """Emulates the tensor-core attention of decode_batch.cu (and, with 128-row
+    blocks, of prefill_attn_tc.cu) on a K / V tile stored in the KV tile
+    layout: S = K Q^T with both operands K-major (LBO 128 B, SBO 2 KB, 256 bytes
+    per 16-dim K step) and O = V^T P^T with V read MN-major (LBO 2 KB along the
+    slots, SBO 128 B along the dims, 4096 bytes per 16-slot K step) and P
+    K-major (LBO 128 B, SBO 1 KB for 64 slots).  The same conventions were
+    checked exact on a B200 by a probe."""
+    g = torch.Generator().manual_seed(11)
+    L, D = 64, 128
+    k = torch.randn(L, D, generator=g).half()
+    v = torch.randn(L, D, generator=g).half()
+    q = torch.randn(2, D, generator=g).half()       # the KV head's two query heads
+    p = torch.rand(2, L, generator=g).half()        # probabilities
+    cache = torch.zeros((1, 1, 1, L, D), dtype=torch.float16)
+    kv_store_tiles(cache, 0, k.view(1, 1, L, D))
+    ktile = cache.reshape(-1).numpy().copy()
+    kv_store_tiles(cache, 0, v.view(1, 1, L, D))
+    vtile = cache.reshape(-1).numpy().copy()
+    # queries: B operand [16 rows x 128 dims], rows 2.. zero; layout (n/8) 2048 + (d/8) 128 + (n%8) 16 + (d%8) 2
+    qop = np.zeros(16 * D, dtype=np.float16)
+    for n in range(2):
+        for d in range(D):
+            qop[((n // 8) * 2048 + (d // 8) * 128 + (n % 8) * 16 + (d % 8) * 2) // 2] = q[n, d].item()
+    s = np.zeros((L, 16))
+    for ks in range(D // 16):
+        a = _operand(ktile, 256 * ks, L, 128, 2048).astype(np.float64)
+        b = _operand(qop, 256 * ks, 16, 128, 2048).astype(np.float64)
+        s += a @ b.T
+    np.testing.assert_allclose(s[:, :2], k.double().numpy() @ q.double().numpy().T, rtol=1e-9, atol=1e-9)
+    assert not s[:, 2:].any()
+    # probabilities: B operand [16 rows x 64 slots], K-major, row g at (g/8) 1024 + (r/8) 128 + (g%8) 16 + (r%8) 2
+    pop = np.zeros(16 * L, dtype=np.float16)
+    for n in range(2):
+        for r in range(L):
+            pop[((n // 8) * 1024 + (r // 8) * 128 + (n % 8) * 16 + (r % 8) * 2) // 2] = p[n, r].item()
+    o = np.zeros((D, 16))
+    for ks in range(L // 16):
+        a = _operand_mn(vtile, 4096 * ks, D, 2048, 128).astype(np.float64).T  # A = V^T: [128 dims x 16 slots]
+        b = _operand(pop, 256 * ks, 16, 128, 1024).astype(np.float64)          # B = P: [16 rows x 16 slots]
+        o += a @ b.T
+    np.testing.assert_allclose(o[:, :2], v.double().numpy().T @ p.double().numpy().T, rtol=1e-9, atol=1e-9)

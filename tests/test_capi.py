@@ -88,3 +88,15 @@ def test_lean_program_rule():
     assert ok(ph(_native.PH_GATEUP, 64, 6144)) == 2
     assert ok(ph(_native.PH_LMHEAD, 64, 6144)) == 2               # the LM head: one chunk only
     assert ok(ph(_native.PH_GEMV, 64, 2048), nct=0) == 1
+
+
+def test_prefill_attention_workspace_bytes():
+    """The prefill attention's workspace: q rows and cache slots [0, start +
+    rows) of every head in 128-row tiles, fp16; 0 for an invalid shape."""
+    L = _native.lib()
+    r128 = lambda x: (x + 127) // 128 * 128  # noqa: E731
+    for rows, start, hq, hkv in [(1, 0, 16, 8), (1024, 0, 16, 8), (300, 0, 16, 8), (100, 200, 16, 8), (5, 3, 2, 1)]:
+        want = (hq * r128(rows) + 2 * hkv * r128(start + rows)) * 128 * 2
+        assert L.aicas_prefill_attention_workspace_bytes(rows, start, hq, hkv) == want
+    assert L.aicas_prefill_attention_workspace_bytes(0, 0, 16, 8) == 0
+    assert L.aicas_prefill_attention_workspace_bytes(4, -1, 16, 8) == 0
